@@ -1,0 +1,258 @@
+/* llmq_cuda.h - C ABI of libllmq_cuda.so, the B200 (sm_100a) implementation of the
+ * int8 (W8A8) LLaMA-family KV-cache decode path of marjoncajocon/llm-project.
+ *
+ * The library is a link-time drop-in for the int8 half of the reference:
+ *   quant.c in full (quant.h:15-33) and the QLlamaModel section of llama.c
+ *   (llama.c:443-657, declared at llama.h:114-140) plus llama_kv_free (llama.h:102).
+ * Every exported name, argument order, struct layout, ownership rule and return
+ * convention below is the reference's, so a caller written against quant.h /
+ * llama.h compiles and links unchanged.  All arithmetic runs on the GPU: the
+ * results are bit-identical to the reference CPU code (same int8 codes, same
+ * int32 accumulators, same fp32 rounding sequence), see DESIGN.md.
+ *
+ * Additions (new names, same C style) carry a comment saying so.  No entry point
+ * takes or returns a torch or CUDA type.  Compute functions that return void in the
+ * reference keep returning void; their failures are reported by
+ * q_llama_last_error() and a one-line message on stderr.
+ */
+#ifndef LLMQ_CUDA_H
+#define LLMQ_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------------- */
+/* Host structs.  The guards are the reference headers' own include guards, so */
+/* this header and tensor.h / quant.h / llama.h may be included in any order.  */
+/* ------------------------------------------------------------------------- */
+#ifndef TENSOR_H
+#define TENSOR_H
+/* Same layout as the reference Tensor (tensor.h:10-16): row-major f32 data,
+ * optional grad, malloc'd shape array.  Tensors this library allocates use a
+ * 64-byte aligned `data` block and a malloc'd `shape`, like tensor.c:33-60, so
+ * the reference tensor_free can release them. */
+typedef struct {
+  float *data;
+  float *grad;
+  int *shape;
+  int ndim;
+  size_t size;
+} Tensor;
+#endif
+
+#ifndef QUANT_H
+#define QUANT_H
+/* int8 weight, (rows=in, cols=out) row-major, one f32 scale per column
+ * (quant.h:22-26).  x(M,rows) @ W -> (M,cols). */
+typedef struct {
+  int rows, cols;
+  signed char *q;
+  float *scale;
+} QTensor;
+#endif
+
+#ifndef LLAMA_H
+#define LLAMA_H
+/* fp32 block / model (llama.h:19-36, 59-66).  Only read here, by
+ * q_llama_quantize_from. */
+typedef struct {
+  int d_model, n_heads, n_kv, head_dim, d_ff;
+  float rope_base, eps;
+  Tensor attn_norm, Wq, Wk, Wv, b_q, b_k, b_v, Wo;
+  Tensor ffn_norm, Wgate, Wup, Wdown;
+} LlamaBlock;
+
+typedef struct {
+  int vocab, d_model, n_layers, n_heads, n_kv, head_dim, d_ff, max_seq;
+  float rope_base, eps;
+  Tensor wte;
+  LlamaBlock *blocks;
+  Tensor final_norm;
+  Tensor lm_head;
+} LlamaModel;
+
+/* KV cache handle (llama.h:94-99).  `len` is the number of cached positions and
+ * is the source of truth on every call: callers restart a sequence by writing
+ * kv.len = 0 (main.c:661).  The cache itself lives on the GPU; the host arrays
+ * k/v are allocated with the reference's shapes and are filled only by
+ * q_llama_kv_sync_host(). */
+typedef struct {
+  int n_layers, max_seq, kv_dim;
+  int len;
+  float **k;
+  float **v;
+} LlamaKV;
+
+/* int8 block / model (llama.h:114-127). */
+typedef struct {
+  Tensor attn_norm, ffn_norm;
+  Tensor b_q, b_k, b_v;
+  QTensor Wq, Wk, Wv, Wo, Wgate, Wup, Wdown;
+} QLlamaBlock;
+
+typedef struct {
+  int vocab, d_model, n_layers, n_heads, n_kv, head_dim, d_ff, max_seq;
+  float rope_base, eps;
+  QTensor wte;
+  QLlamaBlock *blocks;
+  Tensor final_norm;
+  QTensor lm_head;
+} QLlamaModel;
+#endif
+
+/* ========================================================================= */
+/* quant.h entry points                                                       */
+/* ========================================================================= */
+
+/* Replaces quant.c:45-62 (declared quant.h:15).  Per-column symmetric int8
+ * quantisation of a row-major (rows, cols) f32 matrix, computed on the GPU:
+ * scale[j] = max_i|w[i,j]|/127 (1 for an all-zero column),
+ * q = clamp(lrintf(w * (1/scale[j])), -127, 127).  Bit-identical to the
+ * reference.  Host pointers in and out. */
+void quantize_int8_percol(const float *w, int rows, int cols, signed char *q, float *scale);
+
+/* Replaces quant.c:64-68 (quant.h:16).  w[i,j] = q[i,j] * scale[j], on the GPU. */
+void dequantize_int8_percol(const signed char *q, const float *scale, int rows, int cols, float *w);
+
+/* Replace quant.c:70-85 (quant.h:28-30).  Host allocation, as in the reference.
+ * qtensor_free also drops any device copy of the weight made by qmatmul. */
+QTensor qtensor_create(int rows, int cols);
+void qtensor_free(QTensor *t);
+void qtensor_quantize(QTensor *t, const float *w);
+
+/* Replaces quant.c:95-120 (quant.h:33).  C(M,N) = W8A8 product of A(M,K) with W:
+ * each row of A is quantised to int8 with its own absmax scale, multiplied
+ * exactly in int32 against W's codes, and rescaled as a_scale*w_scale[j]*acc.
+ * A and C are host tensors.  W is copied to the GPU (and repacked) on first use
+ * and cached, keyed by W->q; qtensor_free releases the copy. */
+void qmatmul(const Tensor *A, const QTensor *W, Tensor *C);
+
+/* ========================================================================= */
+/* llama.h entry points (int8 model)                                          */
+/* ========================================================================= */
+
+/* Replaces llama.c:610-657 (llama.h:136).  Reads an LLMQ v2 checkpoint into
+ * host memory exactly like the reference (0 on success, 1 with a message on
+ * stderr on any error; the model is freed on failure) and uploads it to the
+ * current GPU. */
+int q_llama_model_load(const char *path, QLlamaModel *out);
+
+/* Replaces llama.c:483-488 (llama.h:129).  Frees host arrays and the device copy
+ * (weights, every KV cache and CUDA graph made for this model). */
+void q_llama_model_free(QLlamaModel *m);
+
+/* Replaces llama.c:490-511 (llama.h:132).  Quantises an fp32 model on the GPU
+ * (bit-identical codes and scales). */
+QLlamaModel q_llama_quantize_from(const LlamaModel *src);
+
+/* Replaces llama.c:513-526 (llama.h:140).  Creates the GPU KV cache
+ * (f32 [n_layers][max_seq][kv_dim], K and V) plus the reference-shaped host
+ * arrays. */
+LlamaKV q_llama_kv_create(const QLlamaModel *m);
+
+/* Replaces llama.c:290-294 (llama.h:102) for caches made by q_llama_kv_create. */
+void llama_kv_free(LlamaKV *kv);
+
+/* Replaces llama.c:528-600 (llama.h:139).  Decodes `token` at position kv->len:
+ * appends its K/V to the GPU cache, attends over 0..kv->len, writes the f32
+ * logits (1, vocab) into the caller's host tensor and advances kv->len.  One
+ * CUDA graph replay per call. */
+void q_llama_decode_step(const QLlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
+
+/* ========================================================================= */
+/* Additions (no counterpart in the reference headers)                        */
+/* ========================================================================= */
+
+enum {
+  LLMQ_OK = 0,
+  LLMQ_ERR_ARG = 1,      /* bad shape / id / position / null pointer */
+  LLMQ_ERR_CUDA = 2,     /* a CUDA runtime call failed */
+  LLMQ_ERR_NO_DEVICE = 3,/* no CUDA device, or not an sm_100 part */
+  LLMQ_ERR_IO = 4,       /* checkpoint read / write failure */
+  LLMQ_ERR_OOM = 5,      /* host or device allocation failed */
+  LLMQ_ERR_STATE = 6     /* model / cache not known to this library */
+};
+
+/* Error code of the most recent failing call on this thread (LLMQ_OK if none)
+ * and its message.  q_llama_clear_error resets both. */
+int q_llama_last_error(void);
+const char *q_llama_last_error_message(void);
+void q_llama_clear_error(void);
+
+/* As q_llama_decode_step, but also returns the greedy next token (first index
+ * of the largest logit, the rule of sampler.c:8-21) computed on the GPU.
+ * `logits` may be NULL, in which case no logits are copied to the host (4 bytes
+ * cross PCIe per token).  Returns -1 on error. */
+int q_llama_decode_step_argmax(const QLlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
+
+/* Copies the GPU KV cache rows [0, kv->len) into kv->k / kv->v (the
+ * reference-shaped host arrays).  Returns LLMQ_OK or an error code. */
+int q_llama_kv_sync_host(const QLlamaModel *m, LlamaKV *kv);
+
+/* Writes an LLMQ v2 checkpoint (the layout q_llama_model_load reads,
+ * llama.c:192-220 and llama.c:603-648): atomically, through `path`.tmp and a
+ * rename.  Returns 0 on success, 1 with a message on stderr on error. */
+int q_llama_model_save(const char *path, const QLlamaModel *m);
+
+/* Model configuration, in LLMQ header order (llama.c:241-243). */
+typedef struct {
+  int vocab, d_model, n_layers, n_heads, n_kv, head_dim, d_ff, max_seq;
+  float rope_base, eps;
+} LlmqConfig;
+
+/* Builds a seeded synthetic int8 model in host memory (not uploaded; the first
+ * q_llama_kv_create / decode call uploads it).  Every 2-D weight is drawn
+ * f32 N(0, stddev) from splitmix64 + Box-Muller keyed by (seed, tensor index,
+ * element index), then quantised per column by the reference rule.  Norm gains
+ * are 1; biases are 0, or N(0, stddev) when `with_bias` (the Qwen2 path).
+ * Multi-threaded; the result does not depend on the thread count.
+ * Returns 0 or an error code. */
+int llmq_synth_model(const LlmqConfig *cfg, uint64_t seed, float stddev, int with_bias,
+                     QLlamaModel *out);
+
+/* Fills an existing QTensor with uniform codes in [-127, 127] and uniform scales
+ * in [1e-3, 1e-2), seeded (the isolated matvec sweep's weights). */
+void llmq_synth_qtensor(QTensor *t, uint64_t seed);
+
+/* Upload / release the device copy of a model explicitly (both are otherwise
+ * implicit).  Returns 0 or an error code. */
+int q_llama_model_upload(const QLlamaModel *m);
+
+/* Greedy generation chained on the GPU: feeds `token` at position kv->len, then
+ * keeps feeding the argmax of each step, for n steps in total (one CUDA graph
+ * replay per step, no host round trip in between).  ids[i] receives the argmax
+ * after step i; kv->len advances by n.  Returns 0 or an error code. */
+int q_llama_generate(const QLlamaModel *m, LlamaKV *kv, int token, int n, int *ids);
+
+/* GPU time in milliseconds of the last q_llama_decode_step[_argmax] (one step,
+ * including its small host<->device copies) or q_llama_generate (all n steps),
+ * from CUDA events on the model's stream. */
+float q_llama_last_step_ms(void);
+
+/* ---- diagnostics for tests and benchmarks ---- */
+
+/* y[i] = expf(x[i]) evaluated on the GPU by the routine the decode kernels use
+ * (bit-identical to the host C library's expf).  Returns 0 or an error code. */
+int llmq_expf_device(const float *x, float *y, long long n);
+
+/* Times `iters` back-to-back launches of one GEMV of an uploaded model
+ * (which: 0 fused QKV, 1 Wo, 2 fused W1|W3, 3 W2, 4 lm-head; `layer` selects
+ * the block) with CUDA events on the model's stream.  *ms_per_launch receives
+ * the mean launch time and *bytes_per_launch the algorithmic bytes of one
+ * launch (int8 weights + f32 scales + f32 input + f32 output).
+ * Returns 0 or an error code. */
+int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int iters, float *ms_per_launch,
+                    double *bytes_per_launch);
+
+/* Kernels launched by one decode step (5 per layer + 2). */
+int llmq_kernels_per_step(const QLlamaModel *m);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LLMQ_CUDA_H */

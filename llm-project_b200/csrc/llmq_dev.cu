@@ -1,0 +1,1044 @@
+// llmq_dev.cu - CUDA runtime layer of libllmq_cuda.so: device contexts, weight
+// upload and tiling, the per-(model, cache) decode graphs, and the launchers of
+// the kernels in llmq_kernels.cuh.  Called only through llmq_internal.h.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "llmq_internal.h"
+#include "llmq_kernels.cuh"
+
+using namespace llmq;
+
+extern "C" const uint32_t llmq_expf_exceptions[];
+extern "C" const uint32_t llmq_expf_exceptions_count;
+
+#define CK(call)                                                                                       \
+  do {                                                                                                 \
+    cudaError_t e_ = (call);                                                                           \
+    if (e_ != cudaSuccess) {                                                                           \
+      llmq_set_error(LLMQ_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+      return 0;                                                                                        \
+    }                                                                                                  \
+  } while (0)
+
+namespace {
+
+constexpr int kKT = 64;         // k rows per tile
+constexpr int kMaxDevices = 64;
+
+size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+int roundup(int v, int m) { return (v + m - 1) / m * m; }
+
+// ------------------------------------------------------------------ context
+struct Mat {
+  uint8_t *w = nullptr;
+  float *ws = nullptr;
+  int K = 0, Kpad = 0, N = 0, Npad = 0, NT = 0, KT = kKT, n_slabs = 0, n_ktiles = 0;
+  size_t bytes() const { return (size_t)Kpad * Npad; }
+};
+
+struct WeightEntry {
+  Mat mat;
+  int rows, cols;
+  const float *scale;
+};
+
+struct DevCtx {
+  bool ready = false;
+  int device = -1;
+  int num_sms = 0;
+  int max_smem = 0;  // dynamic shared memory available to one CTA
+  cudaStream_t stream = nullptr;
+  uint32_t *expf_keys = nullptr;
+  // qmatmul scratch (grow-only; acc/cnt kept zero between launches)
+  float *dA = nullptr, *dC = nullptr;
+  size_t dA_n = 0, dC_n = 0;
+  int *acc = nullptr, *cnt = nullptr, *err = nullptr;
+  size_t acc_n = 0, cnt_n = 0;
+  std::unordered_map<const void *, WeightEntry> weights;
+};
+
+DevCtx g_ctx[kMaxDevices];
+std::recursive_mutex g_mu;
+
+void free_mat(Mat &m) {
+  cudaFree(m.w);
+  cudaFree(m.ws);
+  m = Mat{};
+}
+
+template <int PRO, int EPI, int MR>
+cudaError_t set_gemv_attr(int smem) {
+  return cudaFuncSetAttribute(k_gemv<PRO, EPI, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+}
+
+int init_expf_table(DevCtx &c) {
+  const uint32_t n = llmq_expf_exceptions_count;
+  uint32_t cap = 1;
+  while (cap < 3 * n + 1) cap <<= 1;
+  std::vector<uint32_t> table(cap, 0u);
+  for (uint32_t i = 0; i < n; ++i) {
+    const uint32_t key = llmq_expf_exceptions[i];
+    uint32_t h = expf_hash(key) & (cap - 1);
+    while (table[h] != 0u) h = (h + 1) & (cap - 1);
+    table[h] = key;
+  }
+  CK(cudaMalloc(&c.expf_keys, cap * sizeof(uint32_t)));
+  CK(cudaMemcpy(c.expf_keys, table.data(), cap * sizeof(uint32_t), cudaMemcpyHostToDevice));
+  ExpfTable t{c.expf_keys, cap - 1};
+  CK(cudaMemcpyToSymbol(g_expf_table, &t, sizeof(t)));
+  return 1;
+}
+
+DevCtx *get_ctx() {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    llmq_set_error(LLMQ_ERR_NO_DEVICE, "libllmq_cuda: no CUDA device available (%s)", cudaGetErrorString(e));
+    return nullptr;
+  }
+  DevCtx &c = g_ctx[dev];
+  if (c.ready) return &c;
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, dev);
+  if (e != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_NO_DEVICE, "libllmq_cuda: cannot query device %d (%s)", dev, cudaGetErrorString(e));
+    return nullptr;
+  }
+  if (prop.major != 10) {
+    llmq_set_error(LLMQ_ERR_NO_DEVICE, "libllmq_cuda: device %d is sm_%d%d; this build targets sm_100a (B200)", dev,
+                   prop.major, prop.minor);
+    return nullptr;
+  }
+  c.device = dev;
+  c.num_sms = prop.multiProcessorCount;
+  c.max_smem = static_cast<int>(prop.sharedMemPerBlockOptin) - 2048;  // room for static shared memory
+  if (cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaStreamCreate failed");
+    return nullptr;
+  }
+  if (!init_expf_table(c)) return nullptr;
+  const int sm = c.max_smem;
+  cudaError_t ea = cudaSuccess;
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_PLAIN, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_PLAIN, 8>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_PLAIN, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_EMBED_RMSNORM, EPI_QKV, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_QKV, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_RESID, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_SWIGLU, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_LOGITS, 1>(sm);
+  ea = ea != cudaSuccess ? ea
+                         : cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  if (ea != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
+    return nullptr;
+  }
+  if (cudaMalloc(&c.err, 16) != cudaSuccess || cudaMemset(c.err, 0, 16) != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_OOM, "libllmq_cuda: device allocation failed");
+    return nullptr;
+  }
+  c.ready = true;
+  return &c;
+}
+
+// Grow-only device buffer (contents not preserved).
+template <typename T>
+int ensure(T **p, size_t *have, size_t need, bool zero) {
+  if (*have >= need && *p) return 1;
+  cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  const size_t n = std::max<size_t>(need, 1);
+  CK(cudaMalloc(p, n * sizeof(T)));
+  if (zero) CK(cudaMemset(*p, 0, n * sizeof(T)));
+  *have = n;
+  return 1;
+}
+
+// -------------------------------------------------------------- weight tiling
+// Builds the tiled copy of a (K, N) matrix whose physical column p is column
+// colsrc[p] & 0xffffff of source colsrc[p] >> 24 (-1 = zero padding).
+int build_mat(Mat &out, int K, int Nlog, int NT, const std::vector<int> &colsrc, const signed char *const src[3],
+              const int srcN[3], const float *const srcScale[3]) {
+  out = Mat{};
+  out.K = K;
+  out.N = Nlog;
+  out.NT = NT;
+  out.KT = kKT;
+  out.Kpad = std::max(roundup(K, kKT), kKT);
+  out.Npad = static_cast<int>(colsrc.size());
+  out.n_slabs = out.Npad / NT;
+  out.n_ktiles = out.Kpad / kKT;
+  CK(cudaMalloc(&out.w, std::max<size_t>(out.bytes(), 16)));
+  CK(cudaMalloc(&out.ws, (size_t)out.Npad * sizeof(float)));
+  RepackSrc rs{};
+  int8_t *tmp[3] = {nullptr, nullptr, nullptr};
+  for (int i = 0; i < 3; ++i) {
+    rs.ncols[i] = srcN[i];
+    if (!src[i] || K == 0 || srcN[i] == 0) continue;
+    const size_t bytes = (size_t)K * srcN[i];
+    CK(cudaMalloc(&tmp[i], bytes));
+    CK(cudaMemcpy(tmp[i], src[i], bytes, cudaMemcpyHostToDevice));
+    rs.m[i] = tmp[i];
+  }
+  int *dcol = nullptr;
+  CK(cudaMalloc(&dcol, colsrc.size() * sizeof(int)));
+  CK(cudaMemcpy(dcol, colsrc.data(), colsrc.size() * sizeof(int), cudaMemcpyHostToDevice));
+  const long long chunks = (long long)out.Kpad / 16 * out.Npad;
+  const int blocks = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148LL * 64));
+  k_repack<<<std::max(blocks, 1), 256>>>(rs, dcol, K, out.Kpad, out.Npad, NT, kKT, out.w);
+  CK(cudaGetLastError());
+  std::vector<float> ws(out.Npad, 0.0f);
+  for (int p = 0; p < out.Npad; ++p) {
+    const int cs = colsrc[p];
+    if (cs >= 0) ws[p] = srcScale[cs >> 24][cs & 0xffffff];
+  }
+  CK(cudaMemcpy(out.ws, ws.data(), ws.size() * sizeof(float), cudaMemcpyHostToDevice));
+  CK(cudaDeviceSynchronize());
+  for (int i = 0; i < 3; ++i) cudaFree(tmp[i]);
+  cudaFree(dcol);
+  return 1;
+}
+
+int build_plain(Mat &out, const QTensor &W) {
+  const int NT = 256;
+  const int Npad = std::max(roundup(W.cols, NT), NT);
+  std::vector<int> colsrc(Npad, -1);
+  for (int j = 0; j < W.cols; ++j) colsrc[j] = j;
+  const signed char *src[3] = {W.q, nullptr, nullptr};
+  const int srcN[3] = {W.cols, 0, 0};
+  const float *sc[3] = {W.scale, nullptr, nullptr};
+  return build_mat(out, W.rows, W.cols, NT, colsrc, src, srcN, sc);
+}
+
+// --------------------------------------------------------------- GEMV launch
+struct GemvPlan {
+  int stages = 0;
+  int grid = 0;
+  size_t smem = 0;
+};
+
+int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
+  const size_t tile = (size_t)m.KT * m.NT;
+  const size_t codes = align16((size_t)rows * m.Kpad);
+  size_t xs = std::max<size_t>((size_t)m.NT * 4, (size_t)kThreads * 4);
+  if (pro != PRO_ABSMAX) xs = std::max<size_t>(xs, (size_t)m.K * 4);
+  const size_t fixed = codes + align16(xs);
+  const size_t budget = (size_t)c.max_smem;
+  if (fixed + 2 * (tile + 8) + 16 > budget) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: GEMV K=%d x %d rows does not fit in shared memory", m.K, rows);
+    return 0;
+  }
+  int S = static_cast<int>((budget - fixed - 16) / (tile + 8));
+  S = std::min(S, 12);
+  const long long T = (long long)m.n_slabs * m.n_ktiles;
+  p.stages = S;
+  p.smem = align16((size_t)S * tile + 8 * (size_t)S) + codes + align16(xs);
+  p.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(T, c.num_sms)));
+  return 1;
+}
+
+GemvArgs base_args(const Mat &m, const GemvPlan &p, int *acc, int *cnt, int *err) {
+  GemvArgs a{};
+  a.w = m.w;
+  a.ws = m.ws;
+  a.K = m.K;
+  a.Kpad = m.Kpad;
+  a.N = m.N;
+  a.Npad = m.Npad;
+  a.NT = m.NT;
+  a.KT = m.KT;
+  a.n_slabs = m.n_slabs;
+  a.n_ktiles = m.n_ktiles;
+  a.stages = p.stages;
+  a.rows = 1;
+  a.acc = acc;
+  a.cnt = cnt;
+  a.err = err;
+  return a;
+}
+
+template <int PRO, int EPI, int MR>
+cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(p.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = p.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_gemv<PRO, EPI, MR>, a);
+}
+
+cudaError_t launch_attention(const AttnArgs &a, size_t smem, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(a.n_heads);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_attention, a);
+}
+
+cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
+                          int max_seq, cudaStream_t st) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k_step_finish, step, argmax, err, result, tokens, max_seq);
+}
+
+// ------------------------------------------------------------------- models
+struct DevModel;
+
+struct DevKV {
+  const void *key = nullptr;
+  DevModel *model = nullptr;
+  int max_seq = 0;
+  float *k = nullptr, *v = nullptr;  // [n_layers][max_seq][kvd]
+  cudaGraphExec_t graph[3] = {nullptr, nullptr, nullptr};  // device-chained, host io, host io + logits
+};
+
+struct DevModel {
+  const void *key = nullptr;
+  int device = -1;
+  LlmqConfig cfg{};
+  int qd = 0, kvd = 0;
+  std::vector<Mat> qkv, wo, w13, w2;
+  Mat lm;
+  std::vector<float *> attn_norm, ffn_norm, bias_qkv;
+  float *final_norm = nullptr;
+  int8_t *wte_q = nullptr;
+  float *wte_s = nullptr;
+  float *rope_cos = nullptr, *rope_sin = nullptr;
+  // activations and scratch
+  float *x = nullptr, *q = nullptr, *o = nullptr, *h = nullptr, *logits = nullptr;
+  int *acc = nullptr, *cnt = nullptr, *err = nullptr, *result = nullptr, *tokens = nullptr;
+  unsigned long long *argmax = nullptr;
+  StepState *step = nullptr;
+  // pinned host staging
+  StepState *h_step = nullptr;
+  int *h_result = nullptr;
+  int *h_tokens = nullptr;
+  float *h_logits = nullptr;
+  cudaStream_t stream = nullptr;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  // launch plans
+  GemvPlan p_qkv, p_wo, p_w13, p_w2, p_lm;
+  size_t attn_smem = 0;
+  int max_npad = 0, max_slabs = 0;
+  std::vector<DevKV *> kvs;
+};
+
+std::unordered_map<const void *, DevModel *> g_models;
+std::unordered_map<const void *, DevKV *> g_kvs;
+float g_last_ms = 0.0f;
+
+void release_kv(DevKV *K) {
+  for (auto &g : K->graph)
+    if (g) cudaGraphExecDestroy(g);
+  cudaFree(K->k);
+  cudaFree(K->v);
+  delete K;
+}
+
+void release_model(DevModel *M) {
+  int cur = -1;
+  cudaGetDevice(&cur);
+  if (M->device >= 0) cudaSetDevice(M->device);
+  if (M->stream) cudaStreamSynchronize(M->stream);
+  for (DevKV *K : M->kvs) {
+    g_kvs.erase(K->key);
+    release_kv(K);
+  }
+  for (auto *v : {&M->qkv, &M->wo, &M->w13, &M->w2})
+    for (Mat &m : *v) free_mat(m);
+  free_mat(M->lm);
+  for (auto *v : {&M->attn_norm, &M->ffn_norm, &M->bias_qkv})
+    for (float *p : *v) cudaFree(p);
+  void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o,
+                      M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step};
+  for (void *p : dev_ptrs) cudaFree(p);
+  cudaFreeHost(M->h_step);
+  cudaFreeHost(M->h_result);
+  cudaFreeHost(M->h_tokens);
+  cudaFreeHost(M->h_logits);
+  if (M->ev0) cudaEventDestroy(M->ev0);
+  if (M->ev1) cudaEventDestroy(M->ev1);
+  if (M->stream) cudaStreamDestroy(M->stream);
+  delete M;
+  if (cur >= 0) cudaSetDevice(cur);
+}
+
+template <typename T>
+int dev_upload(T **dst, const T *src, size_t n) {
+  CK(cudaMalloc(dst, std::max<size_t>(n, 1) * sizeof(T)));
+  if (n) CK(cudaMemcpy(*dst, src, n * sizeof(T), cudaMemcpyHostToDevice));
+  return 1;
+}
+template <typename T>
+int dev_zeros(T **dst, size_t n) {
+  CK(cudaMalloc(dst, std::max<size_t>(n, 1) * sizeof(T)));
+  CK(cudaMemset(*dst, 0, std::max<size_t>(n, 1) * sizeof(T)));
+  return 1;
+}
+
+int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
+  LlmqConfig &cfg = M->cfg;
+  cfg.vocab = m->vocab;
+  cfg.d_model = m->d_model;
+  cfg.n_layers = m->n_layers;
+  cfg.n_heads = m->n_heads;
+  cfg.n_kv = m->n_kv;
+  cfg.head_dim = m->head_dim;
+  cfg.d_ff = m->d_ff;
+  cfg.max_seq = m->max_seq;
+  cfg.rope_base = m->rope_base;
+  cfg.eps = m->eps;
+  const int dm = cfg.d_model, hd = cfg.head_dim, dff = cfg.d_ff, L = cfg.n_layers;
+  M->qd = cfg.n_heads * hd;
+  M->kvd = cfg.n_kv * hd;
+  const int qd = M->qd, kvd = M->kvd;
+  if (hd % 2 != 0 || hd > 256) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: head_dim %d unsupported (even, <= 256)", hd);
+    return 0;
+  }
+  M->device = c.device;
+  CK(cudaStreamCreateWithFlags(&M->stream, cudaStreamNonBlocking));
+  CK(cudaEventCreate(&M->ev0));
+  CK(cudaEventCreate(&M->ev1));
+  // fused QKV: [Wq | Wk | Wv], slabs of whole heads
+  const int nt_qkv = (256 / hd) * hd;
+  const int n_qkv = qd + 2 * kvd;
+  for (int l = 0; l < L; ++l) {
+    const QLlamaBlock &b = m->blocks[l];
+    {
+      const int Npad = roundup(n_qkv, nt_qkv);
+      std::vector<int> cs(Npad, -1);
+      for (int p = 0; p < n_qkv; ++p)
+        cs[p] = p < qd ? p : (p < qd + kvd ? ((1 << 24) | (p - qd)) : ((2 << 24) | (p - qd - kvd)));
+      const signed char *src[3] = {b.Wq.q, b.Wk.q, b.Wv.q};
+      const int sn[3] = {qd, kvd, kvd};
+      const float *ss[3] = {b.Wq.scale, b.Wk.scale, b.Wv.scale};
+      M->qkv.emplace_back();
+      if (!build_mat(M->qkv.back(), dm, n_qkv, nt_qkv, cs, src, sn, ss)) return 0;
+      std::vector<float> bias(Npad, 0.0f);
+      std::memcpy(bias.data(), b.b_q.data, qd * sizeof(float));
+      std::memcpy(bias.data() + qd, b.b_k.data, kvd * sizeof(float));
+      std::memcpy(bias.data() + qd + kvd, b.b_v.data, kvd * sizeof(float));
+      float *db = nullptr;
+      if (!dev_upload(&db, bias.data(), bias.size())) return 0;
+      M->bias_qkv.push_back(db);
+    }
+    M->wo.emplace_back();
+    if (!build_plain(M->wo.back(), b.Wo)) return 0;
+    {
+      // W1|W3 interleaved per slab: 128 gate columns, then the same 128 up columns
+      const int half = 128, NT = 2 * half;
+      const int slabs = (dff + half - 1) / half;
+      std::vector<int> cs((size_t)slabs * NT, -1);
+      for (int s = 0; s < slabs; ++s)
+        for (int c2 = 0; c2 < half; ++c2) {
+          const int j = s * half + c2;
+          if (j < dff) {
+            cs[(size_t)s * NT + c2] = j;
+            cs[(size_t)s * NT + half + c2] = (1 << 24) | j;
+          }
+        }
+      const signed char *src[3] = {b.Wgate.q, b.Wup.q, nullptr};
+      const int sn[3] = {dff, dff, 0};
+      const float *ss[3] = {b.Wgate.scale, b.Wup.scale, nullptr};
+      M->w13.emplace_back();
+      if (!build_mat(M->w13.back(), dm, dff, NT, cs, src, sn, ss)) return 0;
+    }
+    M->w2.emplace_back();
+    if (!build_plain(M->w2.back(), b.Wdown)) return 0;
+    float *an = nullptr, *fn = nullptr;
+    if (!dev_upload(&an, b.attn_norm.data, dm) || !dev_upload(&fn, b.ffn_norm.data, dm)) return 0;
+    M->attn_norm.push_back(an);
+    M->ffn_norm.push_back(fn);
+  }
+  if (!build_plain(M->lm, m->lm_head)) return 0;
+  if (!dev_upload(&M->final_norm, m->final_norm.data, dm)) return 0;
+  if (!dev_upload(&M->wte_q, reinterpret_cast<const int8_t *>(m->wte.q), (size_t)m->vocab * dm)) return 0;
+  if (!dev_upload(&M->wte_s, m->wte.scale, dm)) return 0;
+  {
+    const size_t n = (size_t)cfg.max_seq * (hd / 2);
+    std::vector<float> cs(n), sn(n);
+    llmq_rope_tables(cfg.rope_base, hd, cfg.max_seq, cs.data(), sn.data());
+    if (!dev_upload(&M->rope_cos, cs.data(), n) || !dev_upload(&M->rope_sin, sn.data(), n)) return 0;
+  }
+  // plans and scratch
+  if (!plan_gemv(c, M->qkv[0], PRO_RMSNORM, 1, M->p_qkv) || !plan_gemv(c, M->wo[0], PRO_ABSMAX, 1, M->p_wo) ||
+      !plan_gemv(c, M->w13[0], PRO_RMSNORM, 1, M->p_w13) || !plan_gemv(c, M->w2[0], PRO_ABSMAX, 1, M->p_w2) ||
+      !plan_gemv(c, M->lm, PRO_RMSNORM, 1, M->p_lm))
+    return 0;
+  M->attn_smem = ((size_t)((hd + 3) & ~3) + (size_t)cfg.max_seq) * sizeof(float);
+  if (M->attn_smem > (size_t)c.max_smem) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: max_seq %d too long for the attention kernel", cfg.max_seq);
+    return 0;
+  }
+  int max_npad = 0, max_slabs = 0;
+  for (auto *v : {&M->qkv, &M->wo, &M->w13, &M->w2})
+    for (Mat &mm : *v) {
+      max_npad = std::max(max_npad, mm.Npad);
+      max_slabs = std::max(max_slabs, mm.n_slabs);
+    }
+  max_npad = std::max(max_npad, M->lm.Npad);
+  max_slabs = std::max(max_slabs, M->lm.n_slabs);
+  M->max_npad = max_npad;
+  M->max_slabs = max_slabs;
+  if (!dev_zeros(&M->x, dm) || !dev_zeros(&M->q, qd) || !dev_zeros(&M->o, qd) || !dev_zeros(&M->h, dff) ||
+      !dev_zeros(&M->logits, std::max(cfg.vocab, max_npad)) || !dev_zeros(&M->acc, max_npad) ||
+      !dev_zeros(&M->cnt, max_slabs) || !dev_zeros(&M->err, 4) || !dev_zeros(&M->result, 4) ||
+      !dev_zeros(&M->tokens, cfg.max_seq) || !dev_zeros(&M->argmax, 1) || !dev_zeros(&M->step, 1))
+    return 0;
+  CK(cudaMallocHost(&M->h_step, sizeof(StepState)));
+  CK(cudaMallocHost(&M->h_result, 4 * sizeof(int)));
+  CK(cudaMallocHost(&M->h_tokens, (size_t)cfg.max_seq * sizeof(int)));
+  CK(cudaMallocHost(&M->h_logits, (size_t)cfg.vocab * sizeof(float)));
+  CK(cudaDeviceSynchronize());
+  return 1;
+}
+
+DevModel *find_model(const QLlamaModel *m) {
+  auto it = g_models.find(m->blocks);
+  return it == g_models.end() ? nullptr : it->second;
+}
+
+DevModel *get_model(const QLlamaModel *m) {
+  if (!m || !m->blocks) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: null model");
+    return nullptr;
+  }
+  if (DevModel *M = find_model(m)) {
+    if (cudaSetDevice(M->device) != cudaSuccess) {
+      llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cannot select device %d", M->device);
+      return nullptr;
+    }
+    return M;
+  }
+  DevCtx *c = get_ctx();
+  if (!c) return nullptr;
+  DevModel *M = new DevModel();
+  M->key = m->blocks;
+  if (!upload_model(*c, m, M)) {
+    release_model(M);
+    return nullptr;
+  }
+  g_models[M->key] = M;
+  return M;
+}
+
+DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
+  if (!kv || !kv->k || !kv->v) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: null KV cache");
+    return nullptr;
+  }
+  auto it = g_kvs.find(kv->k);
+  if (it != g_kvs.end()) {
+    if (it->second->model != M) {
+      llmq_set_error(LLMQ_ERR_STATE, "libllmq_cuda: this KV cache belongs to another model");
+      return nullptr;
+    }
+    return it->second;
+  }
+  const LlmqConfig &cfg = M->cfg;
+  if (kv->n_layers != cfg.n_layers || kv->kv_dim != M->kvd || kv->max_seq <= 0 || kv->max_seq > cfg.max_seq) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: KV cache shape (%d layers, kv_dim %d, max_seq %d) does not match the model",
+                   kv->n_layers, kv->kv_dim, kv->max_seq);
+    return nullptr;
+  }
+  DevKV *K = new DevKV();
+  K->key = kv->k;
+  K->model = M;
+  K->max_seq = kv->max_seq;
+  const size_t per_layer = (size_t)kv->max_seq * M->kvd;
+  if (!dev_zeros(&K->k, per_layer * cfg.n_layers) || !dev_zeros(&K->v, per_layer * cfg.n_layers)) {
+    release_kv(K);
+    return nullptr;
+  }
+  // A cache that already holds positions (filled elsewhere): adopt its rows.
+  const int len = std::min(std::max(kv->len, 0), kv->max_seq);
+  for (int l = 0; l < cfg.n_layers && len > 0; ++l) {
+    if (cudaMemcpy(K->k + l * per_layer, kv->k[l], (size_t)len * M->kvd * sizeof(float), cudaMemcpyHostToDevice) !=
+            cudaSuccess ||
+        cudaMemcpy(K->v + l * per_layer, kv->v[l], (size_t)len * M->kvd * sizeof(float), cudaMemcpyHostToDevice) !=
+            cudaSuccess) {
+      llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: KV upload failed");
+      release_kv(K);
+      return nullptr;
+    }
+  }
+  M->kvs.push_back(K);
+  g_kvs[K->key] = K;
+  return K;
+}
+
+// Records one decode step into the model stream.  mode 0: token/pos come from
+// the device state (chained steps); 1: copied from h_step, result copied back;
+// 2: as 1, plus the logits.
+int record_step(DevModel *M, DevKV *K, int mode) {
+  cudaStream_t st = M->stream;
+  const LlmqConfig &cfg = M->cfg;
+  const size_t per_layer = (size_t)K->max_seq * M->kvd;
+  if (mode > 0) CK(cudaMemcpyAsync(M->step, M->h_step, sizeof(StepState), cudaMemcpyHostToDevice, st));
+  for (int l = 0; l < cfg.n_layers; ++l) {
+    {
+      GemvArgs a = base_args(M->qkv[l], M->p_qkv, M->acc, M->cnt, M->err);
+      a.in = M->x;
+      a.gamma = M->attn_norm[l];
+      a.eps = cfg.eps;
+      a.step = M->step;
+      a.out = M->q;
+      a.bias = M->bias_qkv[l];
+      a.qd = M->qd;
+      a.kvd = M->kvd;
+      a.hd = cfg.head_dim;
+      a.max_seq = K->max_seq;
+      a.kcache = K->k + l * per_layer;
+      a.vcache = K->v + l * per_layer;
+      a.rope_cos = M->rope_cos;
+      a.rope_sin = M->rope_sin;
+      if (l == 0) {
+        a.wte_q = M->wte_q;
+        a.wte_s = M->wte_s;
+        a.vocab = cfg.vocab;
+        a.x_out = M->x;
+        CK((launch_gemv<PRO_EMBED_RMSNORM, EPI_QKV, 1>(a, M->p_qkv, st, false)));
+      } else {
+        CK((launch_gemv<PRO_RMSNORM, EPI_QKV, 1>(a, M->p_qkv, st, true)));
+      }
+    }
+    {
+      AttnArgs a{};
+      a.q = M->q;
+      a.kcache = K->k + l * per_layer;
+      a.vcache = K->v + l * per_layer;
+      a.out = M->o;
+      a.step = M->step;
+      a.n_heads = cfg.n_heads;
+      a.n_kv = cfg.n_kv;
+      a.hd = cfg.head_dim;
+      a.max_seq = K->max_seq;
+      CK(launch_attention(a, M->attn_smem, st, true));
+    }
+    {
+      GemvArgs a = base_args(M->wo[l], M->p_wo, M->acc, M->cnt, M->err);
+      a.in = M->o;
+      a.out = M->x;
+      CK((launch_gemv<PRO_ABSMAX, EPI_RESID, 1>(a, M->p_wo, st, true)));
+    }
+    {
+      GemvArgs a = base_args(M->w13[l], M->p_w13, M->acc, M->cnt, M->err);
+      a.in = M->x;
+      a.gamma = M->ffn_norm[l];
+      a.eps = cfg.eps;
+      a.out = M->h;
+      CK((launch_gemv<PRO_RMSNORM, EPI_SWIGLU, 1>(a, M->p_w13, st, true)));
+    }
+    {
+      GemvArgs a = base_args(M->w2[l], M->p_w2, M->acc, M->cnt, M->err);
+      a.in = M->h;
+      a.out = M->x;
+      CK((launch_gemv<PRO_ABSMAX, EPI_RESID, 1>(a, M->p_w2, st, true)));
+    }
+  }
+  {
+    GemvArgs a = base_args(M->lm, M->p_lm, M->acc, M->cnt, M->err);
+    a.in = M->x;
+    a.gamma = M->final_norm;
+    a.eps = cfg.eps;
+    a.out = M->logits;
+    a.argmax = M->argmax;
+    CK((launch_gemv<PRO_RMSNORM, EPI_LOGITS, 1>(a, M->p_lm, st, true)));
+  }
+  CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st));
+  if (mode > 0) CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (mode == 2)
+    CK(cudaMemcpyAsync(M->h_logits, M->logits, (size_t)cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost, st));
+  return 1;
+}
+
+int get_graph(DevModel *M, DevKV *K, int mode, cudaGraphExec_t *out) {
+  if (K->graph[mode]) {
+    *out = K->graph[mode];
+    return 1;
+  }
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(M->stream, cudaStreamCaptureModeThreadLocal));
+  const int ok = record_step(M, K, mode);
+  const cudaError_t e = cudaStreamEndCapture(M->stream, &g);
+  if (!ok) {
+    if (g) cudaGraphDestroy(g);
+    return 0;
+  }
+  CK(e);
+  const cudaError_t ei = cudaGraphInstantiate(&K->graph[mode], g, 0);
+  cudaGraphDestroy(g);
+  CK(ei);
+  *out = K->graph[mode];
+  return 1;
+}
+
+int check_step_inputs(DevModel *M, const LlamaKV *kv, int token, int n) {
+  if (token < 0 || token >= M->cfg.vocab) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: token id %d outside [0, %d)", token, M->cfg.vocab);
+    return 0;
+  }
+  if (kv->len < 0 || kv->len + n > kv->max_seq) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: position %d + %d steps exceeds max_seq %d", kv->len, n, kv->max_seq);
+    return 0;
+  }
+  return 1;
+}
+
+int reset_after_device_error(DevModel *M, int flags) {
+  // A failed launch may leave partial sums behind: clear the scratch words.
+  cudaMemsetAsync(M->acc, 0, (size_t)M->max_npad * sizeof(int), M->stream);
+  cudaMemsetAsync(M->cnt, 0, (size_t)M->max_slabs * sizeof(int), M->stream);
+  cudaMemsetAsync(M->argmax, 0, sizeof(unsigned long long), M->stream);
+  cudaMemsetAsync(M->err, 0, 4 * sizeof(int), M->stream);
+  cudaStreamSynchronize(M->stream);
+  llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: device reported error flags 0x%x (%s%s%s)", flags,
+                 (flags & ERR_TIMEOUT) ? "copy timeout " : "", (flags & ERR_BAD_TOKEN) ? "bad token " : "",
+                 (flags & ERR_BAD_POS) ? "bad position" : "");
+  return 0;
+}
+
+}  // namespace
+
+// ======================================================================== API
+extern "C" {
+
+int llmqd_quantize(const float *w, int rows, int cols, signed char *q, float *scale) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (rows < 0 || cols < 0) {
+    llmq_set_error(LLMQ_ERR_ARG, "quantize_int8_percol: negative shape");
+    return 0;
+  }
+  if (cols == 0) return 1;
+  DevCtx *c = get_ctx();
+  if (!c) return 0;
+  const size_t n = (size_t)rows * cols;
+  float *dw = nullptr, *ds = nullptr;
+  int8_t *dq = nullptr;
+  int ok = 1;
+  if (cudaMalloc(&dw, std::max<size_t>(n, 1) * 4) != cudaSuccess || cudaMalloc(&dq, std::max<size_t>(n, 1)) != cudaSuccess ||
+      cudaMalloc(&ds, (size_t)cols * 4) != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_OOM, "quantize_int8_percol: device allocation of %zu bytes failed", n * 5);
+    ok = 0;
+  }
+  if (ok && n && cudaMemcpy(dw, w, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) ok = 0;
+  if (ok) {
+    k_quantize_percol<<<(cols + 127) / 128, 128, 0, c->stream>>>(dw, rows, cols, dq, ds);
+    if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(c->stream) != cudaSuccess) ok = 0;
+  }
+  if (ok && n && cudaMemcpy(q, dq, n, cudaMemcpyDeviceToHost) != cudaSuccess) ok = 0;
+  if (ok && cudaMemcpy(scale, ds, (size_t)cols * 4, cudaMemcpyDeviceToHost) != cudaSuccess) ok = 0;
+  if (!ok && q_llama_last_error() == LLMQ_OK)
+    llmq_set_error(LLMQ_ERR_CUDA, "quantize_int8_percol: CUDA failure (%s)", cudaGetErrorString(cudaGetLastError()));
+  cudaFree(dw);
+  cudaFree(dq);
+  cudaFree(ds);
+  return ok;
+}
+
+int llmqd_dequantize(const signed char *q, const float *scale, int rows, int cols, float *w) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (rows < 0 || cols < 0) {
+    llmq_set_error(LLMQ_ERR_ARG, "dequantize_int8_percol: negative shape");
+    return 0;
+  }
+  const size_t n = (size_t)rows * cols;
+  if (n == 0) return 1;
+  DevCtx *c = get_ctx();
+  if (!c) return 0;
+  float *dw = nullptr, *ds = nullptr;
+  int8_t *dq = nullptr;
+  int ok = cudaMalloc(&dw, n * 4) == cudaSuccess && cudaMalloc(&dq, n) == cudaSuccess &&
+           cudaMalloc(&ds, (size_t)cols * 4) == cudaSuccess;
+  ok = ok && cudaMemcpy(dq, q, n, cudaMemcpyHostToDevice) == cudaSuccess &&
+       cudaMemcpy(ds, scale, (size_t)cols * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  if (ok) {
+    k_dequantize_percol<<<std::min<long long>((n + 255) / 256, 148 * 32), 256, 0, c->stream>>>(dq, ds, rows, cols, dw);
+    ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(c->stream) == cudaSuccess;
+  }
+  ok = ok && cudaMemcpy(w, dw, n * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+  if (!ok) llmq_set_error(LLMQ_ERR_CUDA, "dequantize_int8_percol: CUDA failure");
+  cudaFree(dw);
+  cudaFree(dq);
+  cudaFree(ds);
+  return ok;
+}
+
+void llmqd_forget_weight(const void *q) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  for (DevCtx &c : g_ctx) {
+    if (!c.ready) continue;
+    auto it = c.weights.find(q);
+    if (it == c.weights.end()) continue;
+    cudaSetDevice(c.device);
+    free_mat(it->second.mat);
+    c.weights.erase(it);
+  }
+}
+
+int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (M == 0 || W->cols == 0) return 1;
+  DevCtx *c = get_ctx();
+  if (!c) return 0;
+  auto it = c->weights.find(W->q);
+  if (it != c->weights.end() &&
+      (it->second.rows != W->rows || it->second.cols != W->cols || it->second.scale != W->scale)) {
+    free_mat(it->second.mat);
+    c->weights.erase(it);
+    it = c->weights.end();
+  }
+  if (it == c->weights.end()) {
+    WeightEntry e{};
+    e.rows = W->rows;
+    e.cols = W->cols;
+    e.scale = W->scale;
+    if (!build_plain(e.mat, *W)) return 0;
+    it = c->weights.emplace(W->q, e).first;
+  }
+  const Mat &m = it->second.mat;
+  const int K = W->rows, N = W->cols;
+  const bool many = M > 1;
+  GemvPlan plan;
+  int rows_per = many ? 8 : 1;
+  while (true) {
+    if (plan_gemv(*c, m, PRO_ABSMAX, rows_per, plan)) break;
+    if (rows_per == 1) return 0;
+    q_llama_clear_error();
+    rows_per /= 2;
+  }
+  if (!ensure(&c->dA, &c->dA_n, (size_t)M * K, false) || !ensure(&c->dC, &c->dC_n, (size_t)M * N, false) ||
+      !ensure(&c->acc, &c->acc_n, (size_t)8 * m.Npad, true) || !ensure(&c->cnt, &c->cnt_n, (size_t)m.n_slabs, true))
+    return 0;
+  cudaStream_t st = c->stream;
+  if (K > 0) CK(cudaMemcpyAsync(c->dA, A, (size_t)M * K * sizeof(float), cudaMemcpyHostToDevice, st));
+  for (int r0 = 0; r0 < M; r0 += rows_per) {
+    GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
+    a.rows = std::min(rows_per, M - r0);
+    a.in = c->dA + (size_t)r0 * K;
+    a.out = c->dC + (size_t)r0 * N;
+    if (many)
+      CK((launch_gemv<PRO_ABSMAX, EPI_PLAIN, 8>(a, plan, st, false)));
+    else
+      CK((launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, plan, st, false)));
+  }
+  CK(cudaMemcpyAsync(C, c->dC, (size_t)M * N * sizeof(float), cudaMemcpyDeviceToHost, st));
+  int flags = 0;
+  CK(cudaMemcpyAsync(&flags, c->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (flags) {
+    cudaMemset(c->err, 0, 16);
+    cudaMemset(c->acc, 0, c->acc_n * sizeof(int));
+    cudaMemset(c->cnt, 0, c->cnt_n * sizeof(int));
+    llmq_set_error(LLMQ_ERR_CUDA, "qmatmul: device reported error flags 0x%x", flags);
+    return 0;
+  }
+  return 1;
+}
+
+int llmqd_model_upload(const QLlamaModel *m) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return get_model(m) != nullptr;
+}
+
+void llmqd_model_release(const QLlamaModel *m) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!m || !m->blocks) return;
+  auto it = g_models.find(m->blocks);
+  if (it == g_models.end()) return;
+  DevModel *M = it->second;
+  g_models.erase(it);
+  release_model(M);
+}
+
+int llmqd_kv_register(const QLlamaModel *m, const LlamaKV *kv) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevModel *M = get_model(m);
+  return M && get_kv(M, kv) != nullptr;
+}
+
+void llmqd_kv_release(const LlamaKV *kv) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!kv || !kv->k) return;
+  auto it = g_kvs.find(kv->k);
+  if (it == g_kvs.end()) return;
+  DevKV *K = it->second;
+  g_kvs.erase(it);
+  DevModel *M = K->model;
+  auto &v = M->kvs;
+  v.erase(std::remove(v.begin(), v.end(), K), v.end());
+  int cur = -1;
+  cudaGetDevice(&cur);
+  cudaSetDevice(M->device);
+  cudaStreamSynchronize(M->stream);
+  release_kv(K);
+  if (cur >= 0) cudaSetDevice(cur);
+}
+
+int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevModel *M = get_model(m);
+  if (!M) return 0;
+  DevKV *K = get_kv(M, kv);
+  if (!K || !check_step_inputs(M, kv, token, 1)) return 0;
+  const int mode = logits ? 2 : 1;
+  cudaGraphExec_t g = nullptr;
+  if (!get_graph(M, K, mode, &g)) return 0;
+  M->h_step->token = token;
+  M->h_step->pos = kv->len;
+  CK(cudaEventRecord(M->ev0, M->stream));
+  CK(cudaGraphLaunch(g, M->stream));
+  CK(cudaEventRecord(M->ev1, M->stream));
+  CK(cudaStreamSynchronize(M->stream));
+  cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
+  if (M->h_result[1]) return reset_after_device_error(M, M->h_result[1]);
+  if (logits) std::memcpy(logits, M->h_logits, (size_t)M->cfg.vocab * sizeof(float));
+  if (next) *next = M->h_result[0];
+  return 1;
+}
+
+int llmqd_generate(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevModel *M = get_model(m);
+  if (!M) return 0;
+  DevKV *K = get_kv(M, kv);
+  if (!K || n < 0 || !check_step_inputs(M, kv, token, n)) return 0;
+  if (n == 0) return 1;
+  cudaGraphExec_t g = nullptr;
+  if (!get_graph(M, K, 0, &g)) return 0;
+  M->h_step->token = token;
+  M->h_step->pos = kv->len;
+  cudaStream_t st = M->stream;
+  CK(cudaMemcpyAsync(M->step, M->h_step, sizeof(StepState), cudaMemcpyHostToDevice, st));
+  CK(cudaMemsetAsync(M->result, 0, 4 * sizeof(int), st));
+  CK(cudaEventRecord(M->ev0, st));
+  for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(g, st));
+  CK(cudaEventRecord(M->ev1, st));
+  CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(M->h_tokens, M->tokens + kv->len, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
+  if (M->h_result[3]) return reset_after_device_error(M, M->h_result[3]);
+  std::memcpy(ids, M->h_tokens, (size_t)n * sizeof(int));
+  return 1;
+}
+
+int llmqd_kv_download(const QLlamaModel *m, const LlamaKV *kv, int len) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevModel *M = get_model(m);
+  if (!M) return 0;
+  DevKV *K = get_kv(M, kv);
+  if (!K) return 0;
+  const size_t per_layer = (size_t)K->max_seq * M->kvd;
+  CK(cudaStreamSynchronize(M->stream));
+  for (int l = 0; l < M->cfg.n_layers && len > 0; ++l) {
+    CK(cudaMemcpy(kv->k[l], K->k + l * per_layer, (size_t)len * M->kvd * sizeof(float), cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(kv->v[l], K->v + l * per_layer, (size_t)len * M->kvd * sizeof(float), cudaMemcpyDeviceToHost));
+  }
+  return 1;
+}
+
+float llmqd_last_ms(void) { return g_last_ms; }
+
+// ---- diagnostics exported for tests and the benchmark (declared in llmq_cuda.h)
+LLMQ_API int llmq_expf_device(const float *x, float *y, long long n) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (n <= 0) return LLMQ_OK;
+  DevCtx *c = get_ctx();
+  if (!c) return q_llama_last_error();
+  float *dx = nullptr, *dy = nullptr;
+  int ok = cudaMalloc(&dx, n * 4) == cudaSuccess && cudaMalloc(&dy, n * 4) == cudaSuccess &&
+           cudaMemcpy(dx, x, n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  if (ok) {
+    k_expf_batch<<<148 * 8, 256, 0, c->stream>>>(dx, dy, n);
+    ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(c->stream) == cudaSuccess &&
+         cudaMemcpy(y, dy, n * 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+  }
+  cudaFree(dx);
+  cudaFree(dy);
+  if (!ok) {
+    llmq_set_error(LLMQ_ERR_CUDA, "llmq_expf_device: CUDA failure");
+    return LLMQ_ERR_CUDA;
+  }
+  return LLMQ_OK;
+}
+
+// Times `iters` back-to-back launches of one of the model's GEMVs on the model
+// stream (which: 0 QKV, 1 Wo, 2 W1|W3, 3 W2, 4 lm-head) with CUDA events, using
+// the activations left by the last step.  Reports the mean time per launch and
+// the algorithmic bytes of one launch (int8 weights + scales + input + output).
+LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int iters, float *ms_per_launch,
+                             double *bytes_per_launch) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevModel *M = get_model(m);
+  if (!M) return q_llama_last_error();
+  if (layer < 0 || layer >= M->cfg.n_layers || which < 0 || which > 4 || iters <= 0) {
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_bench_gemv: bad arguments");
+    return LLMQ_ERR_ARG;
+  }
+  const Mat *mt[5] = {&M->qkv[layer], &M->wo[layer], &M->w13[layer], &M->w2[layer], &M->lm};
+  const GemvPlan *pl[5] = {&M->p_qkv, &M->p_wo, &M->p_w13, &M->p_w2, &M->p_lm};
+  const bool rms[5] = {true, false, true, false, true};
+  float *ins[5] = {M->x, M->o, M->x, M->h, M->x};
+  const Mat &mm = *mt[which];
+  const GemvPlan &p = *pl[which];
+  GemvArgs a = base_args(mm, p, M->acc, M->cnt, M->err);
+  a.in = ins[which];
+  a.gamma = M->final_norm;
+  a.eps = M->cfg.eps;
+  a.out = M->logits;
+  cudaStream_t st = M->stream;
+  auto launch = [&]() {
+    return rms[which] ? launch_gemv<PRO_RMSNORM, EPI_PLAIN, 1>(a, p, st, false)
+                      : launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, p, st, false);
+  };
+  for (int i = 0; i < 3; ++i)
+    if (launch() != cudaSuccess) return LLMQ_ERR_CUDA;
+  if (cudaEventRecord(M->ev0, st) != cudaSuccess) return LLMQ_ERR_CUDA;
+  for (int i = 0; i < iters; ++i)
+    if (launch() != cudaSuccess) return LLMQ_ERR_CUDA;
+  if (cudaEventRecord(M->ev1, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "llmq_bench_gemv: CUDA failure");
+    return LLMQ_ERR_CUDA;
+  }
+  float ms = 0.0f;
+  cudaEventElapsedTime(&ms, M->ev0, M->ev1);
+  *ms_per_launch = ms / iters;
+  const int logical_n = which == 2 ? 2 * mm.N : mm.N;
+  *bytes_per_launch = (double)mm.K * logical_n + 4.0 * logical_n + 4.0 * mm.K + 4.0 * (which == 2 ? mm.N : mm.N);
+  return LLMQ_OK;
+}
+
+// Number of kernels one decode step launches (for the benchmark's gpu_launches).
+LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) { return 5 * m->n_layers + 2; }
+
+}  // extern "C"

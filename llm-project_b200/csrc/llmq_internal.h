@@ -1,0 +1,48 @@
+/* llmq_internal.h - internal C interface between the C11 host layer
+ * (llmq_host.c, llmq_synth.c) and the CUDA runtime layer (llmq_dev.cu).
+ * Nothing here is exported from libllmq_cuda.so. */
+#ifndef LLMQ_INTERNAL_H
+#define LLMQ_INTERNAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "llmq_cuda.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LLMQ_API __attribute__((visibility("default")))
+#define LLMQ_HIDDEN __attribute__((visibility("hidden")))
+
+/* error state (thread local) */
+LLMQ_HIDDEN void llmq_set_error(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+
+/* RoPE angle tables for positions [0, max_seq): cos/sin of pos * base^(-2k/hd),
+ * evaluated with the host libm exactly as rope.c:59-61 does. */
+LLMQ_HIDDEN void llmq_rope_tables(float base, int head_dim, int max_seq, float *cos_out, float *sin_out);
+
+/* ---- device layer (llmq_dev.cu); all return 1 on success, 0 with the error set */
+LLMQ_HIDDEN int llmqd_quantize(const float *w, int rows, int cols, signed char *q, float *scale);
+LLMQ_HIDDEN int llmqd_dequantize(const signed char *q, const float *scale, int rows, int cols, float *w);
+LLMQ_HIDDEN int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C);
+LLMQ_HIDDEN void llmqd_forget_weight(const void *q);
+
+LLMQ_HIDDEN int llmqd_model_upload(const QLlamaModel *m);
+LLMQ_HIDDEN void llmqd_model_release(const QLlamaModel *m);
+LLMQ_HIDDEN int llmqd_kv_register(const QLlamaModel *m, const LlamaKV *kv);
+LLMQ_HIDDEN void llmqd_kv_release(const LlamaKV *kv);
+/* One decode step at position kv->len.  logits (may be NULL) receives vocab
+ * floats; *next receives the greedy id. */
+LLMQ_HIDDEN int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next);
+/* n greedy steps chained on the device starting from `token` at kv->len;
+ * ids[i] = argmax after step i. */
+LLMQ_HIDDEN int llmqd_generate(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids);
+LLMQ_HIDDEN int llmqd_kv_download(const QLlamaModel *m, const LlamaKV *kv, int len);
+LLMQ_HIDDEN float llmqd_last_ms(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

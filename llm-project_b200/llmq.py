@@ -1,0 +1,174 @@
+"""ctypes binding of libllmq_cuda.so for Python callers (tests, bench).
+
+The C entry points keep the names and argument meaning of the reference's
+quant.h / llama.h (marjoncajocon/llm-project quant.h:15-33, llama.h:114-140),
+so this module mirrors them one to one, plus thin numpy helpers.  There is no
+fallback: if the shared library is missing, `load()` raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libllmq_cuda.so")
+
+c_float_p = C.POINTER(C.c_float)
+c_int_p = C.POINTER(C.c_int)
+c_byte_p = C.POINTER(C.c_byte)
+
+
+class Tensor(C.Structure):  # tensor.h:10-16
+    _fields_ = [("data", c_float_p), ("grad", c_float_p), ("shape", c_int_p), ("ndim", C.c_int),
+                ("size", C.c_size_t)]
+
+
+class QTensor(C.Structure):  # quant.h:22-26
+    _fields_ = [("rows", C.c_int), ("cols", C.c_int), ("q", c_byte_p), ("scale", c_float_p)]
+
+
+class LlamaBlock(C.Structure):  # llama.h:19-36
+    _fields_ = [("d_model", C.c_int), ("n_heads", C.c_int), ("n_kv", C.c_int), ("head_dim", C.c_int),
+                ("d_ff", C.c_int), ("rope_base", C.c_float), ("eps", C.c_float)] + \
+               [(n, Tensor) for n in ("attn_norm", "Wq", "Wk", "Wv", "b_q", "b_k", "b_v", "Wo",
+                                      "ffn_norm", "Wgate", "Wup", "Wdown")]
+
+
+CONFIG_FIELDS = ("vocab", "d_model", "n_layers", "n_heads", "n_kv", "head_dim", "d_ff", "max_seq")
+
+
+class LlamaModel(C.Structure):  # llama.h:59-66
+    _fields_ = [(n, C.c_int) for n in CONFIG_FIELDS] + \
+               [("rope_base", C.c_float), ("eps", C.c_float), ("wte", Tensor),
+                ("blocks", C.POINTER(LlamaBlock)), ("final_norm", Tensor), ("lm_head", Tensor)]
+
+
+class LlamaKV(C.Structure):  # llama.h:94-99
+    _fields_ = [("n_layers", C.c_int), ("max_seq", C.c_int), ("kv_dim", C.c_int), ("len", C.c_int),
+                ("k", C.POINTER(c_float_p)), ("v", C.POINTER(c_float_p))]
+
+
+class QLlamaBlock(C.Structure):  # llama.h:114-118
+    _fields_ = [(n, Tensor) for n in ("attn_norm", "ffn_norm", "b_q", "b_k", "b_v")] + \
+               [(n, QTensor) for n in ("Wq", "Wk", "Wv", "Wo", "Wgate", "Wup", "Wdown")]
+
+
+class QLlamaModel(C.Structure):  # llama.h:120-127
+    _fields_ = [(n, C.c_int) for n in CONFIG_FIELDS] + \
+               [("rope_base", C.c_float), ("eps", C.c_float), ("wte", QTensor),
+                ("blocks", C.POINTER(QLlamaBlock)), ("final_norm", Tensor), ("lm_head", QTensor)]
+
+
+class LlmqConfig(C.Structure):
+    _fields_ = [(n, C.c_int) for n in CONFIG_FIELDS] + [("rope_base", C.c_float), ("eps", C.c_float)]
+
+
+def config(vocab, d_model, n_layers, n_heads, n_kv, head_dim, d_ff, max_seq, rope_base=10000.0,
+           eps=1e-5) -> LlmqConfig:
+    return LlmqConfig(vocab, d_model, n_layers, n_heads, n_kv, head_dim, d_ff, max_seq, rope_base, eps)
+
+
+# Signatures of every exported entry point: name -> (restype, argtypes).
+SIGNATURES = {
+    "quantize_int8_percol": (None, [c_float_p, C.c_int, C.c_int, c_byte_p, c_float_p]),
+    "dequantize_int8_percol": (None, [c_byte_p, c_float_p, C.c_int, C.c_int, c_float_p]),
+    "qtensor_create": (QTensor, [C.c_int, C.c_int]),
+    "qtensor_free": (None, [C.POINTER(QTensor)]),
+    "qtensor_quantize": (None, [C.POINTER(QTensor), c_float_p]),
+    "qmatmul": (None, [C.POINTER(Tensor), C.POINTER(QTensor), C.POINTER(Tensor)]),
+    "q_llama_model_load": (C.c_int, [C.c_char_p, C.POINTER(QLlamaModel)]),
+    "q_llama_model_free": (None, [C.POINTER(QLlamaModel)]),
+    "q_llama_quantize_from": (QLlamaModel, [C.POINTER(LlamaModel)]),
+    "q_llama_kv_create": (LlamaKV, [C.POINTER(QLlamaModel)]),
+    "llama_kv_free": (None, [C.POINTER(LlamaKV)]),
+    "q_llama_decode_step": (None, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, C.POINTER(Tensor)]),
+    "q_llama_last_error": (C.c_int, []),
+    "q_llama_last_error_message": (C.c_char_p, []),
+    "q_llama_clear_error": (None, []),
+    "q_llama_decode_step_argmax": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int,
+                                             C.POINTER(Tensor)]),
+    "q_llama_kv_sync_host": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV)]),
+    "q_llama_model_save": (C.c_int, [C.c_char_p, C.POINTER(QLlamaModel)]),
+    "llmq_synth_model": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_float, C.c_int,
+                                   C.POINTER(QLlamaModel)]),
+    "llmq_synth_qtensor": (None, [C.POINTER(QTensor), C.c_uint64]),
+    "q_llama_model_upload": (C.c_int, [C.POINTER(QLlamaModel)]),
+    "q_llama_generate": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_int, c_int_p]),
+    "q_llama_last_step_ms": (C.c_float, []),
+    "llmq_expf_device": (C.c_int, [c_float_p, c_float_p, C.c_longlong]),
+    "llmq_bench_gemv": (C.c_int, [C.POINTER(QLlamaModel), C.c_int, C.c_int, C.c_int, c_float_p,
+                                  C.POINTER(C.c_double)]),
+    "llmq_kernels_per_step": (C.c_int, [C.POINTER(QLlamaModel)]),
+}
+
+_lib = None
+
+
+def load(path: str | None = None) -> C.CDLL:
+    """Load libllmq_cuda.so and declare its signatures.  Raises if it is missing."""
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = path or LIB_PATH
+    if not os.path.exists(p):
+        raise FileNotFoundError(f"{p} not built: run __graft_entry__.build() (make -C llm-project_b200/csrc)")
+    lib = C.CDLL(p)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = lib
+    return lib
+
+
+class LlmqError(RuntimeError):
+    pass
+
+
+def check(lib) -> None:
+    """Raise LlmqError if the last call on this thread failed."""
+    code = lib.q_llama_last_error()
+    if code != 0:
+        msg = lib.q_llama_last_error_message().decode(errors="replace")
+        lib.q_llama_clear_error()
+        raise LlmqError(f"libllmq_cuda error {code}: {msg}")
+
+
+# ---------------------------------------------------------------- numpy views
+def host_tensor(arr: np.ndarray) -> Tensor:
+    """A Tensor struct viewing a C-contiguous float32 numpy array (no copy)."""
+    assert arr.dtype == np.float32 and arr.flags["C_CONTIGUOUS"]
+    shape = (C.c_int * arr.ndim)(*arr.shape)
+    t = Tensor(arr.ctypes.data_as(c_float_p), None, C.cast(shape, c_int_p), arr.ndim, arr.size)
+    t._keep = (arr, shape)  # keep the buffers alive with the struct
+    return t
+
+
+def qtensor_view(q: np.ndarray, scale: np.ndarray) -> QTensor:
+    """A QTensor struct viewing int8 codes (rows, cols) and f32 scales (cols)."""
+    assert q.dtype == np.int8 and q.flags["C_CONTIGUOUS"] and q.ndim == 2
+    assert scale.dtype == np.float32 and scale.shape == (q.shape[1],)
+    t = QTensor(q.shape[0], q.shape[1], q.ctypes.data_as(c_byte_p), scale.ctypes.data_as(c_float_p))
+    t._keep = (q, scale)
+    return t
+
+
+def qtensor_arrays(t: QTensor) -> tuple[np.ndarray, np.ndarray]:
+    """numpy copies of a QTensor's codes and scales."""
+    q = np.ctypeslib.as_array(C.cast(t.q, c_byte_p), shape=(t.rows * t.cols,)).astype(np.int8)
+    s = np.ctypeslib.as_array(t.scale, shape=(t.cols,)).copy()
+    return q.reshape(t.rows, t.cols).copy(), s
+
+
+def vec_array(t: Tensor) -> np.ndarray:
+    return np.ctypeslib.as_array(t.data, shape=(t.size,)).copy()
+
+
+def model_config(m: QLlamaModel) -> dict:
+    d = {n: getattr(m, n) for n in CONFIG_FIELDS}
+    d["rope_base"] = m.rope_base
+    d["eps"] = m.eps
+    return d

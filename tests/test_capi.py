@@ -1,0 +1,137 @@
+"""CPU: the C-ABI library loads, exports every entry point include/llmq_cuda.h
+declares, and its host-only logic (LLMQ I/O, argument checks, the synthetic
+generator) behaves like the reference.  No GPU compute is called here."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+import struct
+import subprocess
+
+import numpy as np
+import pytest
+
+import llmq
+from conftest import GOLDEN, ROOT, has_gpu
+from helpers import assert_models_equal, synth
+
+
+def declared_functions() -> list[str]:
+    src = open(os.path.join(ROOT, "include", "llmq_cuda.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w \*]*?\b([a-z_][a-z0-9_]*)\s*\(", src, flags=re.M)
+    return sorted(set(n for n in names if n not in ("if", "while", "sizeof")))
+
+
+def test_header_declares_reference_api():
+    names = declared_functions()
+    for n in ("quantize_int8_percol", "dequantize_int8_percol", "qtensor_create", "qtensor_free",
+              "qtensor_quantize", "qmatmul", "q_llama_model_load", "q_llama_model_free",
+              "q_llama_quantize_from", "q_llama_kv_create", "llama_kv_free", "q_llama_decode_step"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", llmq.LIB_PATH], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
+    declared = set(declared_functions())
+    assert declared <= exported, declared - exported
+    assert exported <= declared, exported - declared  # nothing undeclared leaks out
+    for n in declared:
+        assert hasattr(lib, n)
+
+
+def test_binding_covers_every_symbol():
+    assert set(declared_functions()) == set(llmq.SIGNATURES)
+
+
+def test_loader_rejects_bad_files(lib, tmp_path):
+    good = open(os.path.join(GOLDEN, "mini.llmq"), "rb").read()
+    cases = {
+        "missing": None,
+        "short_header": good[:20],
+        "bad_magic": b"LLMA" + good[4:],
+        "bad_version": good[:4] + struct.pack("<I", 1) + good[8:],
+        "bad_config": good[:8] + struct.pack("<i", 0) + good[12:],
+        "gqa_not_dividing": good[:20] + struct.pack("<i", 3) + good[24:],
+        "truncated_weights": good[:-100],
+    }
+    for name, blob in cases.items():
+        p = tmp_path / (name + ".llmq")
+        if blob is not None:
+            p.write_bytes(blob)
+        m = llmq.QLlamaModel()
+        assert lib.q_llama_model_load(str(p).encode(), C.byref(m)) == 1, name
+    lib.q_llama_clear_error()
+
+
+def test_qmatmul_rejects_bad_shapes(lib):
+    A = np.zeros((2, 5), np.float32)
+    out = np.zeros((2, 3), np.float32)
+    q = np.zeros((4, 3), np.int8)  # K mismatch: A has 5 columns
+    s = np.ones(3, np.float32)
+    ta, tc = llmq.host_tensor(A), llmq.host_tensor(out)
+    qt = llmq.qtensor_view(q, s)
+    lib.q_llama_clear_error()
+    lib.qmatmul(C.byref(ta), C.byref(qt), C.byref(tc))
+    assert lib.q_llama_last_error() == 1  # LLMQ_ERR_ARG
+    lib.q_llama_clear_error()
+
+
+@pytest.mark.skipif(has_gpu(), reason="checks the no-GPU failure path")
+def test_no_gpu_fails_loudly(lib):
+    """Without a GPU the library reports an error; it never computes on the CPU."""
+    A = np.ones((1, 4), np.float32)
+    out = np.full((1, 3), 7.0, np.float32)
+    q = np.ones((4, 3), np.int8)
+    s = np.ones(3, np.float32)
+    ta, tc = llmq.host_tensor(A), llmq.host_tensor(out)
+    qt = llmq.qtensor_view(q, s)
+    lib.q_llama_clear_error()
+    lib.qmatmul(C.byref(ta), C.byref(qt), C.byref(tc))
+    assert lib.q_llama_last_error() == 3  # LLMQ_ERR_NO_DEVICE
+    assert np.all(out == 7.0)
+    lib.q_llama_clear_error()
+    m = llmq.QLlamaModel()
+    assert lib.q_llama_model_load(os.path.join(GOLDEN, "mini.llmq").encode(), C.byref(m)) == 1
+    lib.q_llama_clear_error()
+
+
+def test_save_roundtrip_and_reference_loader(lib, orc, ref, tmp_path):
+    cfg = dict(vocab=96, d_model=32, n_layers=2, n_heads=4, n_kv=2, head_dim=8, d_ff=48, max_seq=40,
+               rope_base=10000.0, eps=1e-5)
+    m = synth(lib, cfg, seed=9, with_bias=True)
+    p = str(tmp_path / "s.llmq")
+    assert lib.q_llama_model_save(p.encode(), C.byref(m)) == 0
+    assert not os.path.exists(p + ".tmp")
+    for loader, free in ((orc.orc_model_load, orc.orc_model_free), (ref.q_llama_model_load, ref.q_llama_model_free)):
+        m2 = llmq.QLlamaModel()
+        assert loader(p.encode(), C.byref(m2)) == 0
+        assert_models_equal(m, m2)
+        free(C.byref(m2))
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_synth_is_seeded_and_follows_the_quantisation_rule(lib):
+    cfg = dict(vocab=64, d_model=48, n_layers=1, n_heads=2, n_kv=1, head_dim=24, d_ff=72, max_seq=16,
+               rope_base=10000.0, eps=1e-5)
+    a, b, c = synth(lib, cfg, seed=1), synth(lib, cfg, seed=1), synth(lib, cfg, seed=2)
+    assert_models_equal(a, b)
+    qa, _ = llmq.qtensor_arrays(a.blocks[0].Wq)
+    qc, _ = llmq.qtensor_arrays(c.blocks[0].Wq)
+    assert not np.array_equal(qa, qc)
+    # per-column absmax maps to +-127 exactly (quant.c:52-58)
+    for name in ("Wq", "Wk", "Wv", "Wo", "Wgate", "Wup", "Wdown"):
+        q, s = llmq.qtensor_arrays(getattr(a.blocks[0], name))
+        assert np.all(np.abs(q).max(axis=0) == 127), name
+        assert np.all(s > 0)
+    # weights look like N(0, 0.02): dequantised std within a few percent
+    q, s = llmq.qtensor_arrays(a.lm_head)
+    w = q.astype(np.float64) * s[None, :]
+    assert abs(w.std() - 0.02) < 0.002
+    np.testing.assert_array_equal(llmq.vec_array(a.blocks[0].b_q), 0.0)
+    np.testing.assert_array_equal(llmq.vec_array(a.blocks[0].attn_norm), 1.0)
+    for m in (a, b, c):
+        lib.q_llama_model_free(C.byref(m))

@@ -1,0 +1,231 @@
+"""GPU parity: libllmq_cuda.so against the oracle restatement (itself pinned to
+the reference) and the golden vectors.  The bar is bit-identical output: same
+int8 codes and scales, same f32 logits, same greedy ids."""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import llmq
+from conftest import GOLDEN
+from helpers import (TINY, bits_equal, fp, gpu_decode, gpu_qmatmul, gpu_quantize, orc_decode, orc_greedy,
+                     orc_qmatmul, orc_quantize, synth)
+
+pytestmark = pytest.mark.gpu
+
+
+def load_gpu(lib, path):
+    m = llmq.QLlamaModel()
+    assert lib.q_llama_model_load(path.encode(), C.byref(m)) == 0, lib.q_llama_last_error_message()
+    return m
+
+
+# ----------------------------------------------------------- quantisation
+@pytest.mark.parametrize("shape", [(1, 1), (3, 5), (64, 32), (300, 129), (4096, 1024)])
+def test_quantize_bit_exact(lib, orc, shape):
+    rng = np.random.default_rng(sum(shape))
+    W = (rng.standard_normal(shape) * 0.02).astype(np.float32)
+    W[:, 0] = 0.0
+    if shape[0] > 3:
+        W[2, -1] = 1e-30
+        W[3, -1] = -3e4
+    qg, sg = gpu_quantize(lib, W)
+    qo, so = orc_quantize(orc, W)
+    np.testing.assert_array_equal(qg, qo)
+    assert bits_equal(sg, so)
+
+
+def test_quantize_golden_quant20(lib):
+    d = np.load(os.path.join(GOLDEN, "quant20.npz"))
+    q, s = gpu_quantize(lib, d["W"])
+    np.testing.assert_array_equal(q, d["q"])
+    assert bits_equal(s, d["scale"])
+
+
+def test_dequantize_bit_exact(lib, orc):
+    rng = np.random.default_rng(4)
+    q = rng.integers(-127, 128, size=(70, 33)).astype(np.int8)
+    s = rng.uniform(1e-3, 1e-2, 33).astype(np.float32)
+    wg, wo = np.zeros((70, 33), np.float32), np.zeros((70, 33), np.float32)
+    lib.dequantize_int8_percol(q.ctypes.data_as(llmq.c_byte_p), fp(s), 70, 33, fp(wg))
+    llmq.check(lib)
+    orc.orc_dequantize_int8_percol(q.ctypes.data_as(llmq.c_byte_p), fp(s), 70, 33, fp(wo))
+    assert bits_equal(wg, wo)
+
+
+# ----------------------------------------------------------------- qmatmul
+@pytest.mark.parametrize("M,K,N", [(1, 1, 1), (1, 16, 256), (2, 37, 19), (3, 100, 300), (1, 288, 32000),
+                                   (8, 768, 288), (9, 64, 1000), (17, 288, 96), (1, 4096, 4096),
+                                   (1, 14336, 4096), (4, 4096, 1024)])
+def test_qmatmul_bit_exact(lib, orc, M, K, N):
+    rng = np.random.default_rng(M * 7919 + K * 31 + N)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    q = rng.integers(-127, 128, size=(K, N)).astype(np.int8)
+    s = rng.uniform(1e-3, 1e-2, size=N).astype(np.float32)
+    assert bits_equal(gpu_qmatmul(lib, A, q, s), orc_qmatmul(orc, A, q, s))
+
+
+def test_qmatmul_golden_edges(lib):
+    for name in ("quant20", "qedge"):
+        d = np.load(os.path.join(GOLDEN, name + ".npz"))
+        assert bits_equal(gpu_qmatmul(lib, d["A"], d["q"], d["scale"]), d["C"]), name
+
+
+def test_qmatmul_weight_cache_tracks_contents(lib, orc):
+    """A cached device copy is dropped when the QTensor is re-quantised."""
+    t = lib.qtensor_create(64, 40)
+    rng = np.random.default_rng(8)
+    A = rng.standard_normal((1, 64)).astype(np.float32)
+    outs = []
+    for seed in (1, 2):
+        W = rng.standard_normal((64, 40)).astype(np.float32)
+        lib.qtensor_quantize(C.byref(t), fp(W))
+        llmq.check(lib)
+        out = np.zeros((1, 40), np.float32)
+        ta, tc = llmq.host_tensor(A), llmq.host_tensor(out)
+        lib.qmatmul(C.byref(ta), C.byref(t), C.byref(tc))
+        llmq.check(lib)
+        q, s = llmq.qtensor_arrays(t)
+        assert bits_equal(out, orc_qmatmul(orc, A, q, s))
+        outs.append(out)
+    assert not np.array_equal(outs[0], outs[1])
+    lib.qtensor_free(C.byref(t))
+
+
+# ------------------------------------------------------------------ decode
+def test_decode_golden_selftest21(lib):
+    d = np.load(os.path.join(GOLDEN, "selftest21.npz"))
+    m = load_gpu(lib, os.path.join(GOLDEN, "selftest21.llmq"))
+    logits, _ = gpu_decode(lib, m, d["ids"])
+    assert bits_equal(logits, d["logits"])
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_decode_golden_mini_300_steps(lib):
+    """Biases, rope_base 5e5, positions 0..299: identical logits and ids."""
+    d = np.load(os.path.join(GOLDEN, "mini.npz"))
+    m = load_gpu(lib, os.path.join(GOLDEN, "mini.llmq"))
+    logits, _ = gpu_decode(lib, m, d["fed"])
+    assert bits_equal(logits[d["save_steps"]], d["logits"])
+    arg = logits.argmax(axis=1)  # numpy argmax also returns the first maximum
+    assert arg.tolist() == d["argmax"].tolist()
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_decode_tiny_config_vs_oracle(lib, orc):
+    """configs[0] shape (dm 288, 6 layers, GQA 6/2, hd 48, vocab 32000)."""
+    m = synth(lib, TINY, seed=1234, with_bias=True)
+    rng = np.random.default_rng(5678)
+    prompt = rng.integers(0, TINY["vocab"], 16)
+    fed, arg, ologits = orc_greedy(orc, m, prompt, 24)
+    glogits, _ = gpu_decode(lib, m, fed)
+    assert bits_equal(glogits, ologits)
+    assert glogits.argmax(axis=1).tolist() == arg
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_decode_8b_shapes_two_layers_vs_oracle(lib, orc):
+    """LLaMA-3-8B layer and head shapes (dm 4096, GQA 32/8, hd 128, dff 14336,
+    vocab 128256, rope 5e5) with 2 layers, so the CPU oracle stays fast."""
+    cfg = dict(vocab=128256, d_model=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128, d_ff=14336,
+               max_seq=64, rope_base=500000.0, eps=1e-5)
+    m = synth(lib, cfg, seed=1234)
+    ids = [17, 128000, 42, 9999]
+    ologits, _ = orc_decode(orc, m, ids)
+    glogits, _ = gpu_decode(lib, m, ids)
+    assert bits_equal(glogits, ologits)
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_generate_matches_stepwise_argmax(lib):
+    m = synth(lib, TINY, seed=77)
+    kv1 = lib.q_llama_kv_create(C.byref(m))
+    ids = (C.c_int * 30)()
+    assert lib.q_llama_generate(C.byref(m), C.byref(kv1), 5, 30, ids) == 0
+    assert kv1.len == 30
+    kv2 = lib.q_llama_kv_create(C.byref(m))
+    tok, seq = 5, []
+    for _ in range(30):
+        tok = lib.q_llama_decode_step_argmax(C.byref(m), C.byref(kv2), tok, None)
+        seq.append(tok)
+    llmq.check(lib)
+    assert list(ids) == seq
+    lib.llama_kv_free(C.byref(kv1))
+    lib.llama_kv_free(C.byref(kv2))
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_kv_sync_host_matches_oracle_cache(lib, orc):
+    m = synth(lib, TINY, seed=3)
+    ids = [1, 2, 3, 4, 5, 6, 7]
+    _, okv = orc_decode(orc, m, ids, kv=orc.orc_kv_create(C.byref(m)))
+    gkv = lib.q_llama_kv_create(C.byref(m))
+    gpu_decode(lib, m, ids, kv=gkv)
+    assert lib.q_llama_kv_sync_host(C.byref(m), C.byref(gkv)) == 0
+    n = len(ids) * gkv.kv_dim
+    for l in range(m.n_layers):
+        for a, b in ((gkv.k, okv.k), (gkv.v, okv.v)):
+            x = np.ctypeslib.as_array(a[l], shape=(n,))
+            y = np.ctypeslib.as_array(b[l], shape=(n,))
+            assert bits_equal(x, y)
+    orc.orc_kv_free(C.byref(okv))
+    lib.llama_kv_free(C.byref(gkv))
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_continues_a_cache_filled_by_the_reference(lib, ref):
+    """A LlamaKV whose first positions were decoded by the reference CPU code is
+    adopted by the GPU path, which continues bit-identically."""
+    m = load_gpu(lib, os.path.join(GOLDEN, "mini.llmq"))
+    d = np.load(os.path.join(GOLDEN, "mini.npz"))
+    kv = ref.q_llama_kv_create(C.byref(m))
+    row = np.zeros((1, m.vocab), np.float32)
+    t = llmq.host_tensor(row)
+    fed = d["fed"]
+    for tok in fed[:20]:
+        ref.q_llama_decode_step(C.byref(m), C.byref(kv), int(tok), C.byref(t))
+    glogits, _ = gpu_decode(lib, m, fed[20:120], kv=kv)
+    assert glogits.argmax(axis=1).tolist() == d["argmax"][20:120].tolist()
+    assert bits_equal(glogits[100 - 20], d["logits"][list(d["save_steps"]).index(100)])
+    ref.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_bad_token_and_full_cache_are_errors(lib):
+    m = synth(lib, dict(TINY, max_seq=4), seed=5)
+    kv = lib.q_llama_kv_create(C.byref(m))
+    row = np.zeros((1, m.vocab), np.float32)
+    t = llmq.host_tensor(row)
+    lib.q_llama_clear_error()
+    lib.q_llama_decode_step(C.byref(m), C.byref(kv), m.vocab, C.byref(t))
+    assert lib.q_llama_last_error() == 1 and kv.len == 0
+    lib.q_llama_clear_error()
+    for i in range(4):
+        lib.q_llama_decode_step(C.byref(m), C.byref(kv), i, C.byref(t))
+        llmq.check(lib)
+    lib.q_llama_decode_step(C.byref(m), C.byref(kv), 0, C.byref(t))
+    assert lib.q_llama_last_error() == 1 and kv.len == 4
+    lib.q_llama_clear_error()
+    lib.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(m))
+
+
+# -------------------------------------------------------------------- expf
+def test_device_expf_equals_host_libm_on_every_float(lib, orc):
+    """The device expf used by softmax and SiLU returns the host C library's
+    expf bit for bit on all 2^32 inputs (NaN inputs: both NaN)."""
+    chunk = 1 << 26
+    dev = np.empty(chunk, np.float32)
+    host = np.empty(chunk, np.float32)
+    mismatches = 0
+    for first in range(0, 1 << 32, chunk):
+        x = np.arange(first, first + chunk, dtype=np.uint64).astype(np.uint32).view(np.float32)
+        assert lib.llmq_expf_device(fp(x), fp(dev), chunk) == 0
+        orc.orc_expf_bits(first, chunk, fp(host))
+        same = dev.view(np.uint32) == host.view(np.uint32)
+        same |= np.isnan(dev) & np.isnan(host)
+        mismatches += int((~same).sum())
+    assert mismatches == 0
