@@ -1,0 +1,397 @@
+"""Benchmark: int8 (W8A8) LLaMA-family KV-cache decode on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 8b|tiny]
+
+Default workload: LLaMA-3-8B-shaped int8 model
+(dm 4096, 32 layers, 32/8 heads, hd 128, dff 14336, vocab 128256, rope 5e5),
+synthetic seeded N(0, 0.02) weights quantised per column, batch 1, a 512-id
+uniform-random prompt, then greedy decode.  A step is one decoded token.
+
+Our arm prints one JSON line with
+  value     tok/s of K greedy steps chained on the GPU (inputs resident in HBM,
+            one CUDA graph per step, timed with CUDA events on the model stream)
+  e2e       tok/s of the same K positions through q_llama_decode_step (the
+            reference API): token in from the host, f32 logits back to the host,
+            host argmax; wall clock
+  roofline  the int8 GEMV kernel (k_gemv, the dominant kernel): algorithmic bytes
+            / CUDA-event time per launch, over the step's launch mix
+  cpu_baseline  the reference's own q_llama_decode_step (oracle/_ref, all host
+            cores) on the same model and KV cache, on a bounded sample of steps
+`--impl reference` times the reference's CPU decode alone on the same config.
+With N > 1 every rank runs an independent replica (the 8B model fits one GPU;
+tensor parallelism is not used for this config): weak scaling, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llm-project_b200"))
+import llmq  # noqa: E402
+
+WORKLOADS = {
+    "8b": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=32, n_heads=32, n_kv=8, head_dim=128, d_ff=14336,
+                        rope_base=500000.0, eps=1e-5), prompt=512, gen=256,
+               name="llama3-8b-shaped int8 W8A8, batch 1: 512-id prompt then greedy decode"),
+    "tiny": dict(cfg=dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768,
+                          rope_base=10000.0, eps=1e-5), prompt=16, gen=240,
+                 name="tiny llama int8 W8A8, batch 1: 16-id prompt then greedy decode"),
+}
+SEED_WEIGHTS, SEED_PROMPT = 1234, 5678
+METRIC = "int8-weight decode tok/s (bs1)"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons with NVML every ~20 ms."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, device_index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # pragma: no cover - reported in the JSON
+            self.error = str(e)
+
+    def _run(self):
+        nv = self._nv
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = get_reasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.02)
+
+    def __enter__(self):
+        if self._h is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._h is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                    "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# -------------------------------------------------------------- model setup
+def make_model(lib, cfg: dict, max_seq: int):
+    c = llmq.config(max_seq=max_seq, **cfg)
+    m = llmq.QLlamaModel()
+    t0 = time.time()
+    rc = lib.llmq_synth_model(C.byref(c), SEED_WEIGHTS, 0.02, 0, C.byref(m))
+    if rc != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    log(f"synthetic model built in {time.time() - t0:.1f}s")
+    return m
+
+
+def weight_bytes(cfg: dict) -> int:
+    dm, L, qd = cfg["d_model"], cfg["n_layers"], cfg["n_heads"] * cfg["head_dim"]
+    kvd, dff, V = cfg["n_kv"] * cfg["head_dim"], cfg["d_ff"], cfg["vocab"]
+    per_layer = dm * (qd + 2 * kvd) + qd * dm + 2 * dm * dff + dff * dm
+    return L * per_layer + dm * V
+
+
+def prompt_ids(cfg, n):
+    return np.random.default_rng(SEED_PROMPT).integers(0, cfg["vocab"], size=n).astype(np.int32)
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args, rank, world):
+    lib = llmq.load()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if lib.q_llama_set_device(local) != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    wl = WORKLOADS[args.workload]
+    cfg = wl["cfg"]
+    P, W, K = wl["prompt"], args.warmup, args.steps
+    max_seq = max(P + wl["gen"], P + W + K)
+    if world > 1:
+        os.environ.setdefault("LLMQ_THREADS", str(max(1, (os.cpu_count() or 1) // world)))
+    m = make_model(lib, cfg, max_seq)
+    t0 = time.time()
+    if lib.q_llama_model_upload(C.byref(m)) != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    log(f"uploaded in {time.time() - t0:.1f}s")
+    kv = lib.q_llama_kv_create(C.byref(m))
+    llmq.check(lib)
+
+    # prompt, token by token through the reference-facing call (untimed)
+    prompt = prompt_ids(cfg, P)
+    nxt = -1
+    for t in prompt:
+        nxt = lib.q_llama_decode_step_argmax(C.byref(m), C.byref(kv), int(t), None)
+    llmq.check(lib)
+    base_len = kv.len
+
+    # warm-up: W greedy steps chained on the device
+    ids = (C.c_int * max(W, K, 1))()
+    if W:
+        if lib.q_llama_generate(C.byref(m), C.byref(kv), nxt, W, ids) != 0:
+            llmq.check(lib)
+        nxt = ids[W - 1]
+    start_len, start_tok = kv.len, nxt
+
+    # ---- timed region: K greedy steps, device-chained
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        if lib.q_llama_generate(C.byref(m), C.byref(kv), start_tok, K, ids) != 0:
+            llmq.check(lib)
+        ms = float(lib.q_llama_last_step_ms())
+    gen_ids = [ids[i] for i in range(K)]
+    if dist is not None:
+        import torch
+        t = torch.tensor([ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    value = world * K / (ms / 1e3)
+
+    # ---- e2e: the same K positions again through q_llama_decode_step
+    kv.len = start_len
+    logits = np.zeros((1, cfg["vocab"]), np.float32)
+    lt = llmq.host_tensor(logits)
+    tok, e2e_ids = start_tok, []
+    t0 = time.perf_counter()
+    for _ in range(K):
+        lib.q_llama_decode_step(C.byref(m), C.byref(kv), tok, C.byref(lt))
+        tok = int(np.argmax(logits[0]))
+        e2e_ids.append(tok)
+    e2e_s = time.perf_counter() - t0
+    llmq.check(lib)
+    e2e_value = world * K / e2e_s
+    if dist is not None:
+        import torch
+        t = torch.tensor([e2e_s], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_value = world * K / float(t.item())
+
+    # ---- roofline of the GEMV kernel: per-kind CUDA-event timings
+    kinds = [(0, cfg["n_layers"]), (1, cfg["n_layers"]), (2, cfg["n_layers"]), (3, cfg["n_layers"]), (4, 1)]
+    g_bytes, g_ms, per_kind = 0.0, 0.0, {}
+    for which, count in kinds:
+        msl, by = C.c_float(), C.c_double()
+        if lib.llmq_bench_gemv(C.byref(m), which, 0, 20, C.byref(msl), C.byref(by)) != 0:
+            llmq.check(lib)
+        g_bytes += count * by.value
+        g_ms += count * msl.value
+        per_kind[["qkv", "wo", "w13", "w2", "lm_head"][which]] = {
+            "ms": round(msl.value, 5), "GBps": round(by.value / msl.value / 1e6, 1)}
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    achieved = g_bytes / (g_ms / 1e3) / 1e9
+    step_bytes = weight_bytes(cfg)
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": profiled_traffic(),
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
+                "kernel": "k_gemv (int8 W8A8 GEMV, all five per-step shapes)",
+                "per_kind": per_kind,
+                "step_bytes": step_bytes,
+                "step_frac": round(step_bytes / (ms / K / 1e3) / 1e9 / hbm_peak, 4)}
+
+    # ---- CPU baseline: the reference's decode on the same model and cache
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        kv.len = start_len
+        cpu = cpu_baseline(lib, m, kv, start_tok, gen_ids)
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": wl["name"], "model": f"{args.workload}-shaped synthetic, seed {SEED_WEIGHTS}",
+                   "global_batch": world, "batch_per_gpu": 1, "kv_len_start": start_len,
+                   "kv_len_end": start_len + K, "prompt": P,
+                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                   "l2": f"inputs larger than L2: {step_bytes / 1e9:.2f} GB of int8 weights streamed per step"},
+        "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 16 + 4 * cfg["vocab"],
+                "api": "q_llama_decode_step (host token, host f32 logits, host argmax)",
+                "same_tokens_as_value_run": e2e_ids == gen_ids},
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+        "gpu_launches": K * int(lib.llmq_kernels_per_step(C.byref(m))),
+        "clocks": clk.summary(),
+    }
+    lib.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(m))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def profiled_traffic():
+    """DRAM bytes per k_gemv launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "k_gemv_8b_decode.md")
+    try:
+        for ln in open(p):
+            if ln.startswith("traffic_bytes_per_launch:"):
+                return float(ln.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
+def cpu_baseline(lib, m, kv, start_tok, gen_ids):
+    """Times the reference's q_llama_decode_step on the host cores, continuing
+    from the GPU-built cache (copied to the host arrays): a bounded sample of the
+    same decode positions.  Also checks its logits equal ours bit for bit."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    cores = os.cpu_count() or 1
+    os.environ["TF_THREADS"] = str(min(cores, 64))
+    ref = oracle.load_reference()
+    kind = "reference"
+    if ref is None:
+        return None
+    if lib.q_llama_kv_sync_host(C.byref(m), C.byref(kv)) != 0:
+        llmq.check(lib)
+    vocab = m.vocab
+    ref_logits = np.zeros((1, vocab), np.float32)
+    rt = llmq.host_tensor(ref_logits)
+    tok, n, t_total, match = start_tok, 0, 0.0, True
+    budget = 15.0
+    while n < len(gen_ids) and n < 64 and t_total < budget:
+        t0 = time.perf_counter()
+        ref.q_llama_decode_step(C.byref(m), C.byref(kv), tok, C.byref(rt))
+        t_total += time.perf_counter() - t0
+        tok = int(np.argmax(ref_logits[0]))
+        match &= tok == gen_ids[n]
+        n += 1
+    return {"value": round(n / t_total, 4), "unit": "tok/s", "cores": min(cores, 64), "kind": kind,
+            "sample": f"{n} decode steps of the same model at positions {kv.len - n}..{kv.len - 1}, "
+                      f"continuing the GPU-built KV cache copied to host memory",
+            "greedy_ids_match_gpu": bool(match)}
+
+
+# ----------------------------------------------------------- reference arm
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    cores = os.cpu_count() or 1
+    os.environ["TF_THREADS"] = str(min(cores, 64))
+    ref = oracle.load_reference()
+    wl = WORKLOADS[args.workload]
+    cfg = wl["cfg"]
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built from the reference "
+                                                            "sources (make -C oracle)"}), flush=True)
+        return
+    lib = llmq.load()  # host-side synthetic-input generator only
+    P, W, K = wl["prompt"], args.warmup, args.steps
+    max_seq = max(P + wl["gen"], P + W + K)
+    m = make_model(lib, cfg, max_seq)
+    kv = ref.q_llama_kv_create(C.byref(m))
+    # The prompt's cache rows are filled with seeded values of realistic scale
+    # rather than decoded (decoding 512 ids on the CPU takes minutes); the timed
+    # steps then attend over the same number of positions as our arm.
+    rng = np.random.default_rng(SEED_PROMPT)
+    kvd = kv.kv_dim
+    for l in range(kv.n_layers):
+        for arr in (kv.k, kv.v):
+            a = np.ctypeslib.as_array(arr[l], shape=(max_seq * kvd,))
+            a[: P * kvd] = rng.standard_normal(P * kvd).astype(np.float32)
+    kv.len = P
+    logits = np.zeros((1, cfg["vocab"]), np.float32)
+    lt = llmq.host_tensor(logits)
+    tok = int(prompt_ids(cfg, P)[-1])
+    for _ in range(W):
+        ref.q_llama_decode_step(C.byref(m), C.byref(kv), tok, C.byref(lt))
+        tok = int(np.argmax(logits[0]))
+    t0 = time.perf_counter()
+    for _ in range(K):
+        ref.q_llama_decode_step(C.byref(m), C.byref(kv), tok, C.byref(lt))
+        tok = int(np.argmax(logits[0]))
+    dt = time.perf_counter() - t0
+    value = K / dt
+    line = {"metric": METRIC, "value": round(value, 4), "unit": "tok/s", "n_gpus": world, "steps": K,
+            "warmup": W, "ms_per_step": round(dt / K * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
+            "config": {"workload": wl["name"], "model": f"{args.workload}-shaped synthetic, seed {SEED_WEIGHTS}",
+                       "global_batch": 1, "kv_len_start": P + W, "kv_len_end": P + W + K,
+                       "parallelism": f"reference CPU thread pool, TF_THREADS={min(cores, 64)}"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": min(cores, 64),
+                             "kind": "reference",
+                             "sample": f"{K} decode steps at positions {P + W}..{P + W + K - 1} "
+                                       f"(prompt cache rows seeded, not decoded)"},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    ref.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(m))
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=240)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8b")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    try:
+        if args.impl == "reference":
+            run_reference(args, rank, world)
+        else:
+            run_ours(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

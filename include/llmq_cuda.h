@@ -118,8 +118,7 @@ void quantize_int8_percol(const float *w, int rows, int cols, signed char *q, fl
 /* Replaces quant.c:64-68 (quant.h:16).  w[i,j] = q[i,j] * scale[j], on the GPU. */
 void dequantize_int8_percol(const signed char *q, const float *scale, int rows, int cols, float *w);
 
-/* Replace quant.c:70-85 (quant.h:28-30).  Host allocation, as in the reference.
- * qtensor_free also drops any device copy of the weight made by qmatmul. */
+/* Replace quant.c:70-85 (quant.h:28-30).  Host allocation, as in the reference. */
 QTensor qtensor_create(int rows, int cols);
 void qtensor_free(QTensor *t);
 void qtensor_quantize(QTensor *t, const float *w);
@@ -127,8 +126,9 @@ void qtensor_quantize(QTensor *t, const float *w);
 /* Replaces quant.c:95-120 (quant.h:33).  C(M,N) = W8A8 product of A(M,K) with W:
  * each row of A is quantised to int8 with its own absmax scale, multiplied
  * exactly in int32 against W's codes, and rescaled as a_scale*w_scale[j]*acc.
- * A and C are host tensors.  W is copied to the GPU (and repacked) on first use
- * and cached, keyed by W->q; qtensor_free releases the copy. */
+ * A, W and C are host memory, read and written on every call exactly like the
+ * reference: each call copies A and W to the GPU (W is tiled there) and C back,
+ * so a QTensor rewritten in place between calls is always seen. */
 void qmatmul(const Tensor *A, const QTensor *W, Tensor *C);
 
 /* ========================================================================= */
@@ -221,6 +221,11 @@ void llmq_synth_qtensor(QTensor *t, uint64_t seed);
 /* Upload / release the device copy of a model explicitly (both are otherwise
  * implicit).  Returns 0 or an error code. */
 int q_llama_model_upload(const QLlamaModel *m);
+
+/* Selects the CUDA device that later uploads, caches and standalone calls on
+ * this thread use (one process per GPU: pass the local rank).  A model keeps
+ * the device it was uploaded to.  Returns 0 or an error code. */
+int q_llama_set_device(int device);
 
 /* Greedy generation chained on the GPU: feeds `token` at position kv->len, then
  * keeps feeding the argmax of each step, for n steps in total (one CUDA graph

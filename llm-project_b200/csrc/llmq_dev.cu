@@ -44,12 +44,6 @@ struct Mat {
   size_t bytes() const { return (size_t)Kpad * Npad; }
 };
 
-struct WeightEntry {
-  Mat mat;
-  int rows, cols;
-  const float *scale;
-};
-
 struct DevCtx {
   bool ready = false;
   int device = -1;
@@ -62,7 +56,9 @@ struct DevCtx {
   size_t dA_n = 0, dC_n = 0;
   int *acc = nullptr, *cnt = nullptr, *err = nullptr;
   size_t acc_n = 0, cnt_n = 0;
-  std::unordered_map<const void *, WeightEntry> weights;
+  uint8_t *wraw = nullptr, *wtile = nullptr;
+  float *wscale = nullptr;
+  size_t wraw_n = 0, wtile_n = 0, wscale_n = 0;
 };
 
 DevCtx g_ctx[kMaxDevices];
@@ -793,40 +789,24 @@ int llmqd_dequantize(const signed char *q, const float *scale, int rows, int col
   return ok;
 }
 
-void llmqd_forget_weight(const void *q) {
-  std::lock_guard<std::recursive_mutex> lk(g_mu);
-  for (DevCtx &c : g_ctx) {
-    if (!c.ready) continue;
-    auto it = c.weights.find(q);
-    if (it == c.weights.end()) continue;
-    cudaSetDevice(c.device);
-    free_mat(it->second.mat);
-    c.weights.erase(it);
-  }
-}
-
 int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
+  // The reference reads W from host memory on every call, and callers may
+  // rewrite a QTensor in place, so W is uploaded and tiled on every call
+  // (into grow-only scratch); nothing is cached across calls.
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   if (M == 0 || W->cols == 0) return 1;
   DevCtx *c = get_ctx();
   if (!c) return 0;
-  auto it = c->weights.find(W->q);
-  if (it != c->weights.end() &&
-      (it->second.rows != W->rows || it->second.cols != W->cols || it->second.scale != W->scale)) {
-    free_mat(it->second.mat);
-    c->weights.erase(it);
-    it = c->weights.end();
-  }
-  if (it == c->weights.end()) {
-    WeightEntry e{};
-    e.rows = W->rows;
-    e.cols = W->cols;
-    e.scale = W->scale;
-    if (!build_plain(e.mat, *W)) return 0;
-    it = c->weights.emplace(W->q, e).first;
-  }
-  const Mat &m = it->second.mat;
   const int K = W->rows, N = W->cols;
+  Mat m;
+  m.K = K;
+  m.N = N;
+  m.NT = 256;
+  m.KT = kKT;
+  m.Kpad = std::max(roundup(K, kKT), kKT);
+  m.Npad = std::max(roundup(N, m.NT), m.NT);
+  m.n_slabs = m.Npad / m.NT;
+  m.n_ktiles = m.Kpad / kKT;
   const bool many = M > 1;
   GemvPlan plan;
   int rows_per = many ? 8 : 1;
@@ -837,10 +817,26 @@ int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
     rows_per /= 2;
   }
   if (!ensure(&c->dA, &c->dA_n, (size_t)M * K, false) || !ensure(&c->dC, &c->dC_n, (size_t)M * N, false) ||
-      !ensure(&c->acc, &c->acc_n, (size_t)8 * m.Npad, true) || !ensure(&c->cnt, &c->cnt_n, (size_t)m.n_slabs, true))
+      !ensure(&c->acc, &c->acc_n, (size_t)8 * m.Npad, true) || !ensure(&c->cnt, &c->cnt_n, (size_t)m.n_slabs, true) ||
+      !ensure(&c->wraw, &c->wraw_n, (size_t)K * N, false) || !ensure(&c->wtile, &c->wtile_n, m.bytes(), false) ||
+      !ensure(&c->wscale, &c->wscale_n, (size_t)m.Npad, false))
     return 0;
+  m.w = c->wtile;
+  m.ws = c->wscale;
   cudaStream_t st = c->stream;
-  if (K > 0) CK(cudaMemcpyAsync(c->dA, A, (size_t)M * K * sizeof(float), cudaMemcpyHostToDevice, st));
+  if (K > 0) {
+    CK(cudaMemcpyAsync(c->wraw, W->q, (size_t)K * N, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(c->dA, A, (size_t)M * K * sizeof(float), cudaMemcpyHostToDevice, st));
+  }
+  CK(cudaMemcpyAsync(c->wscale, W->scale, (size_t)N * sizeof(float), cudaMemcpyHostToDevice, st));
+  CK(cudaMemsetAsync(c->wscale + N, 0, (size_t)(m.Npad - N) * sizeof(float), st));
+  {
+    const long long chunks = (long long)m.Kpad / 16 * m.Npad;
+    const int blocks = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148LL * 64));
+    k_repack_plain<<<std::max(blocks, 1), 256, 0, st>>>(reinterpret_cast<const int8_t *>(c->wraw), K, N, m.Kpad,
+                                                         m.Npad, m.NT, m.KT, c->wtile);
+    CK(cudaGetLastError());
+  }
   for (int r0 = 0; r0 < M; r0 += rows_per) {
     GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
     a.rows = std::min(rows_per, M - r0);
@@ -1042,3 +1038,12 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
 LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) { return 5 * m->n_layers + 2; }
 
 }  // extern "C"
+
+extern "C" LLMQ_API int q_llama_set_device(int device) {
+  const cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_NO_DEVICE, "q_llama_set_device(%d): %s", device, cudaGetErrorString(e));
+    return LLMQ_ERR_NO_DEVICE;
+  }
+  return LLMQ_OK;
+}

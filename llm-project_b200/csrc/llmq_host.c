@@ -95,7 +95,6 @@ LLMQ_API QTensor qtensor_create(int rows, int cols) {
 }
 
 LLMQ_API void qtensor_free(QTensor *t) {
-  if (t->q) llmqd_forget_weight(t->q);
   free(t->q);
   free(t->scale);
   t->q = NULL;
@@ -103,7 +102,6 @@ LLMQ_API void qtensor_free(QTensor *t) {
 }
 
 LLMQ_API void qtensor_quantize(QTensor *t, const float *w) {
-  llmqd_forget_weight(t->q); /* contents change: drop any device copy */
   quantize_int8_percol(w, t->rows, t->cols, t->q, t->scale);
 }
 
@@ -159,7 +157,6 @@ static QLlamaModel model_alloc(const int32_t *c, const float *f) {
 }
 
 static void qt_release(QTensor *t) {
-  if (t->q) llmqd_forget_weight(t->q);
   free(t->q);
   free(t->scale);
   t->q = NULL;

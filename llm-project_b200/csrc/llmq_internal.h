@@ -27,7 +27,6 @@ LLMQ_HIDDEN void llmq_rope_tables(float base, int head_dim, int max_seq, float *
 LLMQ_HIDDEN int llmqd_quantize(const float *w, int rows, int cols, signed char *q, float *scale);
 LLMQ_HIDDEN int llmqd_dequantize(const signed char *q, const float *scale, int rows, int cols, float *w);
 LLMQ_HIDDEN int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C);
-LLMQ_HIDDEN void llmqd_forget_weight(const void *q);
 
 LLMQ_HIDDEN int llmqd_model_upload(const QLlamaModel *m);
 LLMQ_HIDDEN void llmqd_model_release(const QLlamaModel *m);

@@ -690,6 +690,33 @@ __global__ void k_repack(RepackSrc src, const int *colsrc, int K, int Kpad, int 
   }
 }
 
+// Tiles a plain row-major (K, N) matrix: physical column p is column p
+// (p >= N: zero padding).  Same chunk order as k_repack.
+__global__ void k_repack_plain(const int8_t *src, int K, int N, int Kpad, int Npad, int NT, int KT, uint8_t *dst) {
+  const long long chunks = (long long)Kpad / 16 * Npad;
+  const int n_ktiles = Kpad / KT;
+  const int per_tile = (KT / 16) * NT;
+  for (long long ci = blockIdx.x * (long long)blockDim.x + threadIdx.x; ci < chunks;
+       ci += (long long)gridDim.x * blockDim.x) {
+    const long long tile = ci / per_tile;
+    const int within = static_cast<int>(ci - tile * per_tile);
+    const int c = within / NT, nn = within % NT;
+    const long long slab = tile / n_ktiles;
+    const int kt = static_cast<int>(tile - slab * n_ktiles);
+    const int p = static_cast<int>(slab) * NT + nn;
+    const int k0 = kt * KT + c * 16;
+    uint8_t bytes[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) {
+      const int k = k0 + b;
+      bytes[b] = (p < N && k < K) ? static_cast<uint8_t>(src[(size_t)k * N + p]) : 0;
+    }
+    uint4 o;
+    memcpy(&o, bytes, 16);
+    reinterpret_cast<uint4 *>(dst)[ci] = o;
+  }
+}
+
 // expf of a batch (tests compare this against the host libm over all inputs).
 __global__ void k_expf_batch(const float *x, float *y, long long n) {
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)

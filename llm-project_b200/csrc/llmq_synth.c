@@ -107,8 +107,11 @@ static void *qjob_run(void *arg) {
   return NULL;
 }
 
+/* LLMQ_THREADS caps the generator's threads (one process per GPU shares the
+ * host cores); default: every online core. */
 static int n_threads(void) {
-  long n = sysconf(_SC_NPROCESSORS_ONLN);
+  const char *env = getenv("LLMQ_THREADS");
+  long n = (env && atoi(env) > 0) ? atoi(env) : sysconf(_SC_NPROCESSORS_ONLN);
   if (n < 1) n = 1;
   if (n > 128) n = 128;
   return (int)n;
@@ -228,5 +231,4 @@ LLMQ_API void llmq_synth_qtensor(QTensor *t, uint64_t seed) {
     const double u = (double)(splitmix64(skey + (uint64_t)j) >> 11) * 0x1p-53;
     t->scale[j] = (float)(1e-3 + 9e-3 * u);
   }
-  llmqd_forget_weight(t->q);
 }

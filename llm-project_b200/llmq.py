@@ -101,6 +101,7 @@ SIGNATURES = {
     "llmq_bench_gemv": (C.c_int, [C.POINTER(QLlamaModel), C.c_int, C.c_int, C.c_int, c_float_p,
                                   C.POINTER(C.c_double)]),
     "llmq_kernels_per_step": (C.c_int, [C.POINTER(QLlamaModel)]),
+    "q_llama_set_device": (C.c_int, [C.c_int]),
 }
 
 _lib = None
