@@ -43,6 +43,9 @@ WORKLOADS = {
     "8b": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=32, n_heads=32, n_kv=8, head_dim=128, d_ff=14336,
                         rope_base=500000.0, eps=1e-5), prompt=512, gen=256,
                name="llama3-8b-shaped int8 W8A8, batch 1: 512-id prompt then greedy decode"),
+    "8b2": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128, d_ff=14336,
+                         rope_base=500000.0, eps=1e-5), prompt=512, gen=256,
+                name="llama3-8b layer shapes, 2 layers (profiling case), batch 1"),
     "tiny": dict(cfg=dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768,
                           rope_base=10000.0, eps=1e-5), prompt=16, gen=240,
                  name="tiny llama int8 W8A8, batch 1: 16-id prompt then greedy decode"),
@@ -139,7 +142,7 @@ def run_ours(args, rank, world):
         raise RuntimeError(lib.q_llama_last_error_message().decode())
     wl = WORKLOADS[args.workload]
     cfg = wl["cfg"]
-    P, W, K = wl["prompt"], args.warmup, args.steps
+    P, W, K = args.prompt or wl["prompt"], args.warmup, args.steps
     max_seq = max(P + wl["gen"], P + W + K)
     if world > 1:
         os.environ.setdefault("LLMQ_THREADS", str(max(1, (os.cpu_count() or 1) // world)))
@@ -204,6 +207,17 @@ def run_ours(args, rank, world):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_value = world * K / float(t.item())
 
+    # ---- one step replayed kernel by kernel (no graph, no overlap): where the time goes
+    nk = int(lib.llmq_kernels_per_step(C.byref(m)))
+    prof = np.zeros(nk, np.float32)
+    kv.len = start_len
+    if lib.llmq_step_profile(C.byref(m), C.byref(kv), start_tok, prof.ctypes.data_as(llmq.c_float_p), nk) != 0:
+        llmq.check(lib)
+    names = ["qkv", "attn_scores", "attn_pv", "wo", "w13", "w2"]
+    step_profile = {n: round(float(prof[i:nk - 2:len(names)].sum()), 4) for i, n in enumerate(names)}
+    step_profile.update(lm_head=round(float(prof[nk - 2]), 4), finish=round(float(prof[nk - 1]), 4),
+                        total=round(float(prof.sum()), 4), unit="ms per step, kernels serialised")
+
     # ---- roofline of the GEMV kernel: per-kind CUDA-event timings
     kinds = [(0, cfg["n_layers"]), (1, cfg["n_layers"]), (2, cfg["n_layers"]), (3, cfg["n_layers"]), (4, 1)]
     g_bytes, g_ms, per_kind = 0.0, 0.0, {}
@@ -215,6 +229,10 @@ def run_ours(args, rank, world):
         g_ms += count * msl.value
         per_kind[["qkv", "wo", "w13", "w2", "lm_head"][which]] = {
             "ms": round(msl.value, 5), "GBps": round(by.value / msl.value / 1e6, 1)}
+    msl, by = C.c_float(), C.c_double()
+    if lib.llmq_bench_gemv(C.byref(m), 5, 0, 20, C.byref(msl), C.byref(by)) != 0:
+        llmq.check(lib)
+    per_kind["attention"] = {"ms": round(msl.value, 5), "GBps": round(by.value / msl.value / 1e6, 1)}
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -252,6 +270,7 @@ def run_ours(args, rank, world):
                 "same_tokens_as_value_run": e2e_ids == gen_ids},
         "roofline": roofline,
         "cpu_baseline": cpu,
+        "step_profile": step_profile,
         "gpu_launches": K * int(lib.llmq_kernels_per_step(C.byref(m))),
         "clocks": clk.summary(),
     }
@@ -371,6 +390,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (profiling runs)")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -244,17 +244,25 @@ float q_llama_last_step_ms(void);
  * (bit-identical to the host C library's expf).  Returns 0 or an error code. */
 int llmq_expf_device(const float *x, float *y, long long n);
 
-/* Times `iters` back-to-back launches of one GEMV of an uploaded model
- * (which: 0 fused QKV, 1 Wo, 2 fused W1|W3, 3 W2, 4 lm-head; `layer` selects
- * the block) with CUDA events on the model's stream.  *ms_per_launch receives
- * the mean launch time and *bytes_per_launch the algorithmic bytes of one
- * launch (int8 weights + f32 scales + f32 input + f32 output).
- * Returns 0 or an error code. */
+/* Times `iters` back-to-back launches of one kernel of an uploaded model
+ * (which: 0 fused QKV, 1 Wo, 2 fused W1|W3, 3 W2, 4 lm-head GEMV, 5 attention
+ * over the first KV cache at its current position; `layer` selects the block)
+ * with CUDA events on the model's stream.  *ms_per_launch receives the mean
+ * launch time and *bytes_per_launch the algorithmic bytes of one launch (GEMV:
+ * int8 weights + f32 scales + f32 input + f32 output; attention: the K and V
+ * rows read plus q and the output).  Returns 0 or an error code. */
 int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int iters, float *ms_per_launch,
                     double *bytes_per_launch);
 
 /* Kernels launched by one decode step (5 per layer + 2). */
 int llmq_kernels_per_step(const QLlamaModel *m);
+
+/* Runs one decode step of `token` at kv->len outside the CUDA graph, kernel by
+ * kernel with CUDA events between the launches, writes each kernel's time in
+ * milliseconds to ms[0 .. min(max_n, llmq_kernels_per_step(m))) and advances
+ * kv->len like a decode step.  For attributing step time to kernels; the
+ * kernels do not overlap here.  Returns 0 or an error code. */
+int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, int max_n);
 
 #ifdef __cplusplus
 }

@@ -7,6 +7,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -30,17 +31,23 @@ extern "C" const uint32_t llmq_expf_exceptions_count;
 
 namespace {
 
-constexpr int kKT = 64;         // k rows per tile
 constexpr int kMaxDevices = 64;
 
 size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 int roundup(int v, int m) { return (v + m - 1) / m * m; }
 
+// Tile depth: 32 KB tiles (KT 128) once a matrix spans at least 16 of them per
+// SM, else 16 KB tiles (KT 64) so the contiguous split stays balanced.
+int choose_kt(int K, int Npad) {
+  const double bytes = (double)std::max(roundup(K, 64), 64) * Npad;
+  return bytes >= 148.0 * 16 * 32768 ? 128 : 64;
+}
+
 // ------------------------------------------------------------------ context
 struct Mat {
   uint8_t *w = nullptr;
   float *ws = nullptr;
-  int K = 0, Kpad = 0, N = 0, Npad = 0, NT = 0, KT = kKT, n_slabs = 0, n_ktiles = 0;
+  int K = 0, Kpad = 0, N = 0, Npad = 0, NT = 0, KT = 64, n_slabs = 0, n_ktiles = 0;
   size_t bytes() const { return (size_t)Kpad * Npad; }
 };
 
@@ -63,6 +70,15 @@ struct DevCtx {
 
 DevCtx g_ctx[kMaxDevices];
 std::recursive_mutex g_mu;
+// Programmatic dependent launch between the kernels of a step (LLMQ_NO_PDL=1
+// turns it off, for measurements).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = getenv("LLMQ_NO_PDL");
+    return !(e && e[0] == '1');
+  }();
+  return on;
+}
 
 void free_mat(Mat &m) {
   cudaFree(m.w);
@@ -72,7 +88,9 @@ void free_mat(Mat &m) {
 
 template <int PRO, int EPI, int MR>
 cudaError_t set_gemv_attr(int smem) {
-  return cudaFuncSetAttribute(k_gemv<PRO, EPI, MR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = cudaFuncSetAttribute(k_gemv<PRO, EPI, MR, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(k_gemv<PRO, EPI, MR, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
 }
 
 int init_expf_table(DevCtx &c) {
@@ -132,7 +150,8 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_SWIGLU, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_LOGITS, 1>(sm);
   ea = ea != cudaSuccess ? ea
-                         : cudaFuncSetAttribute(k_attention, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+                         : cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  ea = ea != cudaSuccess ? ea : cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   if (ea != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
     return nullptr;
@@ -168,11 +187,11 @@ int build_mat(Mat &out, int K, int Nlog, int NT, const std::vector<int> &colsrc,
   out.K = K;
   out.N = Nlog;
   out.NT = NT;
-  out.KT = kKT;
-  out.Kpad = std::max(roundup(K, kKT), kKT);
+  out.KT = choose_kt(K, (int)colsrc.size());
+  out.Kpad = std::max(roundup(K, out.KT), out.KT);
   out.Npad = static_cast<int>(colsrc.size());
   out.n_slabs = out.Npad / NT;
-  out.n_ktiles = out.Kpad / kKT;
+  out.n_ktiles = out.Kpad / out.KT;
   CK(cudaMalloc(&out.w, std::max<size_t>(out.bytes(), 16)));
   CK(cudaMalloc(&out.ws, (size_t)out.Npad * sizeof(float)));
   RepackSrc rs{};
@@ -190,7 +209,7 @@ int build_mat(Mat &out, int K, int Nlog, int NT, const std::vector<int> &colsrc,
   CK(cudaMemcpy(dcol, colsrc.data(), colsrc.size() * sizeof(int), cudaMemcpyHostToDevice));
   const long long chunks = (long long)out.Kpad / 16 * out.Npad;
   const int blocks = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148LL * 64));
-  k_repack<<<std::max(blocks, 1), 256>>>(rs, dcol, K, out.Kpad, out.Npad, NT, kKT, out.w);
+  k_repack<<<std::max(blocks, 1), 256>>>(rs, dcol, K, out.Kpad, out.Npad, NT, out.KT, out.w);
   CK(cudaGetLastError());
   std::vector<float> ws(out.Npad, 0.0f);
   for (int p = 0; p < out.Npad; ++p) {
@@ -217,27 +236,31 @@ int build_plain(Mat &out, const QTensor &W) {
 
 // --------------------------------------------------------------- GEMV launch
 struct GemvPlan {
+  int kt = 64;
   int stages = 0;
   int grid = 0;
   size_t smem = 0;
 };
 
 int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
-  const size_t tile = (size_t)m.KT * m.NT;
+  const size_t tile = (size_t)kNT * m.KT;
   const size_t codes = align16((size_t)rows * m.Kpad);
-  size_t xs = std::max<size_t>((size_t)m.NT * 4, (size_t)kThreads * 4);
-  if (pro != PRO_ABSMAX) xs = std::max<size_t>(xs, (size_t)m.K * 4);
+  // xs holds one input row (both prologues) and later the epilogue exchange
+  size_t xs = std::max<size_t>((size_t)kNT * 4, (size_t)kThreads * 4);
+  xs = std::max<size_t>(xs, (size_t)m.K * 4);
+  (void)pro;
   const size_t fixed = codes + align16(xs);
   const size_t budget = (size_t)c.max_smem;
   if (fixed + 2 * (tile + 8) + 16 > budget) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: GEMV K=%d x %d rows does not fit in shared memory", m.K, rows);
     return 0;
   }
-  int S = static_cast<int>((budget - fixed - 16) / (tile + 8));
+  int S = static_cast<int>((budget - fixed - 24) / (tile + 8));
   S = std::min(S, 12);
   const long long T = (long long)m.n_slabs * m.n_ktiles;
+  p.kt = m.KT;
   p.stages = S;
-  p.smem = align16((size_t)S * tile + 8 * (size_t)S) + codes + align16(xs);
+  p.smem = align16((size_t)S * tile + 8 * (size_t)(S + 1)) + codes + align16(xs);
   p.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(T, c.num_sms)));
   return 1;
 }
@@ -250,8 +273,8 @@ GemvArgs base_args(const Mat &m, const GemvPlan &p, int *acc, int *cnt, int *err
   a.Kpad = m.Kpad;
   a.N = m.N;
   a.Npad = m.Npad;
-  a.NT = m.NT;
-  a.KT = m.KT;
+
+
   a.n_slabs = m.n_slabs;
   a.n_ktiles = m.n_ktiles;
   a.stages = p.stages;
@@ -264,6 +287,7 @@ GemvArgs base_args(const Mat &m, const GemvPlan &p, int *acc, int *cnt, int *err
 
 template <int PRO, int EPI, int MR>
 cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, bool pdl) {
+  if (p.kt != 64 && p.kt != 128) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(p.grid);
   cfg.blockDim = dim3(kThreads);
@@ -273,22 +297,39 @@ cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, b
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_gemv<PRO, EPI, MR>, a);
+  cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+  return p.kt == 128 ? cudaLaunchKernelEx(&cfg, k_gemv<PRO, EPI, MR, 128>, a)
+                     : cudaLaunchKernelEx(&cfg, k_gemv<PRO, EPI, MR, 64>, a);
 }
 
-cudaError_t launch_attention(const AttnArgs &a, size_t smem, cudaStream_t st, bool pdl) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(a.n_heads);
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
+size_t scores_smem(const AttnArgs &a) {
+  const int hd4 = (a.hd + 3) & ~3, stride = (a.hd & 3) == 0 ? a.hd + 4 : a.hd + 1;
+  return ((size_t)(a.n_heads / a.n_kv) * hd4 + (size_t)kScoreChunk * stride) * sizeof(float);
+}
+size_t pv_smem(const AttnArgs &a) {
+  return ((((size_t)a.max_seq + 3) & ~size_t(3)) + (size_t)kPVRing * kPVChunk * kPVSlice) * sizeof(float);
+}
+
+// The two attention kernels of one layer: scores (part 0), then softmax and
+// values (part 1).
+cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl, int part) {
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg{};
+  cfg.stream = st;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_attention, a);
+  cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+  if (part == 0) {
+    cfg.gridDim = dim3((a.max_seq + kScoreChunk - 1) / kScoreChunk, a.n_kv);
+    cfg.blockDim = dim3(kScoreThreads);
+    cfg.dynamicSmemBytes = scores_smem(a);
+    return cudaLaunchKernelEx(&cfg, k_attn_scores, a);
+  }
+  cfg.gridDim = dim3((a.hd + kPVSlice - 1) / kPVSlice, a.n_heads);
+  cfg.blockDim = dim3(kPVThreads);
+  cfg.dynamicSmemBytes = pv_smem(a);
+  return cudaLaunchKernelEx(&cfg, k_attn_pv, a);
 }
 
 cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
@@ -301,7 +342,7 @@ cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, k_step_finish, step, argmax, err, result, tokens, max_seq);
 }
 
@@ -329,7 +370,7 @@ struct DevModel {
   float *wte_s = nullptr;
   float *rope_cos = nullptr, *rope_sin = nullptr;
   // activations and scratch
-  float *x = nullptr, *q = nullptr, *o = nullptr, *h = nullptr, *logits = nullptr;
+  float *x = nullptr, *q = nullptr, *o = nullptr, *h = nullptr, *logits = nullptr, *scores = nullptr;
   int *acc = nullptr, *cnt = nullptr, *err = nullptr, *result = nullptr, *tokens = nullptr;
   unsigned long long *argmax = nullptr;
   StepState *step = nullptr;
@@ -345,6 +386,8 @@ struct DevModel {
   size_t attn_smem = 0;
   int max_npad = 0, max_slabs = 0;
   std::vector<DevKV *> kvs;
+  // per-kernel events while llmq_step_profile records a step outside a graph
+  std::vector<cudaEvent_t> *prof = nullptr;
 };
 
 std::unordered_map<const void *, DevModel *> g_models;
@@ -373,7 +416,7 @@ void release_model(DevModel *M) {
   free_mat(M->lm);
   for (auto *v : {&M->attn_norm, &M->ffn_norm, &M->bias_qkv})
     for (float *p : *v) cudaFree(p);
-  void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o,
+  void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o, M->scores,
                       M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step};
   for (void *p : dev_ptrs) cudaFree(p);
   cudaFreeHost(M->h_step);
@@ -425,7 +468,7 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   CK(cudaEventCreate(&M->ev0));
   CK(cudaEventCreate(&M->ev1));
   // fused QKV: [Wq | Wk | Wv], slabs of whole heads
-  const int nt_qkv = (256 / hd) * hd;
+  const int nt_qkv = kNT;  // RoPE happens in the attention kernel, so slabs need not align with heads
   const int n_qkv = qd + 2 * kvd;
   for (int l = 0; l < L; ++l) {
     const QLlamaBlock &b = m->blocks[l];
@@ -490,7 +533,15 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
       !plan_gemv(c, M->w13[0], PRO_RMSNORM, 1, M->p_w13) || !plan_gemv(c, M->w2[0], PRO_ABSMAX, 1, M->p_w2) ||
       !plan_gemv(c, M->lm, PRO_RMSNORM, 1, M->p_lm))
     return 0;
-  M->attn_smem = ((size_t)((hd + 3) & ~3) + (size_t)cfg.max_seq) * sizeof(float);
+  {
+    AttnArgs probe{};
+    probe.n_heads = cfg.n_heads;
+    probe.n_kv = cfg.n_kv;
+    probe.hd = hd;
+    probe.max_seq = cfg.max_seq;
+    M->attn_smem = std::max(scores_smem(probe), pv_smem(probe));
+  }
+  if (!dev_zeros(&M->scores, (size_t)cfg.n_heads * cfg.max_seq)) return 0;
   if (M->attn_smem > (size_t)c.max_smem) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: max_seq %d too long for the attention kernel", cfg.max_seq);
     return 0;
@@ -505,7 +556,7 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   max_slabs = std::max(max_slabs, M->lm.n_slabs);
   M->max_npad = max_npad;
   M->max_slabs = max_slabs;
-  if (!dev_zeros(&M->x, dm) || !dev_zeros(&M->q, qd) || !dev_zeros(&M->o, qd) || !dev_zeros(&M->h, dff) ||
+  if (!dev_zeros(&M->x, dm) || !dev_zeros(&M->q, (size_t)qd + kvd) || !dev_zeros(&M->o, qd) || !dev_zeros(&M->h, dff) ||
       !dev_zeros(&M->logits, std::max(cfg.vocab, max_npad)) || !dev_zeros(&M->acc, max_npad) ||
       !dev_zeros(&M->cnt, max_slabs) || !dev_zeros(&M->err, 4) || !dev_zeros(&M->result, 4) ||
       !dev_zeros(&M->tokens, cfg.max_seq) || !dev_zeros(&M->argmax, 1) || !dev_zeros(&M->step, 1))
@@ -547,6 +598,29 @@ DevModel *get_model(const QLlamaModel *m) {
   return M;
 }
 
+// Copies cache rows [0, len) between the reference's host layout
+// (per layer [max_seq][n_kv*hd]) and the head-major device layout
+// (per layer [n_kv][max_seq][hd]).
+int kv_transfer(DevModel *M, DevKV *K, const LlamaKV *kv, int len, cudaMemcpyKind dir) {
+  const int hd = M->cfg.head_dim, nkv = M->cfg.n_kv;
+  const size_t per_layer = (size_t)K->max_seq * M->kvd;
+  for (int l = 0; l < M->cfg.n_layers; ++l)
+    for (int h = 0; h < nkv; ++h) {
+      float *dk = K->k + l * per_layer + (size_t)h * K->max_seq * hd;
+      float *dv = K->v + l * per_layer + (size_t)h * K->max_seq * hd;
+      float *hk = kv->k[l] + (size_t)h * hd, *hv = kv->v[l] + (size_t)h * hd;
+      const size_t hp = (size_t)M->kvd * sizeof(float), dp = (size_t)hd * sizeof(float);
+      if (dir == cudaMemcpyHostToDevice) {
+        CK(cudaMemcpy2D(dk, dp, hk, hp, dp, len, dir));
+        CK(cudaMemcpy2D(dv, dp, hv, hp, dp, len, dir));
+      } else {
+        CK(cudaMemcpy2D(hk, hp, dk, dp, dp, len, dir));
+        CK(cudaMemcpy2D(hv, hp, dv, dp, dp, len, dir));
+      }
+    }
+  return 1;
+}
+
 DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
   if (!kv || !kv->k || !kv->v) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: null KV cache");
@@ -577,15 +651,9 @@ DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
   }
   // A cache that already holds positions (filled elsewhere): adopt its rows.
   const int len = std::min(std::max(kv->len, 0), kv->max_seq);
-  for (int l = 0; l < cfg.n_layers && len > 0; ++l) {
-    if (cudaMemcpy(K->k + l * per_layer, kv->k[l], (size_t)len * M->kvd * sizeof(float), cudaMemcpyHostToDevice) !=
-            cudaSuccess ||
-        cudaMemcpy(K->v + l * per_layer, kv->v[l], (size_t)len * M->kvd * sizeof(float), cudaMemcpyHostToDevice) !=
-            cudaSuccess) {
-      llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: KV upload failed");
-      release_kv(K);
-      return nullptr;
-    }
+  if (len > 0 && !kv_transfer(M, K, kv, len, cudaMemcpyHostToDevice)) {
+    release_kv(K);
+    return nullptr;
   }
   M->kvs.push_back(K);
   g_kvs[K->key] = K;
@@ -596,6 +664,14 @@ DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
 // the device state (chained steps); 1: copied from h_step, result copied back;
 // 2: as 1, plus the logits.
 int record_step(DevModel *M, DevKV *K, int mode) {
+#define PROF_MARK()                                                     \
+  do {                                                                  \
+    if (M->prof) {                                                      \
+      M->prof->emplace_back();                                          \
+      cudaEventCreate(&M->prof->back());                                \
+      cudaEventRecord(M->prof->back(), st);                             \
+    }                                                                   \
+  } while (0)
   cudaStream_t st = M->stream;
   const LlmqConfig &cfg = M->cfg;
   const size_t per_layer = (size_t)K->max_seq * M->kvd;
@@ -613,18 +689,17 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       a.kvd = M->kvd;
       a.hd = cfg.head_dim;
       a.max_seq = K->max_seq;
-      a.kcache = K->k + l * per_layer;
       a.vcache = K->v + l * per_layer;
-      a.rope_cos = M->rope_cos;
-      a.rope_sin = M->rope_sin;
       if (l == 0) {
         a.wte_q = M->wte_q;
         a.wte_s = M->wte_s;
         a.vocab = cfg.vocab;
         a.x_out = M->x;
         CK((launch_gemv<PRO_EMBED_RMSNORM, EPI_QKV, 1>(a, M->p_qkv, st, false)));
+      PROF_MARK();
       } else {
         CK((launch_gemv<PRO_RMSNORM, EPI_QKV, 1>(a, M->p_qkv, st, true)));
+      PROF_MARK();
       }
     }
     {
@@ -632,19 +707,26 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       a.q = M->q;
       a.kcache = K->k + l * per_layer;
       a.vcache = K->v + l * per_layer;
+      a.scores = M->scores;
       a.out = M->o;
       a.step = M->step;
+      a.rope_cos = M->rope_cos;
+      a.rope_sin = M->rope_sin;
       a.n_heads = cfg.n_heads;
       a.n_kv = cfg.n_kv;
       a.hd = cfg.head_dim;
       a.max_seq = K->max_seq;
-      CK(launch_attention(a, M->attn_smem, st, true));
+      CK(launch_attention(a, st, true, 0));
+      PROF_MARK();
+      CK(launch_attention(a, st, true, 1));
+      PROF_MARK();
     }
     {
       GemvArgs a = base_args(M->wo[l], M->p_wo, M->acc, M->cnt, M->err);
       a.in = M->o;
       a.out = M->x;
       CK((launch_gemv<PRO_ABSMAX, EPI_RESID, 1>(a, M->p_wo, st, true)));
+      PROF_MARK();
     }
     {
       GemvArgs a = base_args(M->w13[l], M->p_w13, M->acc, M->cnt, M->err);
@@ -653,12 +735,14 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       a.eps = cfg.eps;
       a.out = M->h;
       CK((launch_gemv<PRO_RMSNORM, EPI_SWIGLU, 1>(a, M->p_w13, st, true)));
+      PROF_MARK();
     }
     {
       GemvArgs a = base_args(M->w2[l], M->p_w2, M->acc, M->cnt, M->err);
       a.in = M->h;
       a.out = M->x;
       CK((launch_gemv<PRO_ABSMAX, EPI_RESID, 1>(a, M->p_w2, st, true)));
+      PROF_MARK();
     }
   }
   {
@@ -669,11 +753,14 @@ int record_step(DevModel *M, DevKV *K, int mode) {
     a.out = M->logits;
     a.argmax = M->argmax;
     CK((launch_gemv<PRO_RMSNORM, EPI_LOGITS, 1>(a, M->p_lm, st, true)));
+      PROF_MARK();
   }
   CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st));
+      PROF_MARK();
   if (mode > 0) CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
   if (mode == 2)
     CK(cudaMemcpyAsync(M->h_logits, M->logits, (size_t)cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost, st));
+#undef PROF_MARK
   return 1;
 }
 
@@ -802,11 +889,11 @@ int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
   m.K = K;
   m.N = N;
   m.NT = 256;
-  m.KT = kKT;
-  m.Kpad = std::max(roundup(K, kKT), kKT);
+  m.KT = choose_kt(K, std::max(roundup(N, kNT), kNT));
+  m.Kpad = std::max(roundup(K, m.KT), m.KT);
   m.Npad = std::max(roundup(N, m.NT), m.NT);
   m.n_slabs = m.Npad / m.NT;
-  m.n_ktiles = m.Kpad / kKT;
+  m.n_ktiles = m.Kpad / m.KT;
   const bool many = M > 1;
   GemvPlan plan;
   int rows_per = many ? 8 : 1;
@@ -834,7 +921,7 @@ int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
     const long long chunks = (long long)m.Kpad / 16 * m.Npad;
     const int blocks = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148LL * 64));
     k_repack_plain<<<std::max(blocks, 1), 256, 0, st>>>(reinterpret_cast<const int8_t *>(c->wraw), K, N, m.Kpad,
-                                                         m.Npad, m.NT, m.KT, c->wtile);
+                                                         m.Npad, kNT, m.KT, c->wtile);
     CK(cudaGetLastError());
   }
   for (int r0 = 0; r0 < M; r0 += rows_per) {
@@ -956,11 +1043,8 @@ int llmqd_kv_download(const QLlamaModel *m, const LlamaKV *kv, int len) {
   if (!K) return 0;
   const size_t per_layer = (size_t)K->max_seq * M->kvd;
   CK(cudaStreamSynchronize(M->stream));
-  for (int l = 0; l < M->cfg.n_layers && len > 0; ++l) {
-    CK(cudaMemcpy(kv->k[l], K->k + l * per_layer, (size_t)len * M->kvd * sizeof(float), cudaMemcpyDeviceToHost));
-    CK(cudaMemcpy(kv->v[l], K->v + l * per_layer, (size_t)len * M->kvd * sizeof(float), cudaMemcpyDeviceToHost));
-  }
-  return 1;
+  (void)per_layer;
+  return len > 0 ? kv_transfer(M, K, kv, len, cudaMemcpyDeviceToHost) : 1;
 }
 
 float llmqd_last_ms(void) { return g_last_ms; }
@@ -997,26 +1081,54 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   DevModel *M = get_model(m);
   if (!M) return q_llama_last_error();
-  if (layer < 0 || layer >= M->cfg.n_layers || which < 0 || which > 4 || iters <= 0) {
+  if (layer < 0 || layer >= M->cfg.n_layers || which < 0 || which > 5 || iters <= 0 ||
+      (which == 5 && M->kvs.empty())) {
     llmq_set_error(LLMQ_ERR_ARG, "llmq_bench_gemv: bad arguments");
     return LLMQ_ERR_ARG;
   }
-  const Mat *mt[5] = {&M->qkv[layer], &M->wo[layer], &M->w13[layer], &M->w2[layer], &M->lm};
-  const GemvPlan *pl[5] = {&M->p_qkv, &M->p_wo, &M->p_w13, &M->p_w2, &M->p_lm};
-  const bool rms[5] = {true, false, true, false, true};
-  float *ins[5] = {M->x, M->o, M->x, M->h, M->x};
-  const Mat &mm = *mt[which];
-  const GemvPlan &p = *pl[which];
-  GemvArgs a = base_args(mm, p, M->acc, M->cnt, M->err);
-  a.in = ins[which];
-  a.gamma = M->final_norm;
-  a.eps = M->cfg.eps;
-  a.out = M->logits;
   cudaStream_t st = M->stream;
-  auto launch = [&]() {
-    return rms[which] ? launch_gemv<PRO_RMSNORM, EPI_PLAIN, 1>(a, p, st, false)
-                      : launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, p, st, false);
-  };
+  std::function<cudaError_t()> launch;
+  GemvArgs a{};
+  AttnArgs at{};
+  if (which == 5) {  // attention over the first cache at its current position
+    DevKV *K = M->kvs.front();
+    const size_t per_layer = (size_t)K->max_seq * M->kvd;
+    at.q = M->q;
+    at.kcache = K->k + layer * per_layer;
+    at.vcache = K->v + layer * per_layer;
+    at.scores = M->scores;
+    at.out = M->o;
+    at.step = M->step;
+    at.rope_cos = M->rope_cos;
+    at.rope_sin = M->rope_sin;
+    at.n_heads = M->cfg.n_heads;
+    at.n_kv = M->cfg.n_kv;
+    at.hd = M->cfg.head_dim;
+    at.max_seq = K->max_seq;
+    launch = [&]() {
+      const cudaError_t e = launch_attention(at, st, false, 0);
+      return e != cudaSuccess ? e : launch_attention(at, st, false, 1);
+    };
+  } else {
+    const Mat *mt[5] = {&M->qkv[layer], &M->wo[layer], &M->w13[layer], &M->w2[layer], &M->lm};
+    const GemvPlan *pl[5] = {&M->p_qkv, &M->p_wo, &M->p_w13, &M->p_w2, &M->p_lm};
+    const bool rms[5] = {true, false, true, false, true};
+    float *ins[5] = {M->x, M->o, M->x, M->h, M->x};
+    const Mat &mm = *mt[which];
+    const GemvPlan &p = *pl[which];
+    a = base_args(mm, p, M->acc, M->cnt, M->err);
+    a.in = ins[which];
+    a.gamma = M->final_norm;
+    a.eps = M->cfg.eps;
+    a.out = M->logits;
+    const bool r = rms[which];
+    launch = [&a, &p, st, r]() {
+      return r ? launch_gemv<PRO_RMSNORM, EPI_PLAIN, 1>(a, p, st, false)
+               : launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, p, st, false);
+    };
+    const int logical_n = which == 2 ? 2 * mm.N : mm.N;
+    *bytes_per_launch = (double)mm.K * logical_n + 4.0 * logical_n + 4.0 * mm.K + 4.0 * mm.N;
+  }
   for (int i = 0; i < 3; ++i)
     if (launch() != cudaSuccess) return LLMQ_ERR_CUDA;
   if (cudaEventRecord(M->ev0, st) != cudaSuccess) return LLMQ_ERR_CUDA;
@@ -1029,13 +1141,17 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
   float ms = 0.0f;
   cudaEventElapsedTime(&ms, M->ev0, M->ev1);
   *ms_per_launch = ms / iters;
-  const int logical_n = which == 2 ? 2 * mm.N : mm.N;
-  *bytes_per_launch = (double)mm.K * logical_n + 4.0 * logical_n + 4.0 * mm.K + 4.0 * (which == 2 ? mm.N : mm.N);
+  if (which == 5) {
+    int pos = 0;
+    cudaMemcpy(&pos, &M->step->pos, sizeof(int), cudaMemcpyDeviceToHost);
+    // K and V rows of one layer read for every query head (the group shares them in L2)
+    *bytes_per_launch = 2.0 * (pos + 1) * M->kvd * 4.0 + 8.0 * M->qd;
+  }
   return LLMQ_OK;
 }
 
 // Number of kernels one decode step launches (for the benchmark's gpu_launches).
-LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) { return 5 * m->n_layers + 2; }
+LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) { return 6 * m->n_layers + 2; }
 
 }  // extern "C"
 
@@ -1046,4 +1162,41 @@ extern "C" LLMQ_API int q_llama_set_device(int device) {
     return LLMQ_ERR_NO_DEVICE;
   }
   return LLMQ_OK;
+}
+
+// Runs one decode step of `token` at kv->len outside the graph, kernel by
+// kernel with CUDA events between launches, and writes each kernel's time in
+// milliseconds to ms[0 .. llmq_kernels_per_step(m)).  Advances kv->len by one
+// like a decode step.  For attribution only: no overlap between kernels.
+extern "C" LLMQ_API int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, int max_n) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevModel *M = get_model(m);
+  if (!M) return q_llama_last_error();
+  DevKV *K = get_kv(M, kv);
+  if (!K || !check_step_inputs(M, kv, token, 1)) return q_llama_last_error();
+  M->h_step->token = token;
+  M->h_step->pos = kv->len;
+  std::vector<cudaEvent_t> evs;
+  cudaEvent_t e0;
+  cudaEventCreate(&e0);
+  M->prof = &evs;
+  cudaEventRecord(e0, M->stream);
+  const int ok = record_step(M, K, 1);
+  M->prof = nullptr;
+  cudaStreamSynchronize(M->stream);
+  int rc = ok ? LLMQ_OK : q_llama_last_error();
+  cudaEvent_t prev = e0;
+  for (size_t i = 0; i < evs.size(); ++i) {
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, prev, evs[i]);
+    if ((int)i < max_n) ms[i] = t;
+    prev = evs[i];
+  }
+  for (cudaEvent_t e : evs) cudaEventDestroy(e);
+  cudaEventDestroy(e0);
+  if (rc == LLMQ_OK) {
+    if (M->h_result[1]) return reset_after_device_error(M, M->h_result[1]), LLMQ_ERR_CUDA;
+    kv->len += 1;
+  }
+  return rc;
 }

@@ -15,7 +15,7 @@
 
 namespace llmq {
 
-constexpr int kThreads = 256;     // GEMV CTA size (8 warps)
+constexpr int kThreads = 512;     // GEMV CTA size (16 warps)
 constexpr int kMaxRows = 8;       // rows per GEMV launch (decode uses 1)
 
 // Error bits written to the per-model error word.
@@ -52,19 +52,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
       : "memory");
   return ok != 0;
 }
-__device__ __forceinline__ uint64_t global_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-// Bounded wait on an mbarrier phase: gives up after ~2 s of wall time (and a hard
-// iteration cap), so a lost copy can never hang the GPU.
-__device__ __noinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase) {
+// Bounded wait on an mbarrier phase: gives up after 2^32 SM cycles (about 2 s
+// at boost clock; the SM-local counter is cheap to read, unlike %globaltimer)
+// or 2^26 polls, so a lost copy can never hang the GPU.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase) {
   if (mbar_try_wait(bar, phase)) return true;
-  const uint64_t t0 = global_ns();
-  for (uint32_t it = 0; it < (1u << 24); ++it) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0; it < (1u << 26); ++it) {
     if (mbar_try_wait(bar, phase)) return true;
-    if ((it & 255u) == 255u && global_ns() - t0 > 2000000000ull) break;
+    if ((it & 63u) == 63u && clock64() - t0 > (1ll << 32)) break;
   }
   return false;
 }
@@ -188,11 +184,20 @@ enum Prologue : int {
 };
 enum Epilogue : int {
   EPI_PLAIN = 0,   // out[r][j] = as*ws*acc                         (qmatmul)
-  EPI_QKV = 1,     // + bias, RoPE on q and k, k/v appended to the cache
+  EPI_QKV = 1,     // + bias; q and k to `out`, v appended to the cache
   EPI_RESID = 2,   // out[j] += as*ws*acc                           (Wo, W2)
   EPI_SWIGLU = 3,  // out[j] = SiLU(gate) * up                      (W1|W3)
   EPI_LOGITS = 4   // logits + device argmax                        (lm-head)
 };
+
+// Tile geometry: a tile is KT rows of k by kNT columns, stored as
+// [KT/16][kNT][16 bytes] so that one column's 16 consecutive k values form one
+// 16-byte chunk (four dp4a operands) and a warp reads 512 contiguous bytes.
+// KT is 64 (16 KB tiles, finer load balance for small matrices) or 128 (32 KB
+// tiles, half the per-tile overhead for large ones).
+constexpr int kNT = 256;
+constexpr int kParts = kThreads / kNT;  // threads per column
+static_assert(kParts * kNT == kThreads, "tile geometry");
 
 struct StepState {
   int token;
@@ -200,9 +205,9 @@ struct StepState {
 };
 
 struct GemvArgs {
-  const uint8_t *w;    // tiles [n_slabs][n_ktiles][KT/16][NT][16]
+  const uint8_t *w;    // tiles [n_slabs][n_ktiles][KT/16][kNT][16]
   const float *ws;     // per physical column scale [Npad]
-  int K, Kpad, N, Npad, NT, KT, n_slabs, n_ktiles, stages, rows;
+  int K, Kpad, N, Npad, n_slabs, n_ktiles, stages, rows;
   int *acc;            // [rows][Npad] int32, zero before and after
   int *cnt;            // [n_slabs], zero before and after
   int *err;
@@ -216,11 +221,10 @@ struct GemvArgs {
   const StepState *step;
   float *x_out;        // PRO_EMBED_RMSNORM: the residual stream is written here
   // epilogue
-  float *out;          // [rows][N]
+  float *out;          // [rows][N]; EPI_QKV: q then k of this step (qd + kvd)
   const float *bias;   // EPI_QKV, physical order
   int qd, kvd, hd, max_seq;
-  float *kcache, *vcache;  // this layer's [max_seq][kvd]
-  const float *rope_cos, *rope_sin;  // [max_seq][hd/2]
+  float *vcache;       // EPI_QKV: this layer's [n_kv][max_seq][hd]
   unsigned long long *argmax;
 };
 
@@ -229,15 +233,26 @@ __device__ __forceinline__ long long tile_owner(long long t, long long T, long l
   return ((t + 1) * G + T - 1) / T - 1;
 }
 
+__device__ __forceinline__ int dot16(const int4 w, const int4 x, int acc) {
+  acc = __dp4a(w.x, x.x, acc);
+  acc = __dp4a(w.y, x.y, acc);
+  acc = __dp4a(w.z, x.z, acc);
+  return __dp4a(w.w, x.w, acc);
+}
+
 // ------------------------------------------------------------ the GEMV kernel
 // x(rows, K) @ W(K, N) with W pre-tiled so every tile is one contiguous bulk
 // copy.  Each CTA owns a contiguous range of tiles (balanced to one tile),
 // streams them through a `stages`-deep shared-memory ring, and accumulates
-// exact int32 dot products with dp4a.  Partial sums of a column slab are added
-// into `acc` with integer atomics; the CTA that completes a slab applies the
-// fused epilogue and re-zeroes `acc` and `cnt` for the next launch.
-template <int PRO, int EPI, int MR>
+// exact int32 dot products with dp4a (two threads per column, each with two
+// independent accumulators).  Partial sums of a column slab are added into
+// `acc` with integer atomics; the CTA that completes a slab applies the fused
+// epilogue and re-zeroes `acc` and `cnt` for the next launch.
+template <int PRO, int EPI, int MR, int KT>
 __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
+  constexpr int kTileBytes = kNT * KT;
+  constexpr int kChunksPerPart = (KT / 16) / kParts;
+  static_assert(kChunksPerPart * kParts * 16 == KT && kChunksPerPart % 2 == 0, "tile depth");
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ float s_red[32];
   __shared__ unsigned long long s_red64[32];
@@ -247,11 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   __shared__ int s_abort;
 
   const int tid = threadIdx.x;
-  const int tile_bytes = a.KT * a.NT;
   const int S = a.stages;
   uint8_t *stage0 = sm;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + (size_t)S * tile_bytes);
-  int8_t *codes = reinterpret_cast<int8_t *>(sm + (((size_t)S * tile_bytes + 8 * S + 15) & ~size_t(15)));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + (size_t)S * kTileBytes);
+  int8_t *codes = reinterpret_cast<int8_t *>(sm + (((size_t)S * kTileBytes + 8 * (S + 1) + 15) & ~size_t(15)));
   float *xs = reinterpret_cast<float *>(codes + (((size_t)a.rows * a.Kpad + 15) & ~size_t(15)));
   float *ebuf = xs;  // epilogue exchange buffer (prologue vector is dead by then)
 
@@ -262,7 +276,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   const int n = static_cast<int>(t_end - t_begin);
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s <= S; ++s) mbar_init(&bars[s], 1);  // S weight stages + the input row
     fence_mbar_init();
     s_abort = 0;
   }
@@ -272,26 +286,44 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   if (tid == 0) {
     const int first = n < S ? n : S;
     for (; issued < first; ++issued) {
-      mbar_expect_tx(&bars[issued], tile_bytes);
-      bulk_load(stage0 + (size_t)issued * tile_bytes, a.w + (size_t)(t_begin + issued) * tile_bytes,
-                tile_bytes, &bars[issued]);
+      mbar_expect_tx(&bars[issued], kTileBytes);
+      bulk_load(stage0 + (size_t)issued * kTileBytes, a.w + (size_t)(t_begin + issued) * kTileBytes,
+                kTileBytes, &bars[issued]);
     }
   }
   pdl_launch_dependents();
   pdl_wait();
 
   // ------------------------------------------------------------ prologue
+  // The input rows come from the previous kernel: copied into xs with one bulk
+  // copy per row once that kernel's writes are visible (plain loads when the
+  // row is not 16-byte sized and aligned).
+  uint64_t *bar_in = bars + S;
+  const bool bulk_in = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.in) & 15) == 0;
+  auto load_row = [&](const float *src, int phase) {
+    if (bulk_in && a.K > 0) {
+      if (tid == 0) {
+        mbar_expect_tx(bar_in, static_cast<uint32_t>(a.K) * 4u);
+        bulk_load(xs, src, static_cast<uint32_t>(a.K) * 4u, bar_in);
+      }
+      if (!mbar_wait_bounded(bar_in, static_cast<uint32_t>(phase & 1))) s_abort = 1;
+    } else {
+      for (int k = tid; k < a.K; k += kThreads) xs[k] = src[k];
+    }
+    __syncthreads();
+  };
   if (PRO == PRO_ABSMAX) {
     for (int r = 0; r < a.rows && r < MR; ++r) {
-      const float *in = a.in + (size_t)r * a.K;
+      load_row(a.in + (size_t)r * a.K, r);
       float m = 0.0f;
-      for (int k = tid; k < a.K; k += kThreads) m = fmaxf(m, fabsf(in[k]));
+      for (int k = tid; k < a.K; k += kThreads) m = fmaxf(m, fabsf(xs[k]));
       m = block_max<kThreads>(m, s_red);
       const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;  // quant.c:106
       const float inv = __fdiv_rn(1.0f, as);                      // quant.c:107
       if (tid == 0) s_as[r] = as;
       int8_t *cr = codes + (size_t)r * a.Kpad;
-      for (int k = tid; k < a.Kpad; k += kThreads) cr[k] = k < a.K ? code_of(__fmul_rn(in[k], inv)) : 0;
+      for (int k = tid; k < a.Kpad; k += kThreads) cr[k] = k < a.K ? code_of(__fmul_rn(xs[k], inv)) : 0;
+      __syncthreads();  // xs is reloaded for the next row
     }
   } else {
     // RMSNorm of one row (rmsnorm.c:7-21), then activation quantisation.
@@ -308,20 +340,47 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         xs[k] = v;
         if (blockIdx.x == 0) a.x_out[k] = v;
       }
+      __syncthreads();
     } else {
-      for (int k = tid; k < K; k += kThreads) xs[k] = a.in[k];
+      load_row(a.in, 0);
     }
-    __syncthreads();
     if (tid == 0) {
-      // The sequential sum of squares: one dependent chain, like the reference.
+      // The sequential sum of squares: one dependent chain of adds, like the
+      // reference; the next 16 values are loaded while the current 16 are added.
       float ms = 0.0f;
       int k = 0;
-      for (; k + 4 <= K; k += 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(xs + k);
-        ms = __fadd_rn(ms, __fmul_rn(v.x, v.x));
-        ms = __fadd_rn(ms, __fmul_rn(v.y, v.y));
-        ms = __fadd_rn(ms, __fmul_rn(v.z, v.z));
-        ms = __fadd_rn(ms, __fmul_rn(v.w, v.w));
+      if ((K & 3) == 0 && K >= 16) {
+        const float4 *v4 = reinterpret_cast<const float4 *>(xs);
+        const int n4 = K >> 2;
+        float4 b0 = v4[0], b1 = v4[1], b2 = v4[2], b3 = v4[3];
+        int i = 4;
+#define LLMQ_SQ_ACC(b)                          \
+  ms = __fadd_rn(ms, __fmul_rn((b).x, (b).x));  \
+  ms = __fadd_rn(ms, __fmul_rn((b).y, (b).y));  \
+  ms = __fadd_rn(ms, __fmul_rn((b).z, (b).z));  \
+  ms = __fadd_rn(ms, __fmul_rn((b).w, (b).w))
+        for (;;) {
+          const bool more = i + 4 <= n4;
+          float4 c0, c1, c2, c3;
+          if (more) {
+            c0 = v4[i];
+            c1 = v4[i + 1];
+            c2 = v4[i + 2];
+            c3 = v4[i + 3];
+          }
+          LLMQ_SQ_ACC(b0);
+          LLMQ_SQ_ACC(b1);
+          LLMQ_SQ_ACC(b2);
+          LLMQ_SQ_ACC(b3);
+          if (!more) break;
+          b0 = c0;
+          b1 = c1;
+          b2 = c2;
+          b3 = c3;
+          i += 4;
+        }
+#undef LLMQ_SQ_ACC
+        k = i * 4;
       }
       for (; k < K; ++k) ms = __fadd_rn(ms, __fmul_rn(xs[k], xs[k]));
       ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
@@ -344,37 +403,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   __syncthreads();
 
   // --------------------------------------------------------------- main loop
-  const int NT = a.NT;
-  const int P = kThreads / NT;  // threads per column
-  const int col = tid % NT;
-  const int part = tid / NT;
-  const bool active = part < P;
-  const int CH = a.KT / 16;
-  int acc[MR];
+  const int col = tid % kNT;
+  const int part = tid / kNT;
+  int acc0[MR], acc1[MR];
 #pragma unroll
-  for (int r = 0; r < MR; ++r) acc[r] = 0;
+  for (int r = 0; r < MR; ++r) acc0[r] = acc1[r] = 0;
 
   auto flush = [&](long long slab) {
-    // combine the P partial sums of each column
+    // combine the two accumulators, then the kParts threads of each column
     int *red = reinterpret_cast<int *>(ebuf);
-    if (P > 1) {
 #pragma unroll
-      for (int r = 0; r < MR; ++r) {
-        if (r >= a.rows) break;
-        __syncthreads();
-        red[tid] = active ? acc[r] : 0;
-        __syncthreads();
-        if (part == 0) {
-          int s = 0;
-          for (int p = 0; p < P; ++p) s += red[p * NT + col];
-          acc[r] = s;
-        }
+    for (int r = 0; r < MR; ++r) {
+      if (r >= a.rows) break;
+      __syncthreads();
+      red[tid] = acc0[r] + acc1[r];
+      __syncthreads();
+      if (part == 0) {
+        int s = 0;
+#pragma unroll
+        for (int p = 0; p < kParts; ++p) s += red[p * kNT + col];
+        atomicAdd(a.acc + (size_t)r * a.Npad + slab * kNT + col, s);
       }
-    }
-    if (part == 0) {
-#pragma unroll
-      for (int r = 0; r < MR; ++r)
-        if (r < a.rows) atomicAdd(a.acc + (size_t)r * a.Npad + slab * NT + col, acc[r]);
     }
     __threadfence();
     __syncthreads();
@@ -388,12 +437,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     __syncthreads();
     if (!s_flag) return;
     __threadfence();
-    // ---- fused epilogue for columns [slab*NT, slab*NT + NT)
-    const int p0 = static_cast<int>(slab) * NT;
+    // ---- fused epilogue for columns [slab*kNT, slab*kNT + kNT)
+    const int p0 = static_cast<int>(slab) * kNT;
     if (EPI == EPI_PLAIN || EPI == EPI_RESID) {
       for (int r = 0; r < a.rows && r < MR; ++r) {
         const float as = s_as[r];
-        for (int c = tid; c < NT; c += kThreads) {
+        for (int c = tid; c < kNT; c += kThreads) {
           const int j = p0 + c;
           const int v = atomicExch(a.acc + (size_t)r * a.Npad + j, 0);
           if (j < a.N) {
@@ -409,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     } else if (EPI == EPI_LOGITS) {
       const float as = s_as[0];
       unsigned long long best = 0ull;
-      for (int c = tid; c < NT; c += kThreads) {
+      for (int c = tid; c < kNT; c += kThreads) {
         const int j = p0 + c;
         const int v = atomicExch(a.acc + j, 0);
         if (j < a.N) {
@@ -422,9 +471,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       best = block_max_u64<kThreads>(best, s_red64);
       if (tid == 0) atomicMax(a.argmax, best);
     } else if (EPI == EPI_SWIGLU) {
-      // slab = NT/2 gate columns followed by the NT/2 matching up columns
+      // slab = kNT/2 gate columns followed by the kNT/2 matching up columns
       const float as = s_as[0];
-      const int half = NT / 2;
+      constexpr int half = kNT / 2;
       for (int c = tid; c < half; c += kThreads) {
         const int j = static_cast<int>(slab) * half + c;  // d_ff index
         const int vg = atomicExch(a.acc + p0 + c, 0);
@@ -437,73 +486,63 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         }
       }
     } else if (EPI == EPI_QKV) {
+      // q, k (before RoPE, which the attention kernel applies) and v of this step
       const float as = s_as[0];
       const int pos = a.step->pos;
-      for (int c = tid; c < NT; c += kThreads) {
-        const int j = p0 + c;
-        const int v = atomicExch(a.acc + j, 0);
-        ebuf[c] = j < a.N ? __fadd_rn(dequant(as, a.ws[j], v), a.bias[j]) : 0.0f;  // llama.c:546-548
-      }
-      __syncthreads();
-      const int half = a.hd / 2;
       const bool pos_ok = pos >= 0 && pos < a.max_seq;
       if (!pos_ok && tid == 0) atomicOr(a.err, ERR_BAD_POS);
-      for (int c = tid; c < NT; c += kThreads) {
+      for (int c = tid; c < kNT; c += kThreads) {
         const int j = p0 + c;
+        const int v = atomicExch(a.acc + j, 0);
         if (j >= a.N || !pos_ok) continue;
-        float y = ebuf[c];
-        if (j < a.qd + a.kvd) {  // RoPE on q and k (rope.c:58-64)
-          const int jj = j < a.qd ? j : j - a.qd;
-          const int kk = jj % a.hd;
-          if (kk < half) {
-            const float cs = a.rope_cos[(size_t)pos * half + kk], sn = a.rope_sin[(size_t)pos * half + kk];
-            y = __fsub_rn(__fmul_rn(ebuf[c], cs), __fmul_rn(ebuf[c + half], sn));
-          } else {
-            const int k0 = kk - half;
-            const float cs = a.rope_cos[(size_t)pos * half + k0], sn = a.rope_sin[(size_t)pos * half + k0];
-            y = __fadd_rn(__fmul_rn(ebuf[c], cs), __fmul_rn(ebuf[c - half], sn));
-          }
-        }
-        if (j < a.qd)
+        const float y = __fadd_rn(dequant(as, a.ws[j], v), a.bias[j]);  // llama.c:546-548
+        if (j < a.qd + a.kvd) {
           a.out[j] = y;
-        else if (j < a.qd + a.kvd)
-          a.kcache[(size_t)pos * a.kvd + (j - a.qd)] = y;  // llama.c:551
-        else
-          a.vcache[(size_t)pos * a.kvd + (j - a.qd - a.kvd)] = y;  // llama.c:552
+        } else {
+          const int jv = j - a.qd - a.kvd, vh = jv / a.hd;
+          a.vcache[((size_t)vh * a.max_seq + pos) * a.hd + (jv - vh * a.hd)] = y;  // llama.c:552
+        }
       }
     }
     if (tid == 0) a.cnt[slab] = 0;
     __syncthreads();
   };
 
-  long long cur = n > 0 ? t_begin / a.n_ktiles : -1;
-  int done = 0;
+  // (slab, kt) of tile t_begin + i and its ring stage / phase, advanced
+  // incrementally (no division in the loop)
+  long long slab = t_begin / a.n_ktiles;
+  int kt = static_cast<int>(t_begin - slab * a.n_ktiles);
+  long long cur = n > 0 ? slab : -1;
+  int done = 0, s = 0;
+  uint32_t phase = 0;
+  const uint8_t *tile_base = stage0 + ((size_t)part * kChunksPerPart * kNT + col) * 16;
+  const int8_t *code_base = codes + part * (kChunksPerPart * 16);
   for (int i = 0; i < n; ++i) {
-    const long long t = t_begin + i;
-    const long long slab = t / a.n_ktiles;
-    const int kt = static_cast<int>(t - slab * a.n_ktiles);
+    if (i > 0 && ++kt == a.n_ktiles) {
+      kt = 0;
+      ++slab;
+    }
     if (slab != cur) {
       flush(cur);
 #pragma unroll
-      for (int r = 0; r < MR; ++r) acc[r] = 0;
+      for (int r = 0; r < MR; ++r) acc0[r] = acc1[r] = 0;
       cur = slab;
     }
-    const int s = i % S;
-    if (!mbar_wait_bounded(&bars[s], static_cast<uint32_t>((i / S) & 1))) s_abort = 1;
-    const uint8_t *tile = stage0 + (size_t)s * tile_bytes;
-    if (active) {
-      const int8_t *cbase = codes + (size_t)kt * a.KT;
-      for (int c = part; c < CH; c += P) {
-        const int4 w = *reinterpret_cast<const int4 *>(tile + ((size_t)c * NT + col) * 16);
+    if (!mbar_wait_bounded(&bars[s], phase)) s_abort = 1;
+    const uint8_t *tile = tile_base + (size_t)s * kTileBytes;
+    int4 wv[kChunksPerPart];
 #pragma unroll
-        for (int r = 0; r < MR; ++r) {
-          if (r < a.rows) {
-            const int4 x = *reinterpret_cast<const int4 *>(cbase + (size_t)r * a.Kpad + c * 16);
-            acc[r] = __dp4a(w.x, x.x, acc[r]);
-            acc[r] = __dp4a(w.y, x.y, acc[r]);
-            acc[r] = __dp4a(w.z, x.z, acc[r]);
-            acc[r] = __dp4a(w.w, x.w, acc[r]);
-          }
+    for (int c = 0; c < kChunksPerPart; ++c) wv[c] = *reinterpret_cast<const int4 *>(tile + (size_t)c * kNT * 16);
+    const int8_t *cb = code_base + (size_t)kt * KT;
+#pragma unroll
+    for (int r = 0; r < MR; ++r) {
+      if (r < a.rows) {
+#pragma unroll
+        for (int c = 0; c < kChunksPerPart; c += 2) {
+          const int4 x0 = *reinterpret_cast<const int4 *>(cb + (size_t)r * a.Kpad + c * 16);
+          const int4 x1 = *reinterpret_cast<const int4 *>(cb + (size_t)r * a.Kpad + c * 16 + 16);
+          acc0[r] = dot16(wv[c], x0, acc0[r]);
+          acc1[r] = dot16(wv[c + 1], x1, acc1[r]);
         }
       }
     }
@@ -511,10 +550,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     done = i + 1;
     if (s_abort) break;
     if (tid == 0 && issued < n) {
-      mbar_expect_tx(&bars[s], tile_bytes);
-      bulk_load(stage0 + (size_t)s * tile_bytes, a.w + (size_t)(t_begin + issued) * tile_bytes, tile_bytes,
+      mbar_expect_tx(&bars[s], kTileBytes);
+      bulk_load(stage0 + (size_t)s * kTileBytes, a.w + (size_t)(t_begin + issued) * kTileBytes, kTileBytes,
                 &bars[s]);
       ++issued;
+    }
+    if (++s == S) {
+      s = 0;
+      phase ^= 1u;
     }
   }
   if (s_abort) {
@@ -522,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     if (tid == 0) {
       atomicOr(a.err, ERR_TIMEOUT);
       for (int i = done; i < issued; ++i) mbar_wait_bounded(&bars[i % S], static_cast<uint32_t>((i / S) & 1));
+      mbar_wait_bounded(bar_in, static_cast<uint32_t>((PRO == PRO_ABSMAX ? (a.rows - 1) : 0) & 1));
     }
     return;
   }
@@ -529,85 +573,213 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
 }
 
 // --------------------------------------------------------------- attention
+// Device KV cache layout, per layer: [n_kv][max_seq][hd] (head-major), so the
+// rows of one KV head are contiguous and can be staged with asynchronous copies.
 struct AttnArgs {
-  const float *q;       // [n_heads * hd]
-  const float *kcache;  // this layer's [max_seq][kvd]
+  const float *q;       // [n_heads * hd] q, then [kvd] k of this step, before RoPE
+  float *kcache;        // this layer's [n_kv][max_seq][hd]
   const float *vcache;
+  float *scores;        // [n_heads][max_seq] scratch
   float *out;           // [n_heads * hd]
   const StepState *step;
+  const float *rope_cos, *rope_sin;  // [max_seq][hd/2]
   int n_heads, n_kv, hd, max_seq;
 };
 
-constexpr int kAttnThreads = 512;
+constexpr int kScoreChunk = 64;    // key positions per scores CTA
+constexpr int kScoreThreads = 256;
+constexpr int kPVSlice = 32;       // output dims per softmax-V CTA
+constexpr int kPVThreads = 256;
+constexpr int kPVChunk = 128;      // value positions per staged chunk
+constexpr int kPVRing = 4;         // staged chunks in flight
 
-// One CTA per query head (llama.c:554-576): scores over positions 0..pos, each a
-// sequential dot product; max; exp; the sequential sum; then for every d the
-// sequential weighted sum over positions.  Needs (max_seq + hd) floats of
-// dynamic shared memory.
-__global__ void __launch_bounds__(kAttnThreads) k_attention(const AttnArgs a) {
-  extern __shared__ __align__(16) float asm_[];
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// RoPE (rope.c:58-64) of element d of one head: pairs (k, k + hd/2).
+__device__ __forceinline__ float rope_elem(const float *x, int d, int half, const float *cs, const float *sn) {
+  if (d < half) return __fsub_rn(__fmul_rn(x[d], cs[d]), __fmul_rn(x[d + half], sn[d]));
+  const int k = d - half;
+  return __fadd_rn(__fmul_rn(x[d], cs[k]), __fmul_rn(x[k], sn[k]));
+}
+
+// Copies rows [r0, r1) x cols [c0, c0 + w) of a row-major f32 matrix (row
+// stride `ld`) into shared memory rows of stride `sld`, with 16-byte
+// asynchronous copies when alignment allows, else plain loads.
+__device__ __forceinline__ void stage_rows(float *dst, int sld, const float *src, int ld, int r0, int r1, int c0,
+                                           int w, int tid, int nthreads) {
+  if (((ld | c0 | w | sld) & 3) == 0) {
+    const int q = w >> 2;
+    for (int i = tid; i < (r1 - r0) * q; i += nthreads) {
+      const int r = i / q, c = (i - r * q) * 4;
+      cp_async16(dst + (size_t)r * sld + c, src + (size_t)(r0 + r) * ld + c0 + c);
+    }
+  } else {
+    for (int i = tid; i < (r1 - r0) * w; i += nthreads) {
+      const int r = i / w, c = i - r * w;
+      dst[(size_t)r * sld + c] = src[(size_t)(r0 + r) * ld + c0 + c];
+    }
+  }
+}
+
+// Scores of one KV head's query group over one chunk of key positions
+// (llama.c:558-565): q and the new k get RoPE here (the chunk holding `pos`
+// appends the rotated k to the cache), each score is a sequential dot product
+// over the head dimension, times 1/sqrt(hd).  Grid (ceil(max_seq/64), n_kv).
+__global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const AttnArgs a) {
+  extern __shared__ __align__(16) float sm_s[];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x;
+  const int kvh = blockIdx.y;
+  const int p0 = blockIdx.x * kScoreChunk;
+  const int pos = a.step->pos;
+  if (pos < 0 || pos >= a.max_seq || p0 > pos) return;  // bad positions are flagged by the QKV epilogue
+  const int hd = a.hd, half = hd / 2, group = a.n_heads / a.n_kv;
+  const int stride = (hd & 3) == 0 ? hd + 4 : hd + 1;  // padded rows: conflict-free column reads
+  const int hd4 = (hd + 3) & ~3;
+  float *qs = sm_s;                                  // [group][hd4]
+  float *ks = sm_s + (size_t)group * hd4;            // [kScoreChunk][stride]
+  const int p1 = min(p0 + kScoreChunk, pos + 1);     // positions [p0, p1)
+  const float *kc = a.kcache + (size_t)kvh * a.max_seq * hd;
+  // cached keys [p0, min(p1, pos)); the key at `pos` is this step's, rotated below
+  stage_rows(ks, stride, kc, hd, p0, min(p1, pos), 0, hd, tid, kScoreThreads);
+  cp_async_commit();
+  const float *cs = a.rope_cos + (size_t)pos * half, *sn = a.rope_sin + (size_t)pos * half;
+  for (int i = tid; i < group * hd; i += kScoreThreads) {
+    const int g = i / hd, d = i - g * hd;
+    qs[g * hd4 + d] = rope_elem(a.q + (size_t)(kvh * group + g) * hd, d, half, cs, sn);
+  }
+  if (pos < p1) {
+    const float *kn = a.q + (size_t)a.n_heads * hd + (size_t)kvh * hd;
+    for (int d = tid; d < hd; d += kScoreThreads) {
+      const float kr = rope_elem(kn, d, half, cs, sn);
+      ks[(size_t)(pos - p0) * stride + d] = kr;
+      a.kcache[((size_t)kvh * a.max_seq + pos) * hd + d] = kr;  // llama.c:551
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));  // llama.c:532
+  for (int i = tid; i < group * kScoreChunk; i += kScoreThreads) {
+    const int g = i / kScoreChunk, p = i - g * kScoreChunk;
+    if (p0 + p >= p1) continue;
+    const float *kr = ks + (size_t)p * stride;
+    const float *qr = qs + (size_t)g * hd4;
+    float dot = 0.0f;
+    if ((hd & 3) == 0) {
+#pragma unroll 4
+      for (int d = 0; d < hd; d += 4) {
+        const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+        const float4 q4 = *reinterpret_cast<const float4 *>(qr + d);
+        dot = __fadd_rn(dot, __fmul_rn(q4.x, k4.x));
+        dot = __fadd_rn(dot, __fmul_rn(q4.y, k4.y));
+        dot = __fadd_rn(dot, __fmul_rn(q4.z, k4.z));
+        dot = __fadd_rn(dot, __fmul_rn(q4.w, k4.w));
+      }
+    } else {
+      for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qr[d], kr[d]));
+    }
+    a.scores[(size_t)(kvh * group + g) * a.max_seq + p0 + p] = __fmul_rn(dot, scale);
+  }
+}
+
+// Softmax and the weighted sum of values for one query head and a slice of
+// kPVSlice output dimensions (llama.c:566-575): max; exp; the sequential sum of
+// the exponentials; w = e/sum; then for every d the sequential sum over
+// positions of w*v.  Value rows stream through a ring of staged chunks.
+// Grid (ceil(hd/32), n_heads); needs (max_seq + kPVRing*kPVChunk*kPVSlice)
+// floats of dynamic shared memory.
+__global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
+  extern __shared__ __align__(16) float sm_v[];
   __shared__ float s_red[32];
   __shared__ float s_inv;
   pdl_launch_dependents();
   pdl_wait();
   const int tid = threadIdx.x;
-  const int h = blockIdx.x;
-  const int group = a.n_heads / a.n_kv;
-  const int kvh = h / group;
-  const int hd = a.hd, kvd = a.n_kv * hd;
-  int pos = a.step->pos;
-  if (pos < 0 || pos >= a.max_seq) return;  // flagged by the QKV epilogue
-  const int np = pos + 1;
-  float *qs = asm_;
-  float *sc = asm_ + ((hd + 3) & ~3);
-  for (int d = tid; d < hd; d += kAttnThreads) qs[d] = a.q[(size_t)h * hd + d];
-  __syncthreads();
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));  // llama.c:532
-  float mloc = -INFINITY;
-  for (int p = tid; p < np; p += kAttnThreads) {
-    const float *kp = a.kcache + (size_t)p * kvd + (size_t)kvh * hd;
-    float dot = 0.0f;
-    if ((hd & 3) == 0) {
-      for (int d = 0; d < hd; d += 4) {
-        const float4 k4 = *reinterpret_cast<const float4 *>(kp + d);
-        dot = __fadd_rn(dot, __fmul_rn(qs[d], k4.x));
-        dot = __fadd_rn(dot, __fmul_rn(qs[d + 1], k4.y));
-        dot = __fadd_rn(dot, __fmul_rn(qs[d + 2], k4.z));
-        dot = __fadd_rn(dot, __fmul_rn(qs[d + 3], k4.w));
-      }
-    } else {
-      for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qs[d], kp[d]));
-    }
-    const float s = __fmul_rn(dot, scale);
-    sc[p] = s;
-    mloc = fmaxf(mloc, s);
+  const int h = blockIdx.y;
+  const int d0 = blockIdx.x * kPVSlice;
+  const int pos = a.step->pos;
+  if (pos < 0 || pos >= a.max_seq) return;
+  const int np = pos + 1, hd = a.hd, group = a.n_heads / a.n_kv, kvh = h / group;
+  const int w = min(kPVSlice, hd - d0);
+  float *wts = sm_v;                                          // [max_seq]
+  float *ring = sm_v + (((size_t)a.max_seq + 3) & ~size_t(3));  // [kPVRing][kPVChunk][kPVSlice]
+  const float *vc = a.vcache + (size_t)kvh * a.max_seq * hd;
+  const int nchunks = (np + kPVChunk - 1) / kPVChunk;
+  // start streaming the value rows while the softmax runs
+  for (int c = 0; c < kPVRing; ++c) {
+    if (c < nchunks)
+      stage_rows(ring + (size_t)c * kPVChunk * kPVSlice, kPVSlice, vc, hd, c * kPVChunk,
+                 min((c + 1) * kPVChunk, np), d0, w, tid, kPVThreads);
+    cp_async_commit();
   }
-  const float mx = block_max<kAttnThreads>(mloc, s_red);
-  for (int p = tid; p < np; p += kAttnThreads) sc[p] = libm_expf(__fsub_rn(sc[p], mx));
+  const float *sc = a.scores + (size_t)h * a.max_seq;
+  float m = -INFINITY;
+  for (int p = tid; p < np; p += kPVThreads) {
+    const float s = sc[p];
+    wts[p] = s;
+    m = fmaxf(m, s);
+  }
+  m = block_max<kPVThreads>(m, s_red);
+  for (int p = tid; p < np; p += kPVThreads) wts[p] = libm_expf(__fsub_rn(wts[p], m));
   __syncthreads();
   if (tid == 0) {
     float sum = 0.0f;
-    for (int p = 0; p < np; ++p) sum = __fadd_rn(sum, sc[p]);
+    int p = 0;
+    for (; p + 16 <= np; p += 16) {  // loads of the group first, then the dependent adds
+      float4 e[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) e[u] = *reinterpret_cast<const float4 *>(wts + p + 4 * u);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        sum = __fadd_rn(sum, e[u].x);
+        sum = __fadd_rn(sum, e[u].y);
+        sum = __fadd_rn(sum, e[u].z);
+        sum = __fadd_rn(sum, e[u].w);
+      }
+    }
+    for (; p < np; ++p) sum = __fadd_rn(sum, wts[p]);
     s_inv = __fdiv_rn(1.0f, sum);
   }
   __syncthreads();
   const float inv = s_inv;
-  for (int p = tid; p < np; p += kAttnThreads) sc[p] = __fmul_rn(sc[p], inv);
-  __syncthreads();
-  for (int d = tid; d < hd; d += kAttnThreads) {
-    const float *vp = a.vcache + (size_t)kvh * hd + d;
-    float o = 0.0f;
-    int p = 0;
-    for (; p + 8 <= np; p += 8) {
-      float v[8];
+  for (int p = tid; p < np; p += kPVThreads) wts[p] = __fmul_rn(wts[p], inv);
+  float o = 0.0f;
+  for (int c = 0; c < nchunks; ++c) {
+    cp_async_wait<kPVRing - 1>();
+    __syncthreads();
+    const float *buf = ring + (size_t)(c % kPVRing) * kPVChunk * kPVSlice;
+    if (tid < w) {
+      const int pe = min((c + 1) * kPVChunk, np) - c * kPVChunk;
+      const float *wc = wts + (size_t)c * kPVChunk;
+      int p = 0;
+      for (; p + 8 <= pe; p += 8) {  // loads of the group first, then the dependent adds
+        float wv[8], vv[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = vp[(size_t)(p + u) * kvd];
+        for (int u = 0; u < 8; ++u) {
+          wv[u] = wc[p + u];
+          vv[u] = buf[(size_t)(p + u) * kPVSlice + tid];
+        }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) o = __fadd_rn(o, __fmul_rn(sc[p + u], v[u]));
+        for (int u = 0; u < 8; ++u) o = __fadd_rn(o, __fmul_rn(wv[u], vv[u]));
+      }
+      for (; p < pe; ++p) o = __fadd_rn(o, __fmul_rn(wc[p], buf[(size_t)p * kPVSlice + tid]));
     }
-    for (; p < np; ++p) o = __fadd_rn(o, __fmul_rn(sc[p], vp[(size_t)p * kvd]));
-    a.out[(size_t)h * hd + d] = o;
+    __syncthreads();
+    const int nc = c + kPVRing;
+    if (nc < nchunks)
+      stage_rows(ring + (size_t)(nc % kPVRing) * kPVChunk * kPVSlice, kPVSlice, vc, hd, nc * kPVChunk,
+                 min((nc + 1) * kPVChunk, np), d0, w, tid, kPVThreads);
+    cp_async_commit();
   }
+  if (tid < w) a.out[(size_t)h * hd + d0 + tid] = o;
 }
 
 // Final step bookkeeping: publish the argmax and error flags, advance the
