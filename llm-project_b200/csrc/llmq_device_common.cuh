@@ -1,0 +1,76 @@
+// llmq_device_common.cuh - device helpers shared by the CUDA translation units
+// of libllmq_cuda.so: the reference's activation-code rounding and rescale, and
+// block-wide max reductions.  Inline functions only (no globals, no kernels).
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace llmq {
+
+// ------------------------------------------------------- reference arithmetic
+// (int)lrintf(v) as the reference's x86-64 build evaluates it (cvtss2si to a
+// 64-bit long, then truncation to int), followed by the clamp to +-127
+// (quant.c:56-58, quant.c:109-111).
+__device__ __forceinline__ int8_t code_of(float v) {
+  int c;
+  if (fabsf(v) < 2147483648.0f) {
+    c = __float2int_rn(v);
+  } else if (fabsf(v) < 9.2233720368547758e18f) {  // finite, fits a long
+    c = static_cast<int>(static_cast<unsigned long long>(__float2ll_rn(v)) & 0xffffffffull);
+  } else {
+    c = 0;  // NaN / out of range: integer indefinite 0x8000000000000000, low half 0
+  }
+  c = c > 127 ? 127 : c;
+  c = c < -127 ? -127 : c;
+  return static_cast<int8_t>(c);
+}
+// as * ws[j] * (float)acc, left to right (quant.c:117)
+__device__ __forceinline__ float dequant(float as, float ws, int acc) {
+  return __fmul_rn(__fmul_rn(as, ws), __int2float_rn(acc));
+}
+
+// ------------------------------------------------------------- block helpers
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < NT / 32 ? red[lane] : v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+template <int NT>
+__device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v, unsigned long long *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < NT / 32 ? red[lane] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long w = __shfl_xor_sync(0xffffffffu, v, o);
+      v = w > v ? w : v;
+    }
+    if (lane == 0) red[0] = v;
+  }
+  __syncthreads();
+  return red[0];
+}
+
+}  // namespace llmq
