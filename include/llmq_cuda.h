@@ -264,6 +264,29 @@ int llmq_kernels_per_step(const QLlamaModel *m);
  * kernels do not overlap here.  Returns 0 or an error code. */
 int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, int max_n);
 
+/* ---- allocation-free entry point ---- */
+
+/* No counterpart in the reference (it has no GPU).  The qmatmul product
+ * (quant.c:95-120, bit-identical results) on buffers the caller already holds on
+ * the current GPU, for callers that cannot call cudaMalloc where they multiply:
+ * a host framework whose own memory pool already owns the GPU's memory, a plugin
+ * that must not change the application's device-memory accounting, or a
+ * latency-critical loop that cannot afford an allocation and the device
+ * synchronisation of the matching cudaFree.
+ *   A      device f32 [M][K]          Wq  device int8 [K][N], row-major (QTensor.q layout)
+ *   Wscale device f32 [N]             C   device f32 [M][N], written
+ *   stream a cudaStream_t (NULL: the default stream); the call only enqueues work.
+ * It allocates nothing: its scratch (split-K int32 sums and counters) is one
+ * fixed __device__ array of 513 KiB inside the library, held by every GPU that
+ * loads it until the process exits; hence N <= 131072 (larger N is rejected with
+ * LLMQ_ERR_ARG, nothing launched).  The first call on a device looks up that
+ * array's address (cudaGetSymbolAddress) with the device current; make that first
+ * call before any stream capture.  All calls share the array: calls that overlap
+ * on the GPU (other streams, other threads) race and must be serialised by the
+ * caller.  Returns 0 or an error code. */
+int qmatmul_device_noalloc(const float *A, int M, int K, const signed char *Wq, const float *Wscale, int N,
+                           float *C, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

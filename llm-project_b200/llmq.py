@@ -103,6 +103,8 @@ SIGNATURES = {
     "llmq_kernels_per_step": (C.c_int, [C.POINTER(QLlamaModel)]),
     "q_llama_set_device": (C.c_int, [C.c_int]),
     "llmq_step_profile": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, c_float_p, C.c_int]),
+    "qmatmul_device_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
+                                         C.c_void_p, C.c_void_p]),
 }
 
 _lib = None
