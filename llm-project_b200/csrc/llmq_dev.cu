@@ -246,9 +246,9 @@ int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
   const size_t tile = (size_t)kNT * m.KT;
   const size_t codes = align16((size_t)rows * m.Kpad);
   // xs holds one input row (both prologues) and later the epilogue exchange
+  // (RMSNorm prologues also keep the K squares after the row)
   size_t xs = std::max<size_t>((size_t)kNT * 4, (size_t)kThreads * 4);
-  xs = std::max<size_t>(xs, (size_t)m.K * 4);
-  (void)pro;
+  xs = std::max<size_t>(xs, (size_t)(pro == PRO_ABSMAX ? 1 : 2) * (((size_t)m.K + 3) & ~size_t(3)) * 4);
   const size_t fixed = codes + align16(xs);
   const size_t budget = (size_t)c.max_smem;
   if (fixed + 2 * (tile + 8) + 16 > budget) {
@@ -1200,3 +1200,10 @@ extern "C" LLMQ_API int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int
   }
   return rc;
 }
+
+#ifdef LLMQ_PHASE_TIMING
+// Profiling builds only: copies the phase timestamps (64 CTAs x 16 points).
+extern "C" LLMQ_API int llmq_phase_ts(unsigned long long *out) {
+  return cudaMemcpyFromSymbol(out, g_phase_ts, sizeof(unsigned long long) * 64 * 16) == cudaSuccess ? 0 : 2;
+}
+#endif

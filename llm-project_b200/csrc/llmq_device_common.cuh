@@ -73,4 +73,45 @@ __device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v
   return red[0];
 }
 
+// Sequential f32 sum acc + v[0] + v[stride] + ... + v[(n-1)*stride], one
+// rounded add after another exactly as a C loop does, with the next 8 values
+// loaded while the current 8 are added (the adds form the only dependency).
+__device__ __forceinline__ float seq_sum(const float *v, int stride, int n, float acc) {
+  int i = 0;
+  if (n >= 8) {
+    float cur[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) cur[u] = v[(size_t)u * stride];
+    for (i = 8; i + 8 <= n; i += 8) {
+      float nxt[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) nxt[u] = v[(size_t)(i + u) * stride];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, cur[u]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) cur[u] = nxt[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, cur[u]);
+  }
+  for (; i < n; ++i) acc = __fadd_rn(acc, v[(size_t)i * stride]);
+  return acc;
+}
+
+// Sequential f32 dot product acc + a[0]*b[0] + a[1]*b[sb] + ..., each product
+// and each sum rounded on its own in C order; the 8 products of a group are
+// formed back to back (independent), then added one after another.
+__device__ __forceinline__ float seq_dot(const float *a, const float *b, int sb, int n, float acc) {
+  int i = 0;
+  for (; i + 8 <= n; i += 8) {
+    float p[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) p[u] = __fmul_rn(a[i + u], b[(size_t)(i + u) * sb]);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, p[u]);
+  }
+  for (; i < n; ++i) acc = __fadd_rn(acc, __fmul_rn(a[i], b[(size_t)i * sb]));
+  return acc;
+}
+
 }  // namespace llmq

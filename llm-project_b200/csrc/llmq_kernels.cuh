@@ -16,6 +16,24 @@
 
 namespace llmq {
 
+// Phase timestamps for profiling builds (-DLLMQ_PHASE_TIMING): thread 0 of the
+// first 64 CTAs records %globaltimer at numbered points.  Compiled out otherwise.
+#ifdef LLMQ_PHASE_TIMING
+__device__ unsigned long long g_phase_ts[64][16];
+#define LLMQ_TSTAMP(i)                                                  \
+  do {                                                                  \
+    if (threadIdx.x == 0 && blockIdx.x < 64 && blockIdx.y == 0) {       \
+      unsigned long long t_;                                            \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));           \
+      g_phase_ts[blockIdx.x][i] = t_;                                   \
+    }                                                                   \
+  } while (0)
+#else
+#define LLMQ_TSTAMP(i) \
+  do {               \
+  } while (0)
+#endif
+
 constexpr int kThreads = 512;     // GEMV CTA size (16 warps)
 constexpr int kMaxRows = 8;       // rows per GEMV launch (decode uses 1)
 
@@ -197,6 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   __shared__ int s_flag;
   __shared__ int s_abort;
 
+  LLMQ_TSTAMP(0);
   const int tid = threadIdx.x;
   const int S = a.stages;
   uint8_t *stage0 = sm;
@@ -227,8 +246,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
                 kTileBytes, &bars[issued]);
     }
   }
+  LLMQ_TSTAMP(1);
   pdl_launch_dependents();
   pdl_wait();
+  LLMQ_TSTAMP(2);
 
   // ------------------------------------------------------------ prologue
   // The input rows come from the previous kernel: copied into xs with one bulk
@@ -280,47 +301,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     } else {
       load_row(a.in, 0);
     }
+    LLMQ_TSTAMP(3);
+    // The sum of squares (rmsnorm.c:15): the products are independent, so all
+    // threads form them; the adds stay one sequential chain in thread 0.
+    float *sq = xs + ((K + 3) & ~3);
+    for (int k = tid; k < K; k += kThreads) sq[k] = __fmul_rn(xs[k], xs[k]);
+    __syncthreads();
     if (tid == 0) {
-      // The sequential sum of squares: one dependent chain of adds, like the
-      // reference; the next 16 values are loaded while the current 16 are added.
-      float ms = 0.0f;
-      int k = 0;
-      if ((K & 3) == 0 && K >= 16) {
-        const float4 *v4 = reinterpret_cast<const float4 *>(xs);
-        const int n4 = K >> 2;
-        float4 b0 = v4[0], b1 = v4[1], b2 = v4[2], b3 = v4[3];
-        int i = 4;
-#define LLMQ_SQ_ACC(b)                          \
-  ms = __fadd_rn(ms, __fmul_rn((b).x, (b).x));  \
-  ms = __fadd_rn(ms, __fmul_rn((b).y, (b).y));  \
-  ms = __fadd_rn(ms, __fmul_rn((b).z, (b).z));  \
-  ms = __fadd_rn(ms, __fmul_rn((b).w, (b).w))
-        for (;;) {
-          const bool more = i + 4 <= n4;
-          float4 c0, c1, c2, c3;
-          if (more) {
-            c0 = v4[i];
-            c1 = v4[i + 1];
-            c2 = v4[i + 2];
-            c3 = v4[i + 3];
-          }
-          LLMQ_SQ_ACC(b0);
-          LLMQ_SQ_ACC(b1);
-          LLMQ_SQ_ACC(b2);
-          LLMQ_SQ_ACC(b3);
-          if (!more) break;
-          b0 = c0;
-          b1 = c1;
-          b2 = c2;
-          b3 = c3;
-          i += 4;
-        }
-#undef LLMQ_SQ_ACC
-        k = i * 4;
-      }
-      for (; k < K; ++k) ms = __fadd_rn(ms, __fmul_rn(xs[k], xs[k]));
+      float ms = seq_sum(sq, 1, K, 0.0f);
       ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
       s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
+      LLMQ_TSTAMP(4);
     }
     __syncthreads();
     const float r = s_r;
@@ -338,6 +329,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   }
   __syncthreads();
 
+  LLMQ_TSTAMP(5);
   // --------------------------------------------------------------- main loop
   const int col = tid % kNT;
   const int part = tid / kNT;
@@ -505,7 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     }
     return;
   }
+  LLMQ_TSTAMP(6);
   if (n > 0) flush(cur);
+  LLMQ_TSTAMP(7);
 }
 
 // --------------------------------------------------------------- attention
@@ -608,20 +602,7 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const AttnArgs a)
     if (p0 + p >= p1) continue;
     const float *kr = ks + (size_t)p * stride;
     const float *qr = qs + (size_t)g * hd4;
-    float dot = 0.0f;
-    if ((hd & 3) == 0) {
-#pragma unroll 4
-      for (int d = 0; d < hd; d += 4) {
-        const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
-        const float4 q4 = *reinterpret_cast<const float4 *>(qr + d);
-        dot = __fadd_rn(dot, __fmul_rn(q4.x, k4.x));
-        dot = __fadd_rn(dot, __fmul_rn(q4.y, k4.y));
-        dot = __fadd_rn(dot, __fmul_rn(q4.z, k4.z));
-        dot = __fadd_rn(dot, __fmul_rn(q4.w, k4.w));
-      }
-    } else {
-      for (int d = 0; d < hd; ++d) dot = __fadd_rn(dot, __fmul_rn(qr[d], kr[d]));
-    }
+    const float dot = seq_dot(qr, kr, 1, hd, 0.0f);  // llama.c:561
     a.scores[(size_t)(kvh * group + g) * a.max_seq + p0 + p] = __fmul_rn(dot, scale);
   }
 }
@@ -643,6 +624,7 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
   const int d0 = blockIdx.x * kPVSlice;
   const int pos = a.step->pos;
   if (pos < 0 || pos >= a.max_seq) return;
+  LLMQ_TSTAMP(0);
   const int np = pos + 1, hd = a.hd, group = a.n_heads / a.n_kv, kvh = h / group;
   const int w = min(kPVSlice, hd - d0);
   float *wts = sm_v;                                          // [max_seq]
@@ -664,27 +646,16 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
     m = fmaxf(m, s);
   }
   m = block_max<kPVThreads>(m, s_red);
+  LLMQ_TSTAMP(1);
   for (int p = tid; p < np; p += kPVThreads) wts[p] = libm_expf(__fsub_rn(wts[p], m));
   __syncthreads();
+  LLMQ_TSTAMP(2);
   if (tid == 0) {
-    float sum = 0.0f;
-    int p = 0;
-    for (; p + 16 <= np; p += 16) {  // loads of the group first, then the dependent adds
-      float4 e[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) e[u] = *reinterpret_cast<const float4 *>(wts + p + 4 * u);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        sum = __fadd_rn(sum, e[u].x);
-        sum = __fadd_rn(sum, e[u].y);
-        sum = __fadd_rn(sum, e[u].z);
-        sum = __fadd_rn(sum, e[u].w);
-      }
-    }
-    for (; p < np; ++p) sum = __fadd_rn(sum, wts[p]);
+    const float sum = seq_sum(wts, 1, np, 0.0f);  // llama.c:567
     s_inv = __fdiv_rn(1.0f, sum);
   }
   __syncthreads();
+  LLMQ_TSTAMP(3);
   const float inv = s_inv;
   for (int p = tid; p < np; p += kPVThreads) wts[p] = __fmul_rn(wts[p], inv);
   float o = 0.0f;
@@ -692,22 +663,9 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
     cp_async_wait<kPVRing - 1>();
     __syncthreads();
     const float *buf = ring + (size_t)(c % kPVRing) * kPVChunk * kPVSlice;
-    if (tid < w) {
-      const int pe = min((c + 1) * kPVChunk, np) - c * kPVChunk;
-      const float *wc = wts + (size_t)c * kPVChunk;
-      int p = 0;
-      for (; p + 8 <= pe; p += 8) {  // loads of the group first, then the dependent adds
-        float wv[8], vv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          wv[u] = wc[p + u];
-          vv[u] = buf[(size_t)(p + u) * kPVSlice + tid];
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) o = __fadd_rn(o, __fmul_rn(wv[u], vv[u]));
-      }
-      for (; p < pe; ++p) o = __fadd_rn(o, __fmul_rn(wc[p], buf[(size_t)p * kPVSlice + tid]));
-    }
+    const int pe = min((c + 1) * kPVChunk, np) - c * kPVChunk;
+    const float *wc = wts + (size_t)c * kPVChunk;
+    if (tid < w) o = seq_dot(wc, buf + tid, kPVSlice, pe, o);  // llama.c:574, in position order
     __syncthreads();
     const int nc = c + kPVRing;
     if (nc < nchunks)
@@ -715,6 +673,7 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
                  min((nc + 1) * kPVChunk, np), d0, w, tid, kPVThreads);
     cp_async_commit();
   }
+  LLMQ_TSTAMP(4);
   if (tid < w) a.out[(size_t)h * hd + d0 + tid] = o;
 }
 
