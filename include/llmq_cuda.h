@@ -254,8 +254,14 @@ int llmq_expf_device(const float *x, float *y, long long n);
 int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int iters, float *ms_per_launch,
                     double *bytes_per_launch);
 
-/* Kernels launched by one decode step (5 per layer + 2). */
+/* Kernels launched by one decode step (6 per layer + 2). */
 int llmq_kernels_per_step(const QLlamaModel *m);
+
+/* Times `iters` device-resident products C(M, N) = A(M, K) x W on the path
+ * qmatmul uses (int8 GEMV for M <= 8, tcgen05 tensor cores for larger M), with
+ * W tiled once and seeded A resident in device memory.  *ms receives the mean
+ * time per product.  Returns 0 or an error code. */
+int llmq_bench_qmatmul(const QTensor *W, int M, int iters, float *ms);
 
 /* Runs one decode step of `token` at kv->len outside the CUDA graph, kernel by
  * kernel with CUDA events between the launches, writes each kernel's time in

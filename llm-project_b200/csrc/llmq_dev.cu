@@ -14,6 +14,7 @@
 
 #include "llmq_internal.h"
 #include "llmq_kernels.cuh"
+#include "llmq_tc_gemm.cuh"
 
 using namespace llmq;
 
@@ -66,6 +67,11 @@ struct DevCtx {
   uint8_t *wraw = nullptr, *wtile = nullptr;
   float *wscale = nullptr;
   size_t wraw_n = 0, wtile_n = 0, wscale_n = 0;
+  // tensor-core path scratch: activation codes, row scales, split-slab partials
+  int8_t *tc_codes = nullptr;
+  float *tc_as = nullptr;
+  int *tc_part = nullptr;
+  size_t tc_codes_n = 0, tc_as_n = 0, tc_part_n = 0;
 };
 
 DevCtx g_ctx[kMaxDevices];
@@ -152,6 +158,8 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea
                          : cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   ea = ea != cudaSuccess ? ea : cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  ea = ea != cudaSuccess ? ea : cudaFuncSetAttribute(k_tc_gemm<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  ea = ea != cudaSuccess ? ea : cudaFuncSetAttribute(k_tc_gemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
   if (ea != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
     return nullptr;
@@ -300,6 +308,49 @@ cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, b
   cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
   return p.kt == 128 ? cudaLaunchKernelEx(&cfg, k_gemv<PRO, EPI, MR, 128>, a)
                      : cudaLaunchKernelEx(&cfg, k_gemv<PRO, EPI, MR, 64>, a);
+}
+
+// ---------------------------------------------------- tensor-core GEMM launch
+// Rows [r0, r0 + rows) of A (rows <= 128) times the tiled matrix m into out.
+int launch_tc(DevCtx &c, const Mat &m, const float *dA, int rows, float *out, cudaStream_t st) {
+  const size_t SB = (size_t)(kNT + kTcRows) * m.KT;
+  int S = static_cast<int>(((size_t)c.max_smem - 1024) / SB);
+  S = std::min(S, kTcMaxStages);
+  if (S < 2) {
+    llmq_set_error(LLMQ_ERR_ARG, "tensor-core GEMM: tile does not fit in shared memory");
+    return 0;
+  }
+  const long long T = (long long)m.n_slabs * m.n_ktiles;
+  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(T, c.num_sms)));
+  if (!ensure(&c.tc_codes, &c.tc_codes_n, (size_t)m.Kpad * kTcRows, false) ||
+      !ensure(&c.tc_as, &c.tc_as_n, (size_t)kTcRows, false) ||
+      !ensure(&c.tc_part, &c.tc_part_n, (size_t)c.num_sms * 2 * kTcRows * kNT, false) ||
+      !ensure(&c.cnt, &c.cnt_n, (size_t)m.n_slabs, true))
+    return 0;
+  k_act_codes<<<kTcRows, 256, 0, st>>>(dA, rows, m.K, m.Kpad, m.KT, c.tc_codes, c.tc_as);
+  CK(cudaGetLastError());
+  TcArgs a{};
+  a.w = m.w;
+  a.acodes = c.tc_codes;
+  a.as = c.tc_as;
+  a.ws = m.ws;
+  a.N = m.N;
+  a.Npad = m.Npad;
+  a.n_slabs = m.n_slabs;
+  a.n_ktiles = m.n_ktiles;
+  a.stages = S;
+  a.rows = rows;
+  a.part = c.tc_part;
+  a.cnt = c.cnt;
+  a.err = c.err;
+  a.out = out;
+  const size_t smem = (size_t)S * SB;
+  if (m.KT == 128)
+    k_tc_gemm<128><<<grid, kTcThreads, smem, st>>>(a);
+  else
+    k_tc_gemm<64><<<grid, kTcThreads, smem, st>>>(a);
+  CK(cudaGetLastError());
+  return 1;
 }
 
 size_t scores_smem(const AttnArgs &a) {
@@ -924,15 +975,20 @@ int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
                                                          m.Npad, kNT, m.KT, c->wtile);
     CK(cudaGetLastError());
   }
-  for (int r0 = 0; r0 < M; r0 += rows_per) {
-    GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
-    a.rows = std::min(rows_per, M - r0);
-    a.in = c->dA + (size_t)r0 * K;
-    a.out = c->dC + (size_t)r0 * N;
-    if (many)
-      CK((launch_gemv<PRO_ABSMAX, EPI_PLAIN, 8>(a, plan, st, false)));
-    else
-      CK((launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, plan, st, false)));
+  if (M > 8) {  // tensor cores, 128 rows per launch
+    for (int r0 = 0; r0 < M; r0 += kTcRows)
+      if (!launch_tc(*c, m, c->dA + (size_t)r0 * K, std::min(kTcRows, M - r0), c->dC + (size_t)r0 * N, st)) return 0;
+  } else {
+    for (int r0 = 0; r0 < M; r0 += rows_per) {
+      GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
+      a.rows = std::min(rows_per, M - r0);
+      a.in = c->dA + (size_t)r0 * K;
+      a.out = c->dC + (size_t)r0 * N;
+      if (many)
+        CK((launch_gemv<PRO_ABSMAX, EPI_PLAIN, 8>(a, plan, st, false)));
+      else
+        CK((launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, plan, st, false)));
+    }
   }
   CK(cudaMemcpyAsync(C, c->dC, (size_t)M * N * sizeof(float), cudaMemcpyDeviceToHost, st));
   int flags = 0;
@@ -1207,3 +1263,79 @@ extern "C" LLMQ_API int llmq_phase_ts(unsigned long long *out) {
   return cudaMemcpyFromSymbol(out, g_phase_ts, sizeof(unsigned long long) * 64 * 16) == cudaSuccess ? 0 : 2;
 }
 #endif
+
+// Times `iters` device-resident products C(M, N) = A(M, K) x W on the path
+// qmatmul takes (GEMV for M <= 8, tensor cores above), with W tiled once and A,
+// C resident; random A.  *ms receives the mean time per product.
+extern "C" LLMQ_API int llmq_bench_qmatmul(const QTensor *W, int M, int iters, float *ms) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevCtx *c = get_ctx();
+  if (!c) return q_llama_last_error();
+  if (M <= 0 || iters <= 0 || !W || W->rows <= 0 || W->cols <= 0) {
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_bench_qmatmul: bad arguments");
+    return LLMQ_ERR_ARG;
+  }
+  Mat m;
+  if (!build_plain(m, *W)) return q_llama_last_error();
+  const int K = W->rows, N = W->cols;
+  std::vector<float> hA((size_t)M * K);
+  uint64_t st64 = 0x9E3779B97F4A7C15ull;
+  for (float &v : hA) {
+    st64 ^= st64 << 13;
+    st64 ^= st64 >> 7;
+    st64 ^= st64 << 17;
+    v = (float)((int64_t)(st64 >> 11) - (1ll << 52)) * 0x1p-52f;
+  }
+  float *dA = nullptr, *dC = nullptr;
+  int rc = LLMQ_OK;
+  if (cudaMalloc(&dA, hA.size() * 4) != cudaSuccess || cudaMalloc(&dC, (size_t)M * N * 4) != cudaSuccess ||
+      cudaMemcpy(dA, hA.data(), hA.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      !ensure(&c->acc, &c->acc_n, (size_t)8 * m.Npad, true) || !ensure(&c->cnt, &c->cnt_n, (size_t)m.n_slabs, true)) {
+    llmq_set_error(LLMQ_ERR_OOM, "llmq_bench_qmatmul: allocation failed");
+    rc = LLMQ_ERR_OOM;
+  }
+  GemvPlan plan;
+  if (rc == LLMQ_OK && M <= 8 && !plan_gemv(*c, m, PRO_ABSMAX, M == 1 ? 1 : 8, plan)) rc = q_llama_last_error();
+  cudaStream_t st = c->stream;
+  auto once = [&]() -> int {
+    if (M > 8) {
+      for (int r0 = 0; r0 < M; r0 += kTcRows)
+        if (!launch_tc(*c, m, dA + (size_t)r0 * K, std::min(kTcRows, M - r0), dC + (size_t)r0 * N, st)) return 0;
+      return 1;
+    }
+    GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
+    a.rows = M;
+    a.in = dA;
+    a.out = dC;
+    return (M == 1 ? launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, plan, st, false)
+                   : launch_gemv<PRO_ABSMAX, EPI_PLAIN, 8>(a, plan, st, false)) == cudaSuccess;
+  };
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (rc == LLMQ_OK) {
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    for (int i = 0; i < 3 && rc == LLMQ_OK; ++i)
+      if (!once()) rc = LLMQ_ERR_CUDA;
+    cudaEventRecord(e0, st);
+    for (int i = 0; i < iters && rc == LLMQ_OK; ++i)
+      if (!once()) rc = LLMQ_ERR_CUDA;
+    cudaEventRecord(e1, st);
+    if (cudaStreamSynchronize(st) != cudaSuccess) rc = LLMQ_ERR_CUDA;
+    float t = 0.0f;
+    cudaEventElapsedTime(&t, e0, e1);
+    *ms = t / iters;
+    int flags = 0;
+    cudaMemcpy(&flags, c->err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (flags) {
+      cudaMemset(c->err, 0, 16);
+      llmq_set_error(LLMQ_ERR_CUDA, "llmq_bench_qmatmul: device error flags 0x%x", flags);
+      rc = LLMQ_ERR_CUDA;
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+  }
+  cudaFree(dA);
+  cudaFree(dC);
+  free_mat(m);
+  return rc;
+}

@@ -105,6 +105,7 @@ SIGNATURES = {
     "llmq_step_profile": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, c_float_p, C.c_int]),
     "qmatmul_device_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                          C.c_void_p, C.c_void_p]),
+    "llmq_bench_qmatmul": (C.c_int, [C.POINTER(QTensor), C.c_int, C.c_int, c_float_p]),
 }
 
 _lib = None

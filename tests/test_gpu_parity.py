@@ -59,7 +59,10 @@ def test_dequantize_bit_exact(lib, orc):
 # ----------------------------------------------------------------- qmatmul
 @pytest.mark.parametrize("M,K,N", [(1, 1, 1), (1, 16, 256), (2, 37, 19), (3, 100, 300), (1, 288, 32000),
                                    (8, 768, 288), (9, 64, 1000), (17, 288, 96), (1, 4096, 4096),
-                                   (1, 14336, 4096), (4, 4096, 1024)])
+                                   (1, 14336, 4096), (4, 4096, 1024),
+                                   # tcgen05 tensor-core path (M > 8): one and several 128-row blocks
+                                   (64, 4096, 4096), (128, 4096, 1024), (200, 768, 300), (256, 4096, 4096), (64, 14336, 1024),
+                                   (33, 37, 19), (64, 4096, 14336)])
 def test_qmatmul_bit_exact(lib, orc, M, K, N):
     rng = np.random.default_rng(M * 7919 + K * 31 + N)
     A = rng.standard_normal((M, K)).astype(np.float32)
@@ -74,8 +77,8 @@ def test_qmatmul_golden_edges(lib):
         assert bits_equal(gpu_qmatmul(lib, d["A"], d["q"], d["scale"]), d["C"]), name
 
 
-def test_qmatmul_weight_cache_tracks_contents(lib, orc):
-    """A cached device copy is dropped when the QTensor is re-quantised."""
+def test_qmatmul_sees_weights_rewritten_in_place(lib, orc):
+    """A QTensor re-quantised in place between calls is seen by the next qmatmul."""
     t = lib.qtensor_create(64, 40)
     rng = np.random.default_rng(8)
     A = rng.standard_normal((1, 64)).astype(np.float32)
