@@ -271,6 +271,7 @@ def run_ours(args, rank, world):
         "roofline": roofline,
         "cpu_baseline": cpu,
         "step_profile": step_profile,
+        "gemv_sweep": gemv_sweep(lib, [1, 64], hbm_peak) if args.workload == "8b" else None,
         "gpu_launches": K * int(lib.llmq_kernels_per_step(C.byref(m))),
         "clocks": clk.summary(),
     }
@@ -278,6 +279,54 @@ def run_ours(args, rank, world):
     lib.q_llama_model_free(C.byref(m))
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+SWEEP_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]  # (out, in)
+
+
+def gemv_sweep(lib, Ms, hbm_peak, iters=20):
+    """isolated int8 products on uniform int8 codes with scales in
+    [1e-3, 1e-2), device-resident A; GB/s of algorithmic bytes and % of HBM."""
+    rows = []
+    for out_f, in_f in SWEEP_SHAPES:
+        t = lib.qtensor_create(in_f, out_f)  # reference layout: rows = in, cols = out
+        lib.llmq_synth_qtensor(C.byref(t), 4321)
+        for M in Ms:
+            ms = C.c_float()
+            if lib.llmq_bench_qmatmul(C.byref(t), M, iters, C.byref(ms)) != 0:
+                llmq.check(lib)
+            K, N = in_f, out_f
+            by = K * N + 4 * N + 4 * M * K + 4 * M * N
+            gbs = by / (ms.value / 1e3) / 1e9
+            rows.append({"out_x_in": f"{out_f}x{in_f}", "M": M, "us": round(ms.value * 1e3, 2),
+                         "GBps": round(gbs, 1), "hbm_frac": round(gbs / hbm_peak, 3),
+                         "TOPS": round(2.0 * M * K * N / (ms.value / 1e3) / 1e12, 1)})
+        lib.qtensor_free(C.byref(t))
+    return rows
+
+
+def run_sweep(args):
+    lib = llmq.load()
+    if lib.q_llama_set_device(int(os.environ.get("LOCAL_RANK", "0"))) != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    peak = hbm_peak_gbs()
+    rows = gemv_sweep(lib, [1, 8, 64, 256], peak)
+    m1 = sorted(r["GBps"] for r in rows if r["M"] == 1)
+    print(json.dumps({"metric": "int8 W8A8 matvec/matmul GB/s (configs[1] sweep, M=1 median)",
+                      "value": m1[len(m1) // 2], "unit": "GB/s", "n_gpus": 1, "higher_is_better": True,
+                      "dtype": "int8", "data": "synthetic", "hbm_peak_gbs": peak,
+                      "config": {"workload": "isolated int8 per-channel products, shapes (out x in) "
+                                             + ", ".join(f"{o}x{i}" for o, i in SWEEP_SHAPES)
+                                             + "; M = 1, 8, 64, 256",
+                                 "path": "k_gemv (dp4a) for M <= 8, k_tc_gemm (tcgen05.mma.kind::i8) above"},
+                      "sweep": rows}), flush=True)
+
+
+def hbm_peak_gbs():
+    try:
+        return float(json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 6650.0
 
 
 def profiled_traffic():
@@ -388,7 +437,7 @@ def main():
     ap.add_argument("--steps", type=int, default=240)
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="8b")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["sweep"], default="8b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (profiling runs)")
     args = ap.parse_args()
@@ -402,7 +451,10 @@ def main():
         import torch.distributed as dist
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
     try:
-        if args.impl == "reference":
+        if args.workload == "sweep":
+            if rank == 0 and args.impl == "ours":
+                run_sweep(args)
+        elif args.impl == "reference":
             run_reference(args, rank, world)
         else:
             run_ours(args, rank, world)
