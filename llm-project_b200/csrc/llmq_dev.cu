@@ -67,11 +67,12 @@ struct DevCtx {
   uint8_t *wraw = nullptr, *wtile = nullptr;
   float *wscale = nullptr;
   size_t wraw_n = 0, wtile_n = 0, wscale_n = 0;
-  // tensor-core path scratch: activation codes, row scales, split-slab partials
+  // tensor-core path scratch: activation codes, row scales, split-K sums and
+  // arrival counters (both kept zero between launches)
   int8_t *tc_codes = nullptr;
   float *tc_as = nullptr;
-  int *tc_part = nullptr;
-  size_t tc_codes_n = 0, tc_as_n = 0, tc_part_n = 0;
+  int *tc_acc = nullptr, *tc_cnt = nullptr;
+  size_t tc_codes_n = 0, tc_as_n = 0, tc_acc_n = 0, tc_cnt_n = 0;
 };
 
 DevCtx g_ctx[kMaxDevices];
@@ -311,25 +312,26 @@ cudaError_t launch_gemv(const GemvArgs &a, const GemvPlan &p, cudaStream_t st, b
 }
 
 // ---------------------------------------------------- tensor-core GEMM launch
-// Rows [r0, r0 + rows) of A (rows <= 128) times the tiled matrix m into out.
-int launch_tc(DevCtx &c, const Mat &m, const float *dA, int rows, float *out, cudaStream_t st) {
-  const size_t SB = (size_t)(kNT + kTcRows) * m.KT;
-  int S = static_cast<int>(((size_t)c.max_smem - 1024) / SB);
-  S = std::min(S, kTcMaxStages);
-  if (S < 2) {
-    llmq_set_error(LLMQ_ERR_ARG, "tensor-core GEMM: tile does not fit in shared memory");
+// Activation codes of `rows` rows of dA (row stride m.K) for the tiled matrix m.
+int launch_act_codes(DevCtx &c, const Mat &m, const float *dA, int rows, cudaStream_t st) {
+  const int n_rb = (rows + kTcRows - 1) / kTcRows;
+  if (!ensure(&c.tc_codes, &c.tc_codes_n, (size_t)m.Kpad * kTcRows * n_rb, false) ||
+      !ensure(&c.tc_as, &c.tc_as_n, (size_t)n_rb * kTcRows, false))
     return 0;
-  }
-  const long long T = (long long)m.n_slabs * m.n_ktiles;
-  const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(T, c.num_sms)));
-  if (!ensure(&c.tc_codes, &c.tc_codes_n, (size_t)m.Kpad * kTcRows, false) ||
-      !ensure(&c.tc_as, &c.tc_as_n, (size_t)kTcRows, false) ||
-      !ensure(&c.tc_part, &c.tc_part_n, (size_t)c.num_sms * 2 * kTcRows * kNT, false) ||
-      !ensure(&c.cnt, &c.cnt_n, (size_t)m.n_slabs, true))
-    return 0;
-  k_act_codes<<<kTcRows, 256, 0, st>>>(dA, rows, m.K, m.Kpad, m.KT, c.tc_codes, c.tc_as);
+  k_act_codes<<<rows, 256, 0, st>>>(dA, rows, m.K, m.Kpad, m.KT, c.tc_codes, c.tc_as);
   CK(cudaGetLastError());
-  TcArgs a{};
+  return 1;
+}
+
+// Fills a TcArgs for `rows` activation rows (codes and scales as written by
+// launch_act_codes) times the tiled matrix m; the split count keeps the grid
+// within two CTAs per SM.
+int plan_tc(DevCtx &c, const Mat &m, int rows, TcArgs &a) {
+  const size_t SB = (size_t)(kNT + kTcRows) * m.KT;
+  const int n_rb = (rows + kTcRows - 1) / kTcRows;
+  const int tiles = m.n_slabs * n_rb;
+  const int splits = std::max(1, std::min(m.n_ktiles, (2 * c.num_sms) / tiles));
+  a = TcArgs{};
   a.w = m.w;
   a.acodes = c.tc_codes;
   a.as = c.tc_as;
@@ -338,19 +340,48 @@ int launch_tc(DevCtx &c, const Mat &m, const float *dA, int rows, float *out, cu
   a.Npad = m.Npad;
   a.n_slabs = m.n_slabs;
   a.n_ktiles = m.n_ktiles;
-  a.stages = S;
+  a.n_rb = n_rb;
+  a.splits = splits;
+  a.stages = (int)std::max<size_t>((kTcStageBytes + SB - 1) / SB, std::min<size_t>(kTcMaxStages, kTcRingBytes / SB));
   a.rows = rows;
-  a.part = c.tc_part;
-  a.cnt = c.cnt;
   a.err = c.err;
-  a.out = out;
-  const size_t smem = (size_t)S * SB;
-  if (m.KT == 128)
-    k_tc_gemm<128><<<grid, kTcThreads, smem, st>>>(a);
-  else
-    k_tc_gemm<64><<<grid, kTcThreads, smem, st>>>(a);
-  CK(cudaGetLastError());
+  if (splits > 1 && (!ensure(&c.tc_acc, &c.tc_acc_n, (size_t)rows * m.Npad, true) ||
+                     !ensure(&c.tc_cnt, &c.tc_cnt_n, (size_t)tiles, true)))
+    return 0;
+  a.acc = c.tc_acc;
+  a.cnt = c.tc_cnt;
   return 1;
+}
+
+int launch_tc_gemm(const TcArgs &a, int KT, cudaStream_t st, bool pdl) {
+  const size_t smem = (size_t)a.stages * (kNT + kTcRows) * KT;
+  const dim3 grid(a.n_slabs * a.n_rb * a.splits);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  CK(KT == 128 ? cudaLaunchKernelEx(&cfg, k_tc_gemm<128>, a) : cudaLaunchKernelEx(&cfg, k_tc_gemm<64>, a));
+  return 1;
+}
+
+// rows rows of dA (row stride m.K) times the tiled matrix m, epilogue `epi`
+// into out (row stride ld).
+int launch_tc(DevCtx &c, const Mat &m, const float *dA, int rows, float *out, int ld, int epi, const float *bias,
+              cudaStream_t st) {
+  if (!launch_act_codes(c, m, dA, rows, st)) return 0;
+  TcArgs a;
+  if (!plan_tc(c, m, rows, a)) return 0;
+  a.epi = epi;
+  a.bias = bias;
+  a.out = out;
+  a.ld = ld;
+  return launch_tc_gemm(a, m.KT, st, false);
 }
 
 size_t scores_smem(const AttnArgs &a) {
@@ -975,9 +1006,8 @@ int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
                                                          m.Npad, kNT, m.KT, c->wtile);
     CK(cudaGetLastError());
   }
-  if (M > 8) {  // tensor cores, 128 rows per launch
-    for (int r0 = 0; r0 < M; r0 += kTcRows)
-      if (!launch_tc(*c, m, c->dA + (size_t)r0 * K, std::min(kTcRows, M - r0), c->dC + (size_t)r0 * N, st)) return 0;
+  if (M > 8) {  // tensor cores
+    if (!launch_tc(*c, m, c->dA, M, c->dC, N, TC_PLAIN, nullptr, st)) return 0;
   } else {
     for (int r0 = 0; r0 < M; r0 += rows_per) {
       GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
@@ -1299,9 +1329,7 @@ extern "C" LLMQ_API int llmq_bench_qmatmul(const QTensor *W, int M, int iters, f
   cudaStream_t st = c->stream;
   auto once = [&]() -> int {
     if (M > 8) {
-      for (int r0 = 0; r0 < M; r0 += kTcRows)
-        if (!launch_tc(*c, m, dA + (size_t)r0 * K, std::min(kTcRows, M - r0), dC + (size_t)r0 * N, st)) return 0;
-      return 1;
+      return launch_tc(*c, m, dA, M, dC, N, TC_PLAIN, nullptr, st);
     }
     GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
     a.rows = M;

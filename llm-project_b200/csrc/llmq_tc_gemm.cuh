@@ -7,7 +7,7 @@
 // 8 rows x 16 bytes per 128-byte core matrix):
 //   B, the weights: the same tiles as k_gemv, [KT/16][256 columns][16 B], so
 //     8-column groups are 128 B apart (SBO) and 16-k chunks 4096 B apart (LBO);
-//   A, the activation codes: written by k_act_codes as [ktile][KT/16][128 rows][16 B],
+//   A, the activation codes: written by k_act_codes as [row block][ktile][KT/16][128 rows][16 B],
 //     so 8-row groups are 128 B apart and 16-k chunks 2048 B apart.
 // One tcgen05.mma covers M=128 rows, N=256 columns (one slab), K=32.
 #pragma once
@@ -19,6 +19,8 @@ namespace llmq {
 constexpr int kTcRows = 128;     // MMA M; activation rows are zero-padded to it
 constexpr int kTcThreads = 128;  // 4 warps, one per 32 TMEM lanes (rows)
 constexpr int kTcMaxStages = 8;
+constexpr int kTcRingBytes = 98304;  // ring per CTA: two CTAs (and 2 x 256 TMEM columns) per SM
+constexpr int kTcStageBytes = 64 * (256 + 1) * 4;  // the epilogue stages 64 accumulator rows in the ring
 constexpr uint32_t kTcTmemCols = 256;  // one 128 x 256 int32 accumulator
 
 // Instruction descriptor: D int32 (2 << 4), A and B signed int8 (1 << 7, 1 << 10),
@@ -65,70 +67,161 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, int v[32]) {
 }
 
 // ---------------------------------------------------------------- act codes
-// Per-row activation quantisation (quant.c:104-113) for rows [0, rows), written
-// as tcgen05 A tiles; rows [rows, 128) get zero codes.  One CTA per row.
+// Activation codes of row m live in 128-row block m / 128, laid out as tcgen05
+// A tiles: [block][ktile][KT/16][128 rows][16 B] (block stride 128 * Kpad).
+__device__ __forceinline__ size_t tc_code_offset(int m, int chunk, int Kpad, int KT) {
+  const int rb = m / kTcRows, mm = m - rb * kTcRows;
+  const int per_tile = KT / 16;
+  const int kt = chunk / per_tile, kc = chunk - kt * per_tile;
+  return (size_t)rb * kTcRows * Kpad + (((size_t)kt * per_tile + kc) * kTcRows + mm) * 16;
+}
+
+// Codes of 16 consecutive values x[0..16) (k >= K gives 0) times `inv`
+// (quant.c:108-112), packed little-endian into one 16-byte chunk.
+__device__ __forceinline__ int4 tc_pack16(const float *x, int k0, int K, float inv) {
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int k = k0 + q * 4 + b;
+      const int8_t c = k < K ? code_of(__fmul_rn(x[k], inv)) : 0;
+      v |= (uint32_t)(uint8_t)c << (8 * b);
+    }
+    w[q] = v;
+  }
+  return make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);
+}
+
+// Per-row activation quantisation (quant.c:104-113) of rows [0, rows) of a
+// (row stride K), written as tcgen05 A tiles.  One CTA per row.
 __global__ void __launch_bounds__(256) k_act_codes(const float *a, int rows, int K, int Kpad, int KT, int8_t *codes,
                                                    float *as_out) {
   __shared__ float s_red[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int m = blockIdx.x;
   const int tid = threadIdx.x;
-  float as = 1.0f, inv = 1.0f;
   const float *row = a + (size_t)m * K;
-  if (m < rows) {
-    float mx = 0.0f;
-    for (int k = tid; k < K; k += 256) mx = fmaxf(mx, fabsf(row[k]));
-    mx = block_max<256>(mx, s_red);
-    as = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
-    inv = __fdiv_rn(1.0f, as);
-    if (tid == 0) as_out[m] = as;
-  }
-  const int chunks_per_tile = KT / 16;
-  for (int k = tid; k < Kpad; k += 256) {
-    const int8_t c = (m < rows && k < K) ? code_of(__fmul_rn(row[k], inv)) : 0;
-    const int kt = k / KT, kc = (k % KT) / 16, kb = k % 16;
-    codes[(((size_t)kt * chunks_per_tile + kc) * kTcRows + m) * 16 + kb] = c;
-  }
+  float mx = 0.0f;
+  for (int k = tid; k < K; k += 256) mx = fmaxf(mx, fabsf(row[k]));
+  mx = block_max<256>(mx, s_red);
+  const float as = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, as);
+  if (tid == 0) as_out[m] = as;
+  for (int ch = tid; ch < Kpad / 16; ch += 256)
+    *reinterpret_cast<int4 *>(codes + tc_code_offset(m, ch, Kpad, KT)) = tc_pack16(row, ch * 16, K, inv);
 }
 
 // ------------------------------------------------------------------- GEMM
-struct TcArgs {
-  const uint8_t *w;       // weight tiles, as for k_gemv
-  const int8_t *acodes;   // [n_ktiles][KT/16][128][16]
-  const float *as;        // per-row activation scales [rows]
-  const float *ws;        // per physical column scale [Npad]
-  int N, Npad, n_slabs, n_ktiles, stages, rows;
-  int *part;              // [gridDim.x][2][128][256] int32 partial sums of split slabs
-  int *cnt;               // [n_slabs], zero before and after
-  int *err;
-  float *out;             // [rows][N]
+// Epilogues applied to y = a_scale[m] * w_scale[p] * acc (quant.c:117) of
+// physical column p of the tiled matrix.
+enum TcEpilogue : int {
+  TC_PLAIN = 0,   // out[m][p] = y                                  (qmatmul)
+  TC_BIAS = 1,    // out[m][p] = y + bias[p]                        (q/k/v, llama.c:546-548)
+  TC_RESID = 2,   // out[m][p] += y                                 (Wo, W2: llama.c:578, 589)
+  TC_SWIGLU = 3,  // slab = 128 gate + 128 up columns: out[m][slab*128 + c] = SiLU(gate) * up (llama.c:583-587)
+  TC_LOGITS = 4   // TC_PLAIN plus the first maximum of each row into argmax[m]   (sampler.c:8-21)
 };
 
-// Which of CTA c's two partial-sum slots holds slab s: 0 if s is the slab of
-// the CTA's first tile, else 1.
-__device__ __forceinline__ int tc_slot(long long c, long long s, long long T, long long G, long long nk) {
-  return ((c * T / G) / nk) == s ? 0 : 1;
+struct TcArgs {
+  const uint8_t *w;       // weight tiles, as for k_gemv
+  const int8_t *acodes;   // see tc_code_offset
+  const float *as;        // per-row activation scales [rows]
+  const float *ws;        // per physical column scale [Npad]
+  const float *bias;      // TC_BIAS, physical order
+  int N;                  // valid physical columns (TC_SWIGLU: output columns)
+  int Npad, n_slabs, n_ktiles, n_rb, splits, stages, rows, epi;
+  int *acc;               // splits > 1: [rows][Npad] int32, zero before and after
+  int *cnt;               // splits > 1: [n_slabs * n_rb] arrivals, zero before and after
+  int *err;
+  unsigned long long *argmax;  // TC_LOGITS: [rows] keys, zero before the launch
+  float *out;             // [rows][ld]
+  int ld;                 // row stride of out
+};
+
+// Epilogue of row m for columns lane + 32 i (i < 8) of one slab; v[i] is the
+// exact int32 dot product of that column.
+__device__ __forceinline__ void tc_epilogue_lane(const TcArgs &a, int m, int slab, int lane, const int v[8]) {
+  const int p0 = slab * kNT;
+  const float as = a.as[m];
+  float *orow = a.out + (size_t)m * a.ld;
+  if (a.epi == TC_SWIGLU) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int c = lane + 32 * i, j = slab * (kNT / 2) + c;
+      if (j < a.N) {
+        const float z = dequant(as, a.ws[p0 + c], v[i]);
+        const float u = dequant(as, a.ws[p0 + kNT / 2 + c], v[i + 4]);
+        const float sg = __fdiv_rn(1.0f, __fadd_rn(1.0f, libm_expf(-z)));  // llama.c:585
+        orow[j] = __fmul_rn(__fmul_rn(z, sg), u);                          // llama.c:586
+      }
+    }
+    return;
+  }
+  unsigned long long best = 0ull;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int j = p0 + lane + 32 * i;
+    if (j < a.N) {
+      const float y = dequant(as, a.ws[j], v[i]);
+      if (a.epi == TC_BIAS) {
+        orow[j] = __fadd_rn(y, a.bias[j]);
+      } else if (a.epi == TC_RESID) {
+        orow[j] = __fadd_rn(orow[j], y);
+      } else {
+        orow[j] = y;
+        if (a.epi == TC_LOGITS) {
+          const unsigned long long key = argmax_key(y, static_cast<uint32_t>(j));
+          best = key > best ? key : best;
+        }
+      }
+    }
+  }
+  if (a.epi == TC_LOGITS) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+      best = other > best ? other : best;
+    }
+    if (lane == 0) atomicMax(a.argmax + m, best);
+  }
 }
 
+__device__ __forceinline__ void red_add_s32(int *p, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// CTA (slab, row block, split) computes the 128 x 256 block of one 256-column
+// slab and 128-row block over k tiles [split*nk/splits, (split+1)*nk/splits).
+// Thread 0 streams (weight, activation) tile pairs through a ring and issues
+// the MMAs.  The accumulator then goes TMEM -> shared memory (64 rows at a
+// time) so that every warp works on whole rows: with one split it applies the
+// epilogue directly; otherwise it adds the block into `acc` (integer adds: the
+// order does not matter) and the last split to arrive applies the epilogue.
 template <int KT>
-__global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads) k_tc_gemm(const TcArgs a) {
   constexpr int WB = kNT * KT;       // weight tile bytes
   constexpr int AB = kTcRows * KT;   // activation tile bytes
   constexpr int SB = WB + AB;
   constexpr int kMma = KT / 32;      // MMAs per tile
+  constexpr int kLd = kNT + 1;       // staged accumulator row stride (words): conflict-free
   extern __shared__ __align__(128) uint8_t sm[];
   __shared__ __align__(8) uint64_t full[kTcMaxStages];
   __shared__ __align__(8) uint64_t empty[kTcMaxStages];
   __shared__ __align__(8) uint64_t accb;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_flag, s_abort;
+  __shared__ int s_abort, s_last;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = a.stages;
-  const long long T = (long long)a.n_slabs * a.n_ktiles;
-  const long long G = gridDim.x;
-  const long long t_begin = (long long)blockIdx.x * T / G;
-  const long long t_end = (long long)(blockIdx.x + 1) * T / G;
-  const int n = static_cast<int>(t_end - t_begin);
-  const long long nk = a.n_ktiles;
+  const int split = blockIdx.x % a.splits;
+  const int tile = blockIdx.x / a.splits;  // row blocks of one slab are neighbours: the slab is read once
+  const int rb = tile % a.n_rb, slab = tile / a.n_rb;
+  const int row0 = rb * kTcRows, rows_here = min(kTcRows, a.rows - row0);
+  const int kt0 = (int)((long long)split * a.n_ktiles / a.splits);
+  const int kt1 = (int)((long long)(split + 1) * a.n_ktiles / a.splits);
+  const int n = kt1 - kt0;
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -139,7 +232,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const TcArgs a) {
     fence_mbar_init();
     s_abort = 0;
   }
-  if (warp == 0) {  // one warp allocates (and later frees) the accumulator columns
+  if (warp == 0) {  // one warp allocates (and at the end frees) the accumulator columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
                  "r"(kTcTmemCols)
                  : "memory");
@@ -150,150 +243,117 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const TcArgs a) {
   tc_fence_after();
   const uint32_t tmem = s_tmem;
 
-  auto issue = [&](int idx, int s, bool weights, bool acts) {
-    const long long t = t_begin + idx;
-    const long long kt = t % nk;
-    uint8_t *dst = sm + (size_t)s * SB;
-    if (weights) bulk_load(dst, a.w + (size_t)t * WB, WB, &full[s]);
-    if (acts) bulk_load(dst + WB, a.acodes + (size_t)kt * AB, AB, &full[s]);
-  };
-  int issued = 0;
+  const uint8_t *wsrc = a.w + ((size_t)slab * a.n_ktiles + kt0) * WB;
+  const int8_t *asrc = a.acodes + (size_t)rb * kTcRows * a.n_ktiles * KT + (size_t)kt0 * AB;
   if (tid == 0) {  // weights do not depend on the previous kernel: start them now
-    for (; issued < n && issued < S; ++issued) {
-      mbar_expect_tx(&full[issued], SB);
-      issue(issued, issued, true, false);
+    for (int i = 0; i < n && i < S; ++i) {
+      mbar_expect_tx(&full[i], SB);
+      bulk_load(sm + (size_t)i * SB, wsrc + (size_t)i * WB, WB, &full[i]);
     }
   }
   pdl_launch_dependents();
   pdl_wait();
-  if (tid == 0)
-    for (int i = 0; i < issued; ++i) issue(i, i, false, true);
-
-  uint32_t acc_phase = 0;
-  bool fresh = true;  // the next MMA overwrites the accumulator
-
-  auto flush = [&](long long slab) {
-    if (tid == 0) umma_commit(&accb);
-    if (!mbar_wait_bounded(&accb, acc_phase)) s_abort = 1;
-    acc_phase ^= 1u;
-    tc_fence_after();
-    const long long c_first = tile_owner(slab * nk, T, G), c_last = tile_owner((slab + 1) * nk - 1, T, G);
-    const bool whole = c_first == c_last;
-    const int m = warp * 32 + lane;  // this thread's TMEM lane = output row
-    const int p0 = static_cast<int>(slab) * kNT;
-    int *slot = a.part + (((size_t)blockIdx.x * 2 + tc_slot(blockIdx.x, slab, T, G, nk)) * kTcRows + m) * kNT;
-    for (int cb = 0; cb < kNT / 32; ++cb) {
-      int v[32];
-      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cb * 32), v);
-      if (m >= a.rows) continue;
-      if (whole) {
-        const float as = a.as[m];
-#pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int j = p0 + cb * 32 + q;
-          if (j < a.N) a.out[(size_t)m * a.N + j] = dequant(as, a.ws[j], v[q]);
-        }
-      } else {
-#pragma unroll
-        for (int q = 0; q < 32; q += 4)
-          *reinterpret_cast<int4 *>(slot + cb * 32 + q) = make_int4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-      }
-    }
-    tc_fence_before();
-    __syncthreads();
-    fresh = true;
-    if (whole) return;
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_flag = atomicAdd(a.cnt + slab, 1) == static_cast<int>(c_last - c_first);
-    __syncthreads();
-    if (!s_flag) return;
-    __threadfence();
-    // last of the slab's CTAs: add the partial sums (exact in any order) and rescale
-    if (m < a.rows) {
-      const float as = a.as[m];
-      for (int j0 = 0; j0 < kNT; j0 += 4) {
-        int4 sum = make_int4(0, 0, 0, 0);
-        for (long long c = c_first; c <= c_last; ++c) {
-          const int4 p = *reinterpret_cast<const int4 *>(
-              a.part + (((size_t)c * 2 + tc_slot(c, slab, T, G, nk)) * kTcRows + m) * kNT + j0);
-          sum.x += p.x;
-          sum.y += p.y;
-          sum.z += p.z;
-          sum.w += p.w;
-        }
-        const int vv[4] = {sum.x, sum.y, sum.z, sum.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int j = p0 + j0 + q;
-          if (j < a.N) a.out[(size_t)m * a.N + j] = dequant(as, a.ws[j], vv[q]);
-        }
-      }
-    }
-    if (tid == 0) a.cnt[slab] = 0;
-    __syncthreads();
-  };
-
-  long long slab = t_begin / nk;
-  int kt = static_cast<int>(t_begin - slab * nk);
-  long long cur = n > 0 ? slab : -1;
-  int s = 0, sp = 0;
-  uint32_t phase = 0, phase_p = 0;
-  for (int i = 0; i < n; ++i) {
-    if (i > 0 && ++kt == a.n_ktiles) {
-      kt = 0;
-      ++slab;
-    }
-    if (slab != cur) {
-      flush(cur);
-      cur = slab;
-    }
-    if (tid == 0 && !s_abort) {
+  if (tid == 0) {
+    for (int i = 0; i < n && i < S; ++i) bulk_load(sm + (size_t)i * SB + WB, asrc + (size_t)i * AB, AB, &full[i]);
+    int issued = min(n, S), i = 0, s = 0, ps = S - 1;
+    uint32_t phase = 0, pphase = 1;  // ring position of tile i and of tile i - 1
+    for (; i < n; ++i) {
       if (!mbar_wait_bounded(&full[s], phase)) {
         s_abort = 1;
-      } else {
-        tc_fence_after();
-        const uint32_t wbase = smem_addr(sm + (size_t)s * SB), abase = wbase + WB;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t wbase = smem_addr(sm + (size_t)s * SB), abase = wbase + WB;
 #pragma unroll
-        for (int j = 0; j < kMma; ++j) {
-          const uint64_t ad = umma_desc(abase + j * 2 * (kTcRows * 16), kTcRows * 16, 128);
-          const uint64_t bd = umma_desc(wbase + j * 2 * (kNT * 16), kNT * 16, 128);
-          umma_s8(tmem, ad, bd, (fresh && j == 0) ? 0u : 1u);
+      for (int j = 0; j < kMma; ++j) {
+        const uint64_t ad = umma_desc(abase + j * 2 * (kTcRows * 16), kTcRows * 16, 128);
+        const uint64_t bd = umma_desc(wbase + j * 2 * (kNT * 16), kNT * 16, 128);
+        umma_s8(tmem, ad, bd, (i > 0 || j > 0) ? 1u : 0u);
+      }
+      umma_commit(&empty[s]);
+      // Refill the stage of tile i - 1 (whose MMAs ran while these were issued)
+      // with tile i - 1 + S.
+      if (i > 0 && i - 1 + S < n) {
+        if (!mbar_wait_bounded(&empty[ps], pphase)) {
+          s_abort = 1;
+          ++i;
+          break;
         }
-        fresh = false;
-        umma_commit(&empty[s]);
-        // refill the stage of the previous tile once its MMAs have read it
-        if (i > 0 && issued < n) {
-          if (!mbar_wait_bounded(&empty[sp], phase_p)) {
-            s_abort = 1;
-          } else {
-            mbar_expect_tx(&full[sp], SB);
-            issue(issued, sp, true, true);
-            ++issued;
-          }
+        mbar_expect_tx(&full[ps], SB);
+        bulk_load(sm + (size_t)ps * SB, wsrc + (size_t)(i - 1 + S) * WB, WB, &full[ps]);
+        bulk_load(sm + (size_t)ps * SB + WB, asrc + (size_t)(i - 1 + S) * AB, AB, &full[ps]);
+        ++issued;
+      }
+      ps = s;
+      pphase = phase;
+      if (++s == S) {
+        s = 0;
+        phase ^= 1u;
+      }
+    }
+    // After a timeout, wait (bounded) for the copies still landing in the ring.
+    for (int t = i; t < issued; ++t) mbar_wait_bounded(&full[t % S], (uint32_t)(t / S) & 1u);
+    umma_commit(&accb);  // arrives when every MMA above is done
+  }
+  if (!mbar_wait_bounded(&accb, 0)) s_abort = 1;
+  tc_fence_after();
+  __syncthreads();  // s_abort is final; the ring is free for staging
+  const bool ok = !s_abort;
+  const bool direct = a.splits == 1;
+  int *stg = reinterpret_cast<int *>(sm);  // [64][kLd]
+  const int p0 = slab * kNT;
+  for (int g = 0; g < 2 && g * 64 < rows_here; ++g) {
+    if ((warp >> 1) == g) {  // warps 2g, 2g+1 own TMEM lanes (rows) [64g, 64g + 64)
+      const int lr = (warp & 1) * 32 + lane;
+#pragma unroll 1
+      for (int cb = 0; cb < kNT / 32; ++cb) {
+        int v[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cb * 32), v);
+#pragma unroll
+        for (int q = 0; q < 32; ++q) stg[lr * kLd + cb * 32 + q] = v[q];
+      }
+    }
+    __syncthreads();
+    const int nr = min(64, rows_here - g * 64);
+    if (ok) {
+      for (int r = warp; r < nr; r += kTcThreads / 32) {
+        const int m = row0 + g * 64 + r;
+        const int *vr = stg + r * kLd;
+        if (direct) {
+          int v[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) v[i] = vr[lane + 32 * i];
+          tc_epilogue_lane(a, m, slab, lane, v);
+        } else {
+          int *accr = a.acc + (size_t)m * a.Npad + p0;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) red_add_s32(accr + lane + 32 * i, vr[lane + 32 * i]);
         }
       }
     }
-    fresh = false;
-    if (i > 0 && ++sp == S) {
-      sp = 0;
-      phase_p ^= 1u;
-    }
-    if (++s == S) {
-      s = 0;
-      phase ^= 1u;
-    }
-    if (((i + 1) & 15) == 0 || i + 1 == n) {  // keep all threads in step with thread 0
-      __syncthreads();
-      if (s_abort) break;
-    }
+    __syncthreads();
   }
-  if (!s_abort && n > 0) flush(cur);
-  // drain: every MMA this CTA issued must be finished before the columns go back
-  if (tid == 0) {
-    umma_commit(&accb);
-    mbar_wait_bounded(&accb, acc_phase);
-    if (s_abort) atomicOr(a.err, ERR_TIMEOUT);
+  if (tid == 0 && !ok) atomicOr(a.err, ERR_TIMEOUT);
+  if (!direct) {
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(a.cnt + tile, 1) == a.splits - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      for (int r = warp; r < rows_here; r += kTcThreads / 32) {
+        const int m = row0 + r;
+        int *accr = a.acc + (size_t)m * a.Npad + p0;
+        int v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[i] = __ldcg(accr + lane + 32 * i);
+          __stcg(accr + lane + 32 * i, 0);
+        }
+        tc_epilogue_lane(a, m, slab, lane, v);
+      }
+      if (tid == 0) a.cnt[tile] = 0;
+    }
   }
   tc_fence_before();
   __syncthreads();
