@@ -242,7 +242,7 @@ def run_ours(args, rank, world):
     achieved = g_bytes / (g_ms / 1e3) / 1e9
     step_bytes = weight_bytes(cfg)
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(achieved / hbm_peak, 4), "traffic": profiled_traffic(),
+                "frac": round(achieved / hbm_peak, 4), "traffic": profiled_traffic(cfg),
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s",
                 "kernel": "k_gemv (int8 W8A8 GEMV, all five per-step shapes)",
                 "per_kind": per_kind,
@@ -329,16 +329,25 @@ def hbm_peak_gbs():
         return 6650.0
 
 
-def profiled_traffic():
-    """DRAM bytes per k_gemv launch from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "k_gemv_8b_decode.md")
+def profiled_traffic(cfg):
+    """Mean DRAM bytes per k_gemv launch of one decode step, from the per-kind
+    ncu figures committed in profiles/k_gemv_8b_decode.md (captured on the
+    8B layer shapes; the step has n_layers launches of each layer kind and one
+    lm_head).  None for other shapes."""
+    if (cfg["d_model"], cfg["d_ff"], cfg["vocab"], cfg["n_heads"], cfg["n_kv"]) != (4096, 14336, 128256, 32, 8):
+        return None
+    per = {}
     try:
-        for ln in open(p):
-            if ln.startswith("traffic_bytes_per_launch:"):
-                return float(ln.split(":", 1)[1])
-    except OSError:
-        pass
-    return None
+        for ln in open(os.path.join(ROOT, "profiles", "k_gemv_8b_decode.md")):
+            if ln.startswith("traffic_bytes "):
+                k, v = ln[len("traffic_bytes "):].split(":", 1)
+                per[k.strip()] = float(v)
+    except (OSError, ValueError):
+        return None
+    if not {"qkv", "wo", "w13", "w2", "lm_head"} <= per.keys():
+        return None
+    L = cfg["n_layers"]
+    return round((L * (per["qkv"] + per["wo"] + per["w13"] + per["w2"]) + per["lm_head"]) / (4 * L + 1))
 
 
 def cpu_baseline(lib, m, kv, start_tok, gen_ids):
