@@ -150,7 +150,7 @@ void q_llama_model_free(QLlamaModel *m);
 QLlamaModel q_llama_quantize_from(const LlamaModel *src);
 
 /* Replaces llama.c:513-526 (llama.h:140).  Creates the GPU KV cache
- * (f32 [n_layers][max_seq][kv_dim], K and V) plus the reference-shaped host
+ * (head-major f32 [n_layers][n_kv][max_seq][head_dim], K and V) plus the reference-shaped host
  * arrays. */
 LlamaKV q_llama_kv_create(const QLlamaModel *m);
 
@@ -188,6 +188,31 @@ void q_llama_clear_error(void);
  * `logits` may be NULL, in which case no logits are copied to the host (4 bytes
  * cross PCIe per token).  Returns -1 on error. */
 int q_llama_decode_step_argmax(const QLlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
+
+/* Batched decode: one token for each of B sequences at once.  Sequence b feeds
+ * tokens[b] at position kvs[b]->len of its own cache; row b of `logits`
+ * (B x vocab floats, caller-owned) receives its logits and every kvs[b]->len
+ * advances by one.  Each row equals what q_llama_decode_step (llama.c:528-600)
+ * gives for that sequence alone, bit for bit; the caches must be distinct.
+ * The reference has no batch entry point: this is the additive
+ * `q_llama_decode_batch` extension of the C API. */
+void q_llama_decode_batch(const QLlamaModel *m, LlamaKV **kvs, const int *tokens, int B, Tensor *logits);
+
+/* As q_llama_decode_batch, but writes the B greedy ids (first maximum,
+ * sampler.c:8-21) to ids[] instead of logits.  Returns 0 or an error code. */
+int q_llama_decode_batch_argmax(const QLlamaModel *m, LlamaKV **kvs, const int *tokens, int B, int *ids);
+
+/* Prefill: feeds ids[0..n) at positions kv->len .. kv->len + n - 1 in one pass
+ * (the tensor-core GEMMs see n rows).  The cache then equals that of n
+ * q_llama_decode_step calls, and `logits` (1 x vocab, may be NULL) receives the
+ * logits of the last id, bit for bit those of the n-th step.  kv->len advances
+ * by n.  Additive extension (the reference feeds prompts token by token,
+ * main.c:650-671). */
+void q_llama_prefill(const QLlamaModel *m, LlamaKV *kv, const int *ids, int n, Tensor *logits);
+
+/* As q_llama_prefill; returns the greedy id after the last prompt token, or -1
+ * on error. */
+int q_llama_prefill_argmax(const QLlamaModel *m, LlamaKV *kv, const int *ids, int n, Tensor *logits);
 
 /* Copies the GPU KV cache rows [0, kv->len) into kv->k / kv->v (the
  * reference-shaped host arrays).  Returns LLMQ_OK or an error code. */

@@ -15,6 +15,7 @@
 #include "llmq_internal.h"
 #include "llmq_kernels.cuh"
 #include "llmq_tc_gemm.cuh"
+#include "llmq_rows.cuh"
 
 using namespace llmq;
 
@@ -93,11 +94,21 @@ void free_mat(Mat &m) {
   m = Mat{};
 }
 
+// Every kernel asks for the largest shared-memory carveout, so consecutive
+// launches with different shared-memory needs never make an SM repartition
+// its L1 / shared memory between them.
+template <typename K>
+cudaError_t set_attr(K *fn, int smem) {
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+}
+
 template <int PRO, int EPI, int MR>
 cudaError_t set_gemv_attr(int smem) {
-  cudaError_t e = cudaFuncSetAttribute(k_gemv<PRO, EPI, MR, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_attr(k_gemv<PRO, EPI, MR, 64>, smem);
   if (e != cudaSuccess) return e;
-  return cudaFuncSetAttribute(k_gemv<PRO, EPI, MR, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  return set_attr(k_gemv<PRO, EPI, MR, 128>, smem);
 }
 
 int init_expf_table(DevCtx &c) {
@@ -156,11 +167,17 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_RESID, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_SWIGLU, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_LOGITS, 1>(sm);
-  ea = ea != cudaSuccess ? ea
-                         : cudaFuncSetAttribute(k_attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-  ea = ea != cudaSuccess ? ea : cudaFuncSetAttribute(k_attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-  ea = ea != cudaSuccess ? ea : cudaFuncSetAttribute(k_tc_gemm<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
-  ea = ea != cudaSuccess ? ea : cudaFuncSetAttribute(k_tc_gemm<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_attn_scores, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_attn_pv, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<64>, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<128>, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_act_codes, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_rows_norm_codes, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_rows_append, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_rows_scores, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_rows_pv, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_rows_finish, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_step_finish, 0);
   if (ea != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
     return nullptr;
@@ -428,6 +445,23 @@ cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err,
   return cudaLaunchKernelEx(&cfg, k_step_finish, step, argmax, err, result, tokens, max_seq);
 }
 
+// Launches `kern` with programmatic dependent launch (the kernel itself waits
+// for its predecessor with griddepcontrol.wait before touching shared data).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // ------------------------------------------------------------------- models
 struct DevModel;
 
@@ -470,6 +504,18 @@ struct DevModel {
   std::vector<DevKV *> kvs;
   // per-kernel events while llmq_step_profile records a step outside a graph
   std::vector<cudaEvent_t> *prof = nullptr;
+  // multi-row passes (batched decode, prefill): grow-only scratch
+  struct Rows {
+    int cap = 0, lm_cap = 0;
+    float *x = nullptr, *qkv = nullptr, *qr = nullptr, *ao = nullptr, *h = nullptr, *scores = nullptr;
+    float *logits = nullptr;
+    RowDesc *rd = nullptr;
+    int *ids = nullptr;
+    unsigned long long *argmax = nullptr;
+    RowDesc *h_rd = nullptr;  // pinned
+    int *h_ids = nullptr;     // pinned
+    int *h_err = nullptr;     // pinned
+  } rows;
 };
 
 std::unordered_map<const void *, DevModel *> g_models;
@@ -501,6 +547,14 @@ void release_model(DevModel *M) {
   void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o, M->scores,
                       M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step};
   for (void *p : dev_ptrs) cudaFree(p);
+  {
+    auto &R = M->rows;
+    void *rp[] = {R.x, R.qkv, R.qr, R.ao, R.h, R.scores, R.logits, R.rd, R.ids, R.argmax};
+    for (void *p : rp) cudaFree(p);
+    cudaFreeHost(R.h_rd);
+    cudaFreeHost(R.h_ids);
+    cudaFreeHost(R.h_err);
+  }
   cudaFreeHost(M->h_step);
   cudaFreeHost(M->h_result);
   cudaFreeHost(M->h_tokens);
@@ -892,6 +946,162 @@ int reset_after_device_error(DevModel *M, int flags) {
   return 0;
 }
 
+// ------------------------------------------------------- multi-row passes
+constexpr int kRowsPerPass = 1024;  // rows of one pass (longer prompts run in several)
+
+int ensure_rows(DevModel *M, int rows, int lm_rows) {
+  auto &R = M->rows;
+  const LlmqConfig &cfg = M->cfg;
+  if (rows > R.cap) {
+    void *old[] = {R.x, R.qkv, R.qr, R.ao, R.h, R.scores, R.rd};
+    for (void *p : old) cudaFree(p);
+    cudaFreeHost(R.h_rd);
+    R.x = R.qkv = R.qr = R.ao = R.h = R.scores = nullptr;
+    R.rd = nullptr;
+    R.h_rd = nullptr;
+    R.cap = 0;
+    const size_t n = (size_t)rows;
+    CK(cudaMalloc(&R.x, n * cfg.d_model * sizeof(float)));
+    CK(cudaMalloc(&R.qkv, n * (M->qd + 2 * M->kvd) * sizeof(float)));
+    CK(cudaMalloc(&R.qr, n * M->qd * sizeof(float)));
+    CK(cudaMalloc(&R.ao, n * M->qd * sizeof(float)));
+    CK(cudaMalloc(&R.h, n * cfg.d_ff * sizeof(float)));
+    CK(cudaMalloc(&R.scores, n * cfg.n_heads * cfg.max_seq * sizeof(float)));
+    CK(cudaMalloc(&R.rd, n * sizeof(RowDesc)));
+    CK(cudaMallocHost(&R.h_rd, n * sizeof(RowDesc)));
+    R.cap = rows;
+  }
+  if (lm_rows > R.lm_cap) {
+    cudaFree(R.logits);
+    cudaFree(R.ids);
+    cudaFree(R.argmax);
+    cudaFreeHost(R.h_ids);
+    R.logits = nullptr;
+    R.ids = nullptr;
+    R.argmax = nullptr;
+    R.h_ids = nullptr;
+    R.lm_cap = 0;
+    CK(cudaMalloc(&R.logits, (size_t)lm_rows * cfg.vocab * sizeof(float)));
+    CK(cudaMalloc(&R.ids, (size_t)lm_rows * sizeof(int)));
+    if (!dev_zeros(&R.argmax, (size_t)lm_rows)) return 0;
+    CK(cudaMallocHost(&R.h_ids, (size_t)lm_rows * sizeof(int)));
+    R.lm_cap = lm_rows;
+  }
+  if (!R.h_err) CK(cudaMallocHost(&R.h_err, 4 * sizeof(int)));
+  return 1;
+}
+
+// One pass over `rows` rows (each one decode step of its own sequence, at its
+// own position).  All layers run for every row; the final norm, lm-head and
+// greedy id run for rows [lm0, rows) only: their ids go to ids_h and, if
+// logits_h is given, their logits (row-major, vocab per row) as well.
+int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, float *logits_h, int *ids_h) {
+  const LlmqConfig &cfg = M->cfg;
+  cudaStream_t st = M->stream;
+  const int dm = cfg.d_model, qd = M->qd, kvd = M->kvd, hd = cfg.head_dim, dff = cfg.d_ff;
+  const int lm_rows = rows - lm0;
+  if (!ensure_rows(M, rows, lm_rows)) return 0;
+  auto &R = M->rows;
+  int max_kpad = M->lm.Kpad;
+  for (int l = 0; l < cfg.n_layers; ++l)
+    max_kpad = std::max({max_kpad, M->qkv[l].Kpad, M->wo[l].Kpad, M->w13[l].Kpad, M->w2[l].Kpad});
+  const int n_rb = (rows + kTcRows - 1) / kTcRows;
+  if (!ensure(&c.tc_codes, &c.tc_codes_n, (size_t)n_rb * kTcRows * max_kpad, false) ||
+      !ensure(&c.tc_as, &c.tc_as_n, (size_t)n_rb * kTcRows, false))
+    return 0;
+  std::memcpy(R.h_rd, rows_h, (size_t)rows * sizeof(RowDesc));
+  CK(cudaMemcpyAsync(R.rd, R.h_rd, (size_t)rows * sizeof(RowDesc), cudaMemcpyHostToDevice, st));
+
+  RowNormArgs na{};
+  na.rd = R.rd;
+  na.x_out = R.x;
+  na.wte_q = M->wte_q;
+  na.wte_s = M->wte_s;
+  na.vocab = cfg.vocab;
+  na.eps = cfg.eps;
+  na.K = dm;
+  na.codes = c.tc_codes;
+  na.as = c.tc_as;
+  na.err = M->err;
+  const size_t norm_smem = 2 * (size_t)((dm + 3) & ~3) * sizeof(float);
+  RowAttnArgs aa{};
+  aa.rd = R.rd;
+  aa.qkv = R.qkv;
+  aa.qr = R.qr;
+  aa.scores = R.scores;
+  aa.out = R.ao;
+  aa.rope_cos = M->rope_cos;
+  aa.rope_sin = M->rope_sin;
+  aa.n_heads = cfg.n_heads;
+  aa.n_kv = cfg.n_kv;
+  aa.hd = hd;
+  aa.smax = cfg.max_seq;
+  aa.err = M->err;
+  AttnArgs probe{};
+  probe.n_heads = cfg.n_heads;
+  probe.n_kv = cfg.n_kv;
+  probe.hd = hd;
+  probe.max_seq = cfg.max_seq;
+  const size_t sc_smem = scores_smem(probe), pv_sm = pv_smem(probe);
+  auto norm = [&](const float *in, const float *gamma, const Mat &m, int nrows) {
+    na.in = in;
+    na.gamma = gamma;
+    na.Kpad = m.Kpad;
+    na.KT = m.KT;
+    return launch_pdl(k_rows_norm_codes, dim3(nrows), dim3(kRowThreads), norm_smem, st, na);
+  };
+  auto codes = [&](const float *in, int K, const Mat &m) {
+    return launch_pdl(k_act_codes, dim3(rows), dim3(256), 0, st, in, rows, K, m.Kpad, m.KT, c.tc_codes, c.tc_as);
+  };
+  auto gemm = [&](const Mat &m, int nrows, int epi, const float *bias, float *out, int ld,
+                  unsigned long long *am) -> int {
+    TcArgs t;
+    if (!plan_tc(c, m, nrows, t)) return 0;
+    t.epi = epi;
+    t.bias = bias;
+    t.out = out;
+    t.ld = ld;
+    t.err = M->err;
+    t.argmax = am;
+    return launch_tc_gemm(t, m.KT, st, pdl_enabled());
+  };
+  for (int l = 0; l < cfg.n_layers; ++l) {
+    CK(norm(l == 0 ? nullptr : R.x, M->attn_norm[l], M->qkv[l], rows));
+    if (!gemm(M->qkv[l], rows, TC_BIAS, M->bias_qkv[l], R.qkv, qd + 2 * kvd, nullptr)) return 0;
+    aa.layer = l;
+    CK(launch_pdl(k_rows_append, dim3(rows), dim3(256), 0, st, aa));
+    CK(launch_pdl(k_rows_scores, dim3((cfg.max_seq + kScoreChunk - 1) / kScoreChunk, cfg.n_kv, rows),
+                  dim3(kScoreThreads), sc_smem, st, aa));
+    CK(launch_pdl(k_rows_pv, dim3((hd + kPVSlice - 1) / kPVSlice, cfg.n_heads, rows), dim3(kPVThreads), pv_sm, st,
+                  aa));
+    CK(codes(R.ao, qd, M->wo[l]));
+    if (!gemm(M->wo[l], rows, TC_RESID, nullptr, R.x, dm, nullptr)) return 0;
+    CK(norm(R.x, M->ffn_norm[l], M->w13[l], rows));
+    if (!gemm(M->w13[l], rows, TC_SWIGLU, nullptr, R.h, dff, nullptr)) return 0;
+    CK(codes(R.h, dff, M->w2[l]));
+    if (!gemm(M->w2[l], rows, TC_RESID, nullptr, R.x, dm, nullptr)) return 0;
+  }
+  if (lm_rows > 0) {
+    CK(norm(R.x + (size_t)lm0 * dm, M->final_norm, M->lm, lm_rows));
+    if (!gemm(M->lm, lm_rows, TC_LOGITS, nullptr, R.logits, cfg.vocab, R.argmax)) return 0;
+    CK(launch_pdl(k_rows_finish, dim3(1), dim3(256), 0, st, R.argmax, lm_rows, R.ids));
+    CK(cudaMemcpyAsync(R.h_ids, R.ids, (size_t)lm_rows * sizeof(int), cudaMemcpyDeviceToHost, st));
+    if (logits_h)
+      CK(cudaMemcpyAsync(logits_h, R.logits, (size_t)lm_rows * cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost,
+                         st));
+  }
+  CK(cudaMemcpyAsync(R.h_err, M->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (R.h_err[0]) {
+    if (c.tc_acc) cudaMemsetAsync(c.tc_acc, 0, c.tc_acc_n * sizeof(int), st);
+    if (c.tc_cnt) cudaMemsetAsync(c.tc_cnt, 0, c.tc_cnt_n * sizeof(int), st);
+    cudaMemsetAsync(R.argmax, 0, (size_t)R.lm_cap * sizeof(unsigned long long), st);
+    return reset_after_device_error(M, R.h_err[0]);
+  }
+  if (lm_rows > 0 && ids_h) std::memcpy(ids_h, R.h_ids, (size_t)lm_rows * sizeof(int));
+  return 1;
+}
+
 }  // namespace
 
 // ======================================================================== API
@@ -1118,6 +1328,80 @@ int llmqd_generate(const QLlamaModel *m, const LlamaKV *kv, int token, int n, in
   cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
   if (M->h_result[3]) return reset_after_device_error(M, M->h_result[3]);
   std::memcpy(ids, M->h_tokens, (size_t)n * sizeof(int));
+  return 1;
+}
+
+int llmqd_decode_rows(const QLlamaModel *m, LlamaKV *const *kvs, const int *tokens, int B, float *logits,
+                      int *ids) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (B <= 0 || !kvs || !tokens) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_decode_batch: bad arguments");
+    return 0;
+  }
+  DevModel *M = get_model(m);
+  if (!M) return 0;
+  DevCtx *c = get_ctx();
+  if (!c) return 0;
+  std::vector<RowDesc> rows((size_t)B);
+  for (int b = 0; b < B; ++b) {
+    const LlamaKV *kv = kvs[b];
+    DevKV *K = get_kv(M, kv);
+    if (!K || !check_step_inputs(M, kv, tokens[b], 1)) return 0;
+    for (int e = 0; e < b; ++e)
+      if (rows[e].k == K->k) {
+        llmq_set_error(LLMQ_ERR_ARG, "q_llama_decode_batch: sequence %d and %d share one KV cache", e, b);
+        return 0;
+      }
+    rows[b] = RowDesc{K->k, K->v, K->max_seq, kv->len, tokens[b], 0};
+  }
+  std::vector<int> tmp;
+  if (!ids) {
+    tmp.resize((size_t)B);
+    ids = tmp.data();
+  }
+  CK(cudaEventRecord(M->ev0, M->stream));
+  for (int off = 0; off < B; off += kRowsPerPass) {
+    const int n = std::min(kRowsPerPass, B - off);
+    if (!run_rows(*c, M, rows.data() + off, n, 0, logits ? logits + (size_t)off * M->cfg.vocab : nullptr, ids + off))
+      return 0;
+  }
+  CK(cudaEventRecord(M->ev1, M->stream));
+  CK(cudaEventSynchronize(M->ev1));
+  cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
+  return 1;
+}
+
+int llmqd_prefill(const QLlamaModel *m, const LlamaKV *kv, const int *ids, int n, float *logits, int *next) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (n <= 0 || !ids) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_prefill: bad arguments");
+    return 0;
+  }
+  DevModel *M = get_model(m);
+  if (!M) return 0;
+  DevCtx *c = get_ctx();
+  if (!c) return 0;
+  DevKV *K = get_kv(M, kv);
+  if (!K || !check_step_inputs(M, kv, 0, n)) return 0;
+  for (int i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= M->cfg.vocab) {
+      llmq_set_error(LLMQ_ERR_ARG, "q_llama_prefill: token id %d at %d outside [0, %d)", ids[i], i, M->cfg.vocab);
+      return 0;
+    }
+  std::vector<RowDesc> rows((size_t)std::min(n, kRowsPerPass));
+  int last = -1;
+  CK(cudaEventRecord(M->ev0, M->stream));
+  for (int off = 0; off < n; off += kRowsPerPass) {
+    const int cnt = std::min(kRowsPerPass, n - off);
+    for (int r = 0; r < cnt; ++r) rows[r] = RowDesc{K->k, K->v, K->max_seq, kv->len + off + r, ids[off + r], 0};
+    const bool final_pass = off + cnt == n;
+    if (!run_rows(*c, M, rows.data(), cnt, final_pass ? cnt - 1 : cnt, final_pass ? logits : nullptr, &last))
+      return 0;
+  }
+  CK(cudaEventRecord(M->ev1, M->stream));
+  CK(cudaEventSynchronize(M->ev1));
+  cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
+  if (next) *next = last;
   return 1;
 }
 

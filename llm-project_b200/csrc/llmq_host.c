@@ -404,6 +404,44 @@ LLMQ_API int q_llama_generate(const QLlamaModel *m, LlamaKV *kv, int token, int 
   return LLMQ_OK;
 }
 
+LLMQ_API void q_llama_decode_batch(const QLlamaModel *m, LlamaKV **kvs, const int *tokens, int B, Tensor *logits) {
+  if (!logits || !logits->data || B <= 0 || logits->size < (size_t)B * (size_t)m->vocab) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_decode_batch: logits tensor must hold B x %d floats", m->vocab);
+    return;
+  }
+  if (llmqd_decode_rows(m, kvs, tokens, B, logits->data, NULL))
+    for (int b = 0; b < B; b++) kvs[b]->len = kvs[b]->len + 1;
+}
+
+LLMQ_API int q_llama_decode_batch_argmax(const QLlamaModel *m, LlamaKV **kvs, const int *tokens, int B, int *ids) {
+  if (B <= 0 || !ids) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_decode_batch_argmax: bad arguments");
+    return LLMQ_ERR_ARG;
+  }
+  if (!llmqd_decode_rows(m, kvs, tokens, B, NULL, ids)) return q_llama_last_error();
+  for (int b = 0; b < B; b++) kvs[b]->len = kvs[b]->len + 1;
+  return LLMQ_OK;
+}
+
+LLMQ_API void q_llama_prefill(const QLlamaModel *m, LlamaKV *kv, const int *ids, int n, Tensor *logits) {
+  if (logits && (!logits->data || logits->size < (size_t)m->vocab)) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_prefill: logits tensor must hold %d floats", m->vocab);
+    return;
+  }
+  if (llmqd_prefill(m, kv, ids, n, logits ? logits->data : NULL, NULL)) kv->len = kv->len + n;
+}
+
+LLMQ_API int q_llama_prefill_argmax(const QLlamaModel *m, LlamaKV *kv, const int *ids, int n, Tensor *logits) {
+  if (logits && (!logits->data || logits->size < (size_t)m->vocab)) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_prefill_argmax: logits tensor must hold %d floats", m->vocab);
+    return -1;
+  }
+  int next = -1;
+  if (!llmqd_prefill(m, kv, ids, n, logits ? logits->data : NULL, &next)) return -1;
+  kv->len = kv->len + n;
+  return next;
+}
+
 LLMQ_API int q_llama_kv_sync_host(const QLlamaModel *m, LlamaKV *kv) {
   if (!llmqd_kv_download(m, kv, kv->len)) return q_llama_last_error();
   return LLMQ_OK;

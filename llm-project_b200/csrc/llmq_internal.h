@@ -39,6 +39,12 @@ LLMQ_HIDDEN int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token,
  * ids[i] = argmax after step i. */
 LLMQ_HIDDEN int llmqd_generate(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids);
 LLMQ_HIDDEN int llmqd_kv_download(const QLlamaModel *m, const LlamaKV *kv, int len);
+/* Multi-row passes: B sequences one token each (batched decode), or n prompt
+ * tokens of one sequence (prefill).  logits/ids may be NULL. */
+LLMQ_HIDDEN int llmqd_decode_rows(const QLlamaModel *m, LlamaKV *const *kvs, const int *tokens, int B,
+                                  float *logits, int *ids);
+LLMQ_HIDDEN int llmqd_prefill(const QLlamaModel *m, const LlamaKV *kv, const int *ids, int n, float *logits,
+                              int *next);
 LLMQ_HIDDEN float llmqd_last_ms(void);
 
 #ifdef __cplusplus

@@ -106,6 +106,13 @@ SIGNATURES = {
     "qmatmul_device_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,
                                          C.c_void_p, C.c_void_p]),
     "llmq_bench_qmatmul": (C.c_int, [C.POINTER(QTensor), C.c_int, C.c_int, c_float_p]),
+    "q_llama_decode_batch": (None, [C.POINTER(QLlamaModel), C.POINTER(C.POINTER(LlamaKV)), c_int_p, C.c_int,
+                                    C.POINTER(Tensor)]),
+    "q_llama_decode_batch_argmax": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(C.POINTER(LlamaKV)), c_int_p,
+                                              C.c_int, c_int_p]),
+    "q_llama_prefill": (None, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), c_int_p, C.c_int, C.POINTER(Tensor)]),
+    "q_llama_prefill_argmax": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), c_int_p, C.c_int,
+                                         C.POINTER(Tensor)]),
 }
 
 _lib = None
@@ -166,6 +173,17 @@ def qtensor_arrays(t: QTensor) -> tuple[np.ndarray, np.ndarray]:
     q = np.ctypeslib.as_array(C.cast(t.q, c_byte_p), shape=(t.rows * t.cols,)).astype(np.int8)
     s = np.ctypeslib.as_array(t.scale, shape=(t.cols,)).copy()
     return q.reshape(t.rows, t.cols).copy(), s
+
+
+def kv_pointers(kvs) -> C.Array:
+    """A LlamaKV*[] array for the batched entry points (the structs stay owned
+    by the caller and must outlive the call)."""
+    arr = (C.POINTER(LlamaKV) * len(kvs))(*[C.pointer(k) for k in kvs])
+    return arr
+
+
+def int_array(vals) -> C.Array:
+    return (C.c_int * len(vals))(*[int(v) for v in vals])
 
 
 def vec_array(t: Tensor) -> np.ndarray:
