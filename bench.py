@@ -1,7 +1,7 @@
 """Benchmark: int8 (W8A8) LLaMA-family KV-cache decode on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload 8b|tiny]
+                    [--workload 8b|8b2|tiny|serve64|sweep]
 
 Default workload: LLaMA-3-8B-shaped int8 model
 (dm 4096, 32 layers, 32/8 heads, hd 128, dff 14336, vocab 128256, rope 5e5),
@@ -46,6 +46,10 @@ WORKLOADS = {
     "8b2": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128, d_ff=14336,
                          rope_base=500000.0, eps=1e-5), prompt=512, gen=256,
                 name="llama3-8b layer shapes, 2 layers (profiling case), batch 1"),
+    "serve64": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=32, n_heads=32, n_kv=8, head_dim=128,
+                             d_ff=14336, rope_base=500000.0, eps=1e-5), prompt=2048, gen=128, batch=64,
+                    name="llama3-8b-shaped int8 W8A8 batched serving: 64 sequences, 2048-id prompts prefilled, "
+                         "then batched greedy decode"),
     "tiny": dict(cfg=dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768,
                           rope_base=10000.0, eps=1e-5), prompt=16, gen=240,
                  name="tiny llama int8 W8A8, batch 1: 16-id prompt then greedy decode"),
@@ -281,6 +285,146 @@ def run_ours(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
+def run_serve(args, rank, world):
+    """B sequences each prefilled with its own P-id prompt
+    (q_llama_prefill_argmax, one sequence per call, the GEMMs see up to 1024
+    rows), then batched greedy decode of all B sequences
+    (q_llama_decode_batch_argmax, one row per sequence).  A step is one batched
+    decode step (B tokens)."""
+    lib = llmq.load()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if lib.q_llama_set_device(local) != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    wl = WORKLOADS[args.workload]
+    cfg = wl["cfg"]
+    B, P, W, K = wl["batch"], args.prompt or wl["prompt"], args.warmup, args.steps
+    max_seq = P + W + K
+    if world > 1:
+        os.environ.setdefault("LLMQ_THREADS", str(max(1, (os.cpu_count() or 1) // world)))
+    m = make_model(lib, cfg, max_seq)
+    if lib.q_llama_model_upload(C.byref(m)) != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    kvs = []
+    for _ in range(B):
+        kvs.append(lib.q_llama_kv_create(C.byref(m)))
+        llmq.check(lib)
+    rng = np.random.default_rng(SEED_PROMPT)
+    prompts = rng.integers(0, cfg["vocab"], size=(B, P)).astype(np.int32)
+
+    # ---- prefill: every sequence's prompt in one call per sequence
+    pre_ms, nxt = 0.0, []
+    t0 = time.perf_counter()
+    for b in range(B):
+        ids = prompts[b]
+        tok = lib.q_llama_prefill_argmax(C.byref(m), C.byref(kvs[b]), ids.ctypes.data_as(llmq.c_int_p), P, None)
+        if tok < 0:
+            llmq.check(lib)
+        pre_ms += float(lib.q_llama_last_step_ms())
+        nxt.append(tok)
+    pre_wall = time.perf_counter() - t0
+    kvp = llmq.kv_pointers(kvs)
+    out = (C.c_int * B)()
+
+    def step(tokens):
+        rc = lib.q_llama_decode_batch_argmax(C.byref(m), kvp, llmq.int_array(tokens), B, out)
+        if rc != 0:
+            llmq.check(lib)
+        return [out[i] for i in range(B)], float(lib.q_llama_last_step_ms())
+
+    for _ in range(W):
+        nxt, _ = step(nxt)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    dev_ms, launches = 0.0, 0
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        for _ in range(K):
+            nxt, ms = step(nxt)
+            dev_ms += ms
+            launches += int(lib.llmq_last_launches())
+        wall = time.perf_counter() - t0
+    if dist is not None:
+        import torch
+        t = torch.tensor([dev_ms, wall], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_ms, wall = float(t[0]), float(t[1])
+    value = world * B * K / (dev_ms / 1e3)
+    e2e = world * B * K / wall
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    # algorithmic bytes of one step: the int8 weights once, plus every
+    # sequence's K and V rows [0, pos] of every layer (f32)
+    kvd = cfg["n_kv"] * cfg["head_dim"]
+    mean_pos = P + W + (K - 1) / 2.0
+    kv_bytes = B * cfg["n_layers"] * 2 * (mean_pos + 1) * kvd * 4
+    step_bytes = weight_bytes(cfg) + kv_bytes
+    achieved = step_bytes / (dev_ms / K / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = serve_cpu_baseline(lib, m, kvs[0])
+    line = {
+        "metric": "int8-weight decode tok/s (bs64)", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": wl["name"], "model": f"8b-shaped synthetic, seed {SEED_WEIGHTS}",
+                   "global_batch": B * world, "batch_per_gpu": B, "prompt": P,
+                   "kv_len_start": P + W, "kv_len_end": P + W + K, "parallelism": "single GPU per replica",
+                   "l2": f"inputs larger than L2: {weight_bytes(cfg) / 1e9:.2f} GB weights + "
+                         f"{kv_bytes / 1e9:.1f} GB KV per step"},
+        "prefill": {"tok_per_s": round(world * B * P / (pre_ms / 1e3), 1), "gpu_ms": round(pre_ms, 1),
+                    "wall_s": round(pre_wall, 2), "api": "q_llama_prefill_argmax, one sequence per call"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": B * (4 + 32),
+                "d2h_bytes_per_step": B * 4 + 4,
+                "api": "q_llama_decode_batch_argmax (host ids in and out, one call per step)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                     "kernel": "whole batched step (weights + f32 KV rows read once)",
+                     "step_bytes": int(step_bytes)},
+        "cpu_baseline": cpu,
+        "gpu_launches": launches,
+        "clocks": clk.summary(),
+    }
+    for kv in kvs:
+        lib.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(m))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def serve_cpu_baseline(lib, m, kv):
+    """The reference's q_llama_decode_step on the host cores continuing one of
+    the sequences (its GPU cache copied to the host arrays).  The reference
+    has no batch entry point: B sequences cost B times one, so its batch-B
+    tokens/s equals this single-sequence rate."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    cores = os.cpu_count() or 1
+    os.environ["TF_THREADS"] = str(min(cores, 64))
+    ref = oracle.load_reference()
+    if ref is None:
+        return None
+    if lib.q_llama_kv_sync_host(C.byref(m), C.byref(kv)) != 0:
+        llmq.check(lib)
+    logits = np.zeros((1, m.vocab), np.float32)
+    lt = llmq.host_tensor(logits)
+    tok, n, t_total = 1, 0, 0.0
+    while n < 32 and t_total < 15.0 and kv.len < kv.max_seq:
+        t0 = time.perf_counter()
+        ref.q_llama_decode_step(C.byref(m), C.byref(kv), tok, C.byref(lt))
+        t_total += time.perf_counter() - t0
+        tok = int(np.argmax(logits[0]))
+        n += 1
+    return {"value": round(n / t_total, 4), "unit": "tok/s", "cores": min(cores, 64), "kind": "reference",
+            "sample": f"{n} single-sequence decode steps at positions {kv.len - n}..{kv.len - 1} of one "
+                      f"of the sequences (the reference decodes a batch one sequence at a time)"}
+
+
 SWEEP_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]  # (out, in)
 
 
@@ -443,13 +587,15 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=240)
+    ap.add_argument("--steps", type=int, default=None, help="timed steps (default 240; serve64: 112)")
     ap.add_argument("--warmup", type=int, default=16)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["sweep"], default="8b")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (profiling runs)")
     args = ap.parse_args()
+    if args.steps is None:
+        args.steps = 128 - args.warmup if args.workload == "serve64" else 240
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -465,6 +611,8 @@ def main():
                 run_sweep(args)
         elif args.impl == "reference":
             run_reference(args, rank, world)
+        elif args.workload == "serve64":
+            run_serve(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

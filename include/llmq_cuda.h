@@ -214,6 +214,10 @@ void q_llama_prefill(const QLlamaModel *m, LlamaKV *kv, const int *ids, int n, T
  * on error. */
 int q_llama_prefill_argmax(const QLlamaModel *m, LlamaKV *kv, const int *ids, int n, Tensor *logits);
 
+/* Kernels launched by the last q_llama_decode_batch[_argmax] or
+ * q_llama_prefill[_argmax] call (diagnostic; no reference counterpart). */
+long long llmq_last_launches(void);
+
 /* Copies the GPU KV cache rows [0, kv->len) into kv->k / kv->v (the
  * reference-shaped host arrays).  Returns LLMQ_OK or an error code. */
 int q_llama_kv_sync_host(const QLlamaModel *m, LlamaKV *kv);

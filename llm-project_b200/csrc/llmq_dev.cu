@@ -68,12 +68,12 @@ struct DevCtx {
   uint8_t *wraw = nullptr, *wtile = nullptr;
   float *wscale = nullptr;
   size_t wraw_n = 0, wtile_n = 0, wscale_n = 0;
-  // tensor-core path scratch: activation codes, row scales, split-K sums and
-  // arrival counters (both kept zero between launches)
+  // tensor-core path scratch: activation codes, row scales, split-K sums (kept
+  // zero between launches)
   int8_t *tc_codes = nullptr;
   float *tc_as = nullptr;
-  int *tc_acc = nullptr, *tc_cnt = nullptr;
-  size_t tc_codes_n = 0, tc_as_n = 0, tc_acc_n = 0, tc_cnt_n = 0;
+  int *tc_acc = nullptr;
+  size_t tc_codes_n = 0, tc_as_n = 0, tc_acc_n = 0;
 };
 
 DevCtx g_ctx[kMaxDevices];
@@ -97,9 +97,18 @@ void free_mat(Mat &m) {
 // Every kernel asks for the largest shared-memory carveout, so consecutive
 // launches with different shared-memory needs never make an SM repartition
 // its L1 / shared memory between them.
+// The dynamic limit is `smem`, or less where the kernel's static shared memory
+// leaves less of the per-block maximum `optin`.
+int g_smem_optin = 0;
+long long g_launches = 0;       // kernels launched by the running multi-row call
+long long g_last_launches = 0;  // ... by the last completed one
 template <typename K>
 cudaError_t set_attr(K *fn, int smem) {
-  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncAttributes fa{};
+  cudaError_t e = cudaFuncGetAttributes(&fa, fn);
+  if (e != cudaSuccess) return e;
+  smem = std::min(smem, g_smem_optin - static_cast<int>(fa.sharedSizeBytes));
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
 }
@@ -152,6 +161,7 @@ DevCtx *get_ctx() {
   c.device = dev;
   c.num_sms = prop.multiProcessorCount;
   c.max_smem = static_cast<int>(prop.sharedMemPerBlockOptin) - 2048;  // room for static shared memory
+  g_smem_optin = static_cast<int>(prop.sharedMemPerBlockOptin);
   if (cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaStreamCreate failed");
     return nullptr;
@@ -172,6 +182,7 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<64>, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<128>, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_act_codes, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_tc_epilogue, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_norm_codes, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_append, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_scores, sm);
@@ -362,11 +373,8 @@ int plan_tc(DevCtx &c, const Mat &m, int rows, TcArgs &a) {
   a.stages = (int)std::max<size_t>((kTcStageBytes + SB - 1) / SB, std::min<size_t>(kTcMaxStages, kTcRingBytes / SB));
   a.rows = rows;
   a.err = c.err;
-  if (splits > 1 && (!ensure(&c.tc_acc, &c.tc_acc_n, (size_t)rows * m.Npad, true) ||
-                     !ensure(&c.tc_cnt, &c.tc_cnt_n, (size_t)tiles, true)))
-    return 0;
+  if (splits > 1 && !ensure(&c.tc_acc, &c.tc_acc_n, (size_t)rows * m.Npad, true)) return 0;
   a.acc = c.tc_acc;
-  a.cnt = c.tc_cnt;
   return 1;
 }
 
@@ -384,6 +392,15 @@ int launch_tc_gemm(const TcArgs &a, int KT, cudaStream_t st, bool pdl) {
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   CK(KT == 128 ? cudaLaunchKernelEx(&cfg, k_tc_gemm<128>, a) : cudaLaunchKernelEx(&cfg, k_tc_gemm<64>, a));
+  ++g_launches;
+  if (a.splits > 1) {
+    ++g_launches;
+    cfg.gridDim = dim3((a.rows * a.n_slabs + 3) / 4);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = 0;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    CK(cudaLaunchKernelEx(&cfg, k_tc_epilogue, a));
+  }
   return 1;
 }
 
@@ -459,6 +476,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  ++g_launches;
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
@@ -1037,12 +1055,15 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   aa.hd = hd;
   aa.smax = cfg.max_seq;
   aa.err = M->err;
-  AttnArgs probe{};
-  probe.n_heads = cfg.n_heads;
-  probe.n_kv = cfg.n_kv;
-  probe.hd = hd;
-  probe.max_seq = cfg.max_seq;
-  const size_t sc_smem = scores_smem(probe), pv_sm = pv_smem(probe);
+  const int group = cfg.n_heads / cfg.n_kv;
+  const size_t sc_sm = rows_scores_smem(group, hd), pv_sm = rows_pv_smem(group, hd, cfg.max_seq);
+  const int attn_threads = (group * hd + 31) / 32 * 32;
+  if (hd % 4 != 0 || group > kAttnMaxGroup || attn_threads > 1024 || pv_sm + 4096 > (size_t)g_smem_optin) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: batched attention needs head_dim %% 4 == 0, group <= %d, "
+                   "group*head_dim <= 1024 and max_seq %d short enough for shared memory", kAttnMaxGroup,
+                   cfg.max_seq);
+    return 0;
+  }
   auto norm = [&](const float *in, const float *gamma, const Mat &m, int nrows) {
     na.in = in;
     na.gamma = gamma;
@@ -1070,10 +1091,9 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
     if (!gemm(M->qkv[l], rows, TC_BIAS, M->bias_qkv[l], R.qkv, qd + 2 * kvd, nullptr)) return 0;
     aa.layer = l;
     CK(launch_pdl(k_rows_append, dim3(rows), dim3(256), 0, st, aa));
-    CK(launch_pdl(k_rows_scores, dim3((cfg.max_seq + kScoreChunk - 1) / kScoreChunk, cfg.n_kv, rows),
-                  dim3(kScoreThreads), sc_smem, st, aa));
-    CK(launch_pdl(k_rows_pv, dim3((hd + kPVSlice - 1) / kPVSlice, cfg.n_heads, rows), dim3(kPVThreads), pv_sm, st,
-                  aa));
+    CK(launch_pdl(k_rows_scores, dim3((cfg.max_seq + kRowScoreKeys - 1) / kRowScoreKeys, cfg.n_kv, rows),
+                  dim3(kRowScoreThreads), sc_sm, st, aa));
+    CK(launch_pdl(k_rows_pv, dim3(cfg.n_kv, rows), dim3(attn_threads), pv_sm, st, aa));
     CK(codes(R.ao, qd, M->wo[l]));
     if (!gemm(M->wo[l], rows, TC_RESID, nullptr, R.x, dm, nullptr)) return 0;
     CK(norm(R.x, M->ffn_norm[l], M->w13[l], rows));
@@ -1094,7 +1114,6 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   CK(cudaStreamSynchronize(st));
   if (R.h_err[0]) {
     if (c.tc_acc) cudaMemsetAsync(c.tc_acc, 0, c.tc_acc_n * sizeof(int), st);
-    if (c.tc_cnt) cudaMemsetAsync(c.tc_cnt, 0, c.tc_cnt_n * sizeof(int), st);
     cudaMemsetAsync(R.argmax, 0, (size_t)R.lm_cap * sizeof(unsigned long long), st);
     return reset_after_device_error(M, R.h_err[0]);
   }
@@ -1359,6 +1378,7 @@ int llmqd_decode_rows(const QLlamaModel *m, LlamaKV *const *kvs, const int *toke
     tmp.resize((size_t)B);
     ids = tmp.data();
   }
+  g_launches = 0;
   CK(cudaEventRecord(M->ev0, M->stream));
   for (int off = 0; off < B; off += kRowsPerPass) {
     const int n = std::min(kRowsPerPass, B - off);
@@ -1368,6 +1388,7 @@ int llmqd_decode_rows(const QLlamaModel *m, LlamaKV *const *kvs, const int *toke
   CK(cudaEventRecord(M->ev1, M->stream));
   CK(cudaEventSynchronize(M->ev1));
   cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
+  g_last_launches = g_launches;
   return 1;
 }
 
@@ -1390,6 +1411,7 @@ int llmqd_prefill(const QLlamaModel *m, const LlamaKV *kv, const int *ids, int n
     }
   std::vector<RowDesc> rows((size_t)std::min(n, kRowsPerPass));
   int last = -1;
+  g_launches = 0;
   CK(cudaEventRecord(M->ev0, M->stream));
   for (int off = 0; off < n; off += kRowsPerPass) {
     const int cnt = std::min(kRowsPerPass, n - off);
@@ -1401,6 +1423,7 @@ int llmqd_prefill(const QLlamaModel *m, const LlamaKV *kv, const int *ids, int n
   CK(cudaEventRecord(M->ev1, M->stream));
   CK(cudaEventSynchronize(M->ev1));
   cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
+  g_last_launches = g_launches;
   if (next) *next = last;
   return 1;
 }
@@ -1420,6 +1443,8 @@ int llmqd_kv_download(const QLlamaModel *m, const LlamaKV *kv, int len) {
 float llmqd_last_ms(void) { return g_last_ms; }
 
 // ---- diagnostics exported for tests and the benchmark (declared in llmq_cuda.h)
+LLMQ_API long long llmq_last_launches(void) { return g_last_launches; }
+
 LLMQ_API int llmq_expf_device(const float *x, float *y, long long n) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   if (n <= 0) return LLMQ_OK;

@@ -94,7 +94,7 @@ struct RowAttnArgs {
   float *scores;          // [rows][n_heads][smax]
   float *out;             // [rows][qd]
   const float *rope_cos, *rope_sin;  // [max_seq][hd/2]
-  int layer, n_heads, n_kv, hd, smax;
+  int layer, n_heads, n_kv, hd, smax;  // smax: the model's max_seq (score row stride)
   int *err;
 };
 
@@ -128,102 +128,205 @@ __global__ void __launch_bounds__(256) k_rows_append(const RowAttnArgs a) {
   }
 }
 
+// Sequential dot product acc + a[0]*b[0] + ... + a[n-1]*b[n-1] (each product
+// rounded, then added in index order) with 16-byte shared-memory loads; a and b
+// 16-byte aligned, n a multiple of 4.
+__device__ __forceinline__ float seq_dot_v4(const float *a, const float *b, int n, float acc) {
+  const float4 *a4 = reinterpret_cast<const float4 *>(a), *b4 = reinterpret_cast<const float4 *>(b);
+  const int n4 = n >> 2;
+  int i = 0;
+  for (; i + 2 <= n4; i += 2) {
+    const float4 x0 = a4[i], y0 = b4[i], x1 = a4[i + 1], y1 = b4[i + 1];
+    const float p0 = __fmul_rn(x0.x, y0.x), p1 = __fmul_rn(x0.y, y0.y), p2 = __fmul_rn(x0.z, y0.z),
+                p3 = __fmul_rn(x0.w, y0.w), p4 = __fmul_rn(x1.x, y1.x), p5 = __fmul_rn(x1.y, y1.y),
+                p6 = __fmul_rn(x1.z, y1.z), p7 = __fmul_rn(x1.w, y1.w);
+    acc = __fadd_rn(acc, p0);
+    acc = __fadd_rn(acc, p1);
+    acc = __fadd_rn(acc, p2);
+    acc = __fadd_rn(acc, p3);
+    acc = __fadd_rn(acc, p4);
+    acc = __fadd_rn(acc, p5);
+    acc = __fadd_rn(acc, p6);
+    acc = __fadd_rn(acc, p7);
+  }
+  if (i < n4) {
+    const float4 x0 = a4[i], y0 = b4[i];
+    acc = __fadd_rn(acc, __fmul_rn(x0.x, y0.x));
+    acc = __fadd_rn(acc, __fmul_rn(x0.y, y0.y));
+    acc = __fadd_rn(acc, __fmul_rn(x0.z, y0.z));
+    acc = __fadd_rn(acc, __fmul_rn(x0.w, y0.w));
+  }
+  return acc;
+}
+
 // Scores of one row's query group (one KV head) over one chunk of key
 // positions [p0, min(p0 + 64, pos + 1)) of its cache (llama.c:558-565): each a
-// sequential dot product over the head dimension, times 1/sqrt(hd).
-// Grid (ceil(smax / 64), n_kv, rows).
-__global__ void __launch_bounds__(kScoreThreads) k_rows_scores(const RowAttnArgs a) {
+// sequential dot product over the head dimension, times 1/sqrt(hd).  The keys
+// are staged in rows padded to hd + 4 floats, so the 16-byte loads of the 8
+// threads of a load phase (8 consecutive keys) hit distinct banks.
+// Grid (ceil(smax / 64), n_kv, rows), 256 threads; head_dim % 4 == 0.
+constexpr int kRowScoreKeys = 64;
+constexpr int kRowScoreThreads = 256;
+__host__ __device__ inline size_t rows_scores_smem(int group, int hd) {
+  return ((size_t)group * hd + (size_t)kRowScoreKeys * (hd + 4)) * sizeof(float);
+}
+__global__ void __launch_bounds__(kRowScoreThreads) k_rows_scores(const RowAttnArgs a) {
   extern __shared__ __align__(16) float sm_s[];
   pdl_launch_dependents();
   pdl_wait();
   const int tid = threadIdx.x, kvh = blockIdx.y, r = blockIdx.z;
   const RowDesc d = a.rd[r];
-  const int p0 = blockIdx.x * kScoreChunk;
+  const int p0 = blockIdx.x * kRowScoreKeys;
   if (d.pos < 0 || d.pos >= d.max_seq || p0 > d.pos) return;
-  const int hd = a.hd, group = a.n_heads / a.n_kv, qd = a.n_heads * hd;
-  const int stride = (hd & 3) == 0 ? hd + 4 : hd + 1;
-  const int hd4 = (hd + 3) & ~3;
-  float *qs = sm_s;                        // [group][hd4]
-  float *ks = sm_s + (size_t)group * hd4;  // [kScoreChunk][stride]
-  const int p1 = min(p0 + kScoreChunk, d.pos + 1);
-  stage_rows(ks, stride, d.k + row_cache_offset(d, a.layer, a.n_kv, kvh, hd), hd, p0, p1, 0, hd, tid,
-             kScoreThreads);
+  const int hd = a.hd, group = a.n_heads / a.n_kv, qd = a.n_heads * hd, ks = hd + 4;
+  float *qs = sm_s;                        // [group][hd]
+  float *kst = sm_s + (size_t)group * hd;  // [64][hd + 4]
+  const int p1 = min(p0 + kRowScoreKeys, d.pos + 1);
+  stage_rows(kst, ks, d.k + row_cache_offset(d, a.layer, a.n_kv, kvh, hd), hd, p0, p1, 0, hd, tid,
+             kRowScoreThreads);
   cp_async_commit();
-  const float *q = a.qr + (size_t)r * qd + (size_t)kvh * group * hd;
-  for (int i = tid; i < group * hd; i += kScoreThreads) {
-    const int g = i / hd, e = i - g * hd;
-    qs[g * hd4 + e] = q[i];
-  }
+  const float4 *q4 = reinterpret_cast<const float4 *>(a.qr + (size_t)r * qd + (size_t)kvh * group * hd);
+  for (int i = tid; i < group * hd / 4; i += kRowScoreThreads) reinterpret_cast<float4 *>(qs)[i] = q4[i];
   cp_async_wait<0>();
   __syncthreads();
   const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));  // llama.c:532
   float *srow = a.scores + ((size_t)r * a.n_heads + (size_t)kvh * group) * a.smax;
-  for (int i = tid; i < group * kScoreChunk; i += kScoreThreads) {
-    const int g = i / kScoreChunk, p = i - g * kScoreChunk;
+  for (int t = tid; t < group * kRowScoreKeys; t += kRowScoreThreads) {
+    const int g = t / kRowScoreKeys, p = t - g * kRowScoreKeys;
     if (p0 + p >= p1) continue;
-    const float dot = seq_dot(qs + (size_t)g * hd4, ks + (size_t)p * stride, 1, hd, 0.0f);  // llama.c:561
+    const float dot = seq_dot_v4(qs + (size_t)g * hd, kst + (size_t)p * ks, hd, 0.0f);  // llama.c:561
     srow[(size_t)g * a.smax + p0 + p] = __fmul_rn(dot, scale);
   }
 }
 
-// Softmax and the weighted sum of values for one row, one query head and a
-// slice of kPVSlice output dimensions (llama.c:566-575), as k_attn_pv.
-// Grid (ceil(hd / 32), n_heads, rows); (smax + kPVRing*kPVChunk*kPVSlice)
-// floats of dynamic shared memory.
-__global__ void __launch_bounds__(kPVThreads) k_rows_pv(const RowAttnArgs a) {
-  extern __shared__ __align__(16) float sm_v[];
-  __shared__ float s_red[32];
-  __shared__ float s_inv;
-  pdl_launch_dependents();
-  pdl_wait();
-  const int tid = threadIdx.x, h = blockIdx.y, r = blockIdx.z;
-  const RowDesc d = a.rd[r];
-  if (d.pos < 0 || d.pos >= d.max_seq) return;
-  const int d0 = blockIdx.x * kPVSlice;
-  const int np = d.pos + 1, hd = a.hd, group = a.n_heads / a.n_kv, kvh = h / group;
-  const int w = min(kPVSlice, hd - d0);
-  float *wts = sm_v;                                           // [smax]
-  float *ring = sm_v + (((size_t)a.smax + 3) & ~size_t(3));  // [kPVRing][kPVChunk][kPVSlice]
-  const float *vc = d.v + row_cache_offset(d, a.layer, a.n_kv, kvh, hd);
-  const int nchunks = (np + kPVChunk - 1) / kPVChunk;
-  for (int c = 0; c < kPVRing; ++c) {
-    if (c < nchunks)
-      stage_rows(ring + (size_t)c * kPVChunk * kPVSlice, kPVSlice, vc, hd, c * kPVChunk,
-                 min((c + 1) * kPVChunk, np), d0, w, tid, kPVThreads);
-    cp_async_commit();
-  }
-  const float *sc = a.scores + ((size_t)r * a.n_heads + h) * a.smax;
-  float m = -INFINITY;
-  for (int p = tid; p < np; p += kPVThreads) {
-    const float s = sc[p];
-    wts[p] = s;
-    m = fmaxf(m, s);
-  }
-  m = block_max<kPVThreads>(m, s_red);
-  for (int p = tid; p < np; p += kPVThreads) wts[p] = libm_expf(__fsub_rn(wts[p], m));
-  __syncthreads();
+// Softmax and values of one row for one KV head and its whole query group
+// (llama.c:566-575), in one CTA of group * hd threads (rounded up to a warp):
+// the group's scores come into shared memory; per head the max, expf(s - max),
+// the sequential sum of the exponentials (one thread per head) and
+// w = e * (1/sum); then the values [0, pos] stream through a ring
+// (kPvStages stages of kPvKeys positions, one bulk copy each) and thread (g, e)
+// forms out[g][e] = sum_p w[g][p] * v[p][e] sequentially in position order.
+// Each value row is read once for the whole group.  Grid (n_kv, rows); dynamic
+// shared memory rows_pv_smem().
+constexpr int kPvKeys = 64;
+constexpr int kPvStages = 2;
+constexpr int kAttnMaxGroup = 16;
+__host__ __device__ inline size_t rows_pv_smem(int group, int hd, int smax) {
+  return ((size_t)kPvStages * kPvKeys * hd + (size_t)group * ((smax + 3) & ~3)) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(1024) k_rows_pv(const RowAttnArgs a) {
+  extern __shared__ __align__(16) float sm_a[];
+  __shared__ __align__(8) uint64_t full[kPvStages];
+  __shared__ float s_max[kAttnMaxGroup][32];
+  __shared__ float s_inv[kAttnMaxGroup];
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x;
+  const int kvh = blockIdx.x, r = blockIdx.y;
+  const int hd = a.hd, group = a.n_heads / a.n_kv, qd = a.n_heads * hd, smax4 = (a.smax + 3) & ~3;
+  float *ring = sm_a;                                     // [S][kPvKeys][hd]
+  float *wts = ring + (size_t)kPvStages * kPvKeys * hd;  // [group][smax4]
   if (tid == 0) {
-    const float sum = seq_sum(wts, 1, np, 0.0f);  // llama.c:567
-    s_inv = __fdiv_rn(1.0f, sum);
+    for (int i = 0; i < kPvStages; ++i) mbar_init(&full[i], 1);
+    fence_mbar_init();
+    s_abort = 0;
   }
   __syncthreads();
-  const float inv = s_inv;
-  for (int p = tid; p < np; p += kPVThreads) wts[p] = __fmul_rn(wts[p], inv);
-  float o = 0.0f;
-  for (int c = 0; c < nchunks; ++c) {
-    cp_async_wait<kPVRing - 1>();
-    __syncthreads();
-    const float *buf = ring + (size_t)(c % kPVRing) * kPVChunk * kPVSlice;
-    const int pe = min((c + 1) * kPVChunk, np) - c * kPVChunk;
-    if (tid < w) o = seq_dot(wts + (size_t)c * kPVChunk, buf + tid, kPVSlice, pe, o);  // llama.c:574
-    __syncthreads();
-    const int nc = c + kPVRing;
-    if (nc < nchunks)
-      stage_rows(ring + (size_t)(nc % kPVRing) * kPVChunk * kPVSlice, kPVSlice, vc, hd, nc * kPVChunk,
-                 min((nc + 1) * kPVChunk, np), d0, w, tid, kPVThreads);
-    cp_async_commit();
+  const RowDesc d = a.rd[r];  // written by the host before the pass: no wait needed
+  if (d.pos < 0 || d.pos >= d.max_seq) return;  // flagged by k_rows_append
+  const int np = d.pos + 1, nch = (np + kPvKeys - 1) / kPvKeys;
+  const float *vc = d.v + row_cache_offset(d, a.layer, a.n_kv, kvh, hd);
+  const uint32_t row_bytes = (uint32_t)hd * 4u;
+  auto issue = [&](int c) {  // thread 0
+    const int st = c % kPvStages, c0 = c * kPvKeys, cnt = min(kPvKeys, np - c0);
+    mbar_expect_tx(&full[st], (uint32_t)cnt * row_bytes);
+    bulk_load(ring + (size_t)st * kPvKeys * hd, vc + (size_t)c0 * hd, (uint32_t)cnt * row_bytes, &full[st]);
+  };
+  pdl_launch_dependents();
+  pdl_wait();  // the values of this step's rows and the scores come from the previous kernels
+  int issued = 0;
+  if (tid == 0)
+    for (; issued < kPvStages && issued < nch; ++issued) issue(issued);
+  // ---- softmax per head (llama.c:566-572)
+  const float *sc = a.scores + ((size_t)r * a.n_heads + (size_t)kvh * group) * a.smax;
+  float mloc[kAttnMaxGroup];
+  for (int g = 0; g < group; ++g) {
+    float m = -INFINITY;
+    for (int p = tid; p < np; p += nthr) {
+      const float v = sc[(size_t)g * a.smax + p];
+      wts[(size_t)g * smax4 + p] = v;
+      m = fmaxf(m, v);
+    }
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    mloc[g] = m;
   }
-  if (tid < w) a.out[(size_t)r * a.n_heads * hd + (size_t)h * hd + d0 + tid] = o;
+  if (lane == 0)
+    for (int g = 0; g < group; ++g) s_max[g][warp] = mloc[g];
+  __syncthreads();
+  if (tid < group) {
+    float m = -INFINITY;
+    for (int w = 0; w < (nthr + 31) / 32; ++w) m = fmaxf(m, s_max[tid][w]);
+    s_max[tid][0] = m;
+  }
+  __syncthreads();
+  for (int t = tid; t < group * np; t += nthr) {
+    const int g = t / np, p = t - g * np;
+    float *e = wts + (size_t)g * smax4 + p;
+    *e = libm_expf(__fsub_rn(*e, s_max[g][0]));
+  }
+  __syncthreads();
+  if (tid < group) s_inv[tid] = __fdiv_rn(1.0f, seq_sum(wts + (size_t)tid * smax4, 1, np, 0.0f));  // llama.c:567
+  __syncthreads();
+  for (int t = tid; t < group * np; t += nthr) {
+    const int g = t / np, p = t - g * np;
+    wts[(size_t)g * smax4 + p] = __fmul_rn(wts[(size_t)g * smax4 + p], s_inv[g]);
+  }
+  __syncthreads();
+  // ---- weighted sum of the values (llama.c:573-575)
+  const int g = tid / hd, e = tid - g * hd;
+  const float *wg = wts + (size_t)min(g, group - 1) * smax4;
+  float o = 0.0f;
+  int c = 0;
+  for (; c < nch; ++c) {
+    const int st = c % kPvStages;
+    const bool got = mbar_wait_bounded(&full[st], (uint32_t)(c / kPvStages) & 1u);
+    if (!got) s_abort = 1;
+    const float *buf = ring + (size_t)st * kPvKeys * hd + e;
+    const int c0 = c * kPvKeys, cnt = min(kPvKeys, np - c0);
+    if (g < group && got) {
+      const float4 *w4 = reinterpret_cast<const float4 *>(wg + c0);
+      int p = 0;
+      for (; p + 8 <= cnt; p += 8) {
+        const float4 wa = w4[p >> 2], wb = w4[(p >> 2) + 1];
+        const float v0 = buf[(size_t)(p + 0) * hd], v1 = buf[(size_t)(p + 1) * hd], v2 = buf[(size_t)(p + 2) * hd],
+                    v3 = buf[(size_t)(p + 3) * hd], v4 = buf[(size_t)(p + 4) * hd], v5 = buf[(size_t)(p + 5) * hd],
+                    v6 = buf[(size_t)(p + 6) * hd], v7 = buf[(size_t)(p + 7) * hd];
+        const float q0 = __fmul_rn(wa.x, v0), q1 = __fmul_rn(wa.y, v1), q2 = __fmul_rn(wa.z, v2),
+                    q3 = __fmul_rn(wa.w, v3), q4 = __fmul_rn(wb.x, v4), q5 = __fmul_rn(wb.y, v5),
+                    q6 = __fmul_rn(wb.z, v6), q7 = __fmul_rn(wb.w, v7);
+        o = __fadd_rn(o, q0);
+        o = __fadd_rn(o, q1);
+        o = __fadd_rn(o, q2);
+        o = __fadd_rn(o, q3);
+        o = __fadd_rn(o, q4);
+        o = __fadd_rn(o, q5);
+        o = __fadd_rn(o, q6);
+        o = __fadd_rn(o, q7);
+      }
+      for (; p < cnt; ++p) o = __fadd_rn(o, __fmul_rn(wg[c0 + p], buf[(size_t)p * hd]));  // llama.c:574
+    }
+    __syncthreads();
+    if (s_abort) break;  // chunk c stays counted as outstanding
+    if (tid == 0 && issued < nch) issue(issued++);
+  }
+  if (s_abort) {
+    if (tid == 0) {
+      atomicOr(a.err, ERR_TIMEOUT);
+      for (int t = c; t < issued; ++t) mbar_wait_bounded(&full[t % kPvStages], (uint32_t)(t / kPvStages) & 1u);
+    }
+    return;
+  }
+  if (g < group) a.out[(size_t)r * qd + (size_t)(kvh * group + g) * hd + e] = o;
 }
 
 // Greedy ids of the rows (first maximum: sampler.c:8-21) from the lm-head

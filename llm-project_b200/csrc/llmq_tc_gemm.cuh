@@ -133,8 +133,7 @@ struct TcArgs {
   const float *bias;      // TC_BIAS, physical order
   int N;                  // valid physical columns (TC_SWIGLU: output columns)
   int Npad, n_slabs, n_ktiles, n_rb, splits, stages, rows, epi;
-  int *acc;               // splits > 1: [rows][Npad] int32, zero before and after
-  int *cnt;               // splits > 1: [n_slabs * n_rb] arrivals, zero before and after
+  int *acc;               // splits > 1: [rows][Npad] int32, zero before and after (k_tc_epilogue)
   int *err;
   unsigned long long *argmax;  // TC_LOGITS: [rows] keys, zero before the launch
   float *out;             // [rows][ld]
@@ -199,7 +198,7 @@ __device__ __forceinline__ void red_add_s32(int *p, int v) {
 // the MMAs.  The accumulator then goes TMEM -> shared memory (64 rows at a
 // time) so that every warp works on whole rows: with one split it applies the
 // epilogue directly; otherwise it adds the block into `acc` (integer adds: the
-// order does not matter) and the last split to arrive applies the epilogue.
+// order does not matter) and k_tc_epilogue, the next launch, applies it.
 template <int KT>
 __global__ void __launch_bounds__(kTcThreads) k_tc_gemm(const TcArgs a) {
   constexpr int WB = kNT * KT;       // weight tile bytes
@@ -212,7 +211,7 @@ __global__ void __launch_bounds__(kTcThreads) k_tc_gemm(const TcArgs a) {
   __shared__ __align__(8) uint64_t empty[kTcMaxStages];
   __shared__ __align__(8) uint64_t accb;
   __shared__ uint32_t s_tmem;
-  __shared__ int s_abort, s_last;
+  __shared__ int s_abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int S = a.stages;
   const int split = blockIdx.x % a.splits;
@@ -334,32 +333,30 @@ __global__ void __launch_bounds__(kTcThreads) k_tc_gemm(const TcArgs a) {
     __syncthreads();
   }
   if (tid == 0 && !ok) atomicOr(a.err, ERR_TIMEOUT);
-  if (!direct) {
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = atomicAdd(a.cnt + tile, 1) == a.splits - 1;
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      for (int r = warp; r < rows_here; r += kTcThreads / 32) {
-        const int m = row0 + r;
-        int *accr = a.acc + (size_t)m * a.Npad + p0;
-        int v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          v[i] = __ldcg(accr + lane + 32 * i);
-          __stcg(accr + lane + 32 * i, 0);
-        }
-        tc_epilogue_lane(a, m, slab, lane, v);
-      }
-      if (tid == 0) a.cnt[tile] = 0;
-    }
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
+}
+
+// Epilogue of a split-K product: one warp per (row, slab) takes the summed
+// int32 block from `acc`, re-zeroes it and applies the epilogue.
+// Grid ceil(rows * n_slabs / 4) x 128 threads.
+__global__ void __launch_bounds__(128) k_tc_epilogue(const TcArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (gw >= a.rows * a.n_slabs) return;
+  const int m = gw % a.rows, slab = gw / a.rows;
+  int *accr = a.acc + (size_t)m * a.Npad + slab * kNT;
+  int v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __ldcg(accr + lane + 32 * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) __stcg(accr + lane + 32 * i, 0);
+  tc_epilogue_lane(a, m, slab, lane, v);
 }
 
 }  // namespace llmq

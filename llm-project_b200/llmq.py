@@ -111,6 +111,7 @@ SIGNATURES = {
     "q_llama_decode_batch_argmax": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(C.POINTER(LlamaKV)), c_int_p,
                                               C.c_int, c_int_p]),
     "q_llama_prefill": (None, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), c_int_p, C.c_int, C.POINTER(Tensor)]),
+    "llmq_last_launches": (C.c_longlong, []),
     "q_llama_prefill_argmax": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), c_int_p, C.c_int,
                                          C.POINTER(Tensor)]),
 }
