@@ -1,7 +1,7 @@
 """Benchmark: int8 (W8A8) LLaMA-family KV-cache decode on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload 8b|8b2|tiny|serve64|sweep]
+                    [--workload 8b|8b2|tiny|serve64|70b|sweep]
 
 Default workload: LLaMA-3-8B-shaped int8 model
 (dm 4096, 32 layers, 32/8 heads, hd 128, dff 14336, vocab 128256, rope 5e5),
@@ -50,6 +50,10 @@ WORKLOADS = {
                              d_ff=14336, rope_base=500000.0, eps=1e-5), prompt=2048, gen=128, batch=64,
                     name="llama3-8b-shaped int8 W8A8 batched serving: 64 sequences, 2048-id prompts prefilled, "
                          "then batched greedy decode"),
+    "70b": dict(cfg=dict(vocab=128256, d_model=8192, n_layers=80, n_heads=64, n_kv=8, head_dim=128, d_ff=28672,
+                         rope_base=500000.0, eps=1e-5), prompt=1024, gen=256, tp=True,
+                name="llama3-70b-shaped int8 W8A8, batch 1, tensor-parallel over all GPUs: 1024-id prompt then "
+                     "greedy decode"),
     "tiny": dict(cfg=dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768,
                           rope_base=10000.0, eps=1e-5), prompt=16, gen=240,
                  name="tiny llama int8 W8A8, batch 1: 16-id prompt then greedy decode"),
@@ -397,6 +401,107 @@ def run_serve(args, rank, world):
         print(json.dumps(line), flush=True)
 
 
+def run_tp(args, rank, world):
+    """one sequence decoded by a tensor-parallel group of all N
+    GPUs (N = 1: the whole model on one GPU).  Weights: the fast seeded
+    generator (uniform int8 codes, per-column scales), shard per rank.  A step
+    is one token; value = tokens/s of the sequence (strong scaling)."""
+    lib = llmq.load()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if lib.q_llama_set_device(local) != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    wl = WORKLOADS[args.workload]
+    cfg = wl["cfg"]
+    P, W, K = args.prompt or wl["prompt"], args.warmup, args.steps
+    max_seq = P + W + K
+    os.environ.setdefault("LLMQ_THREADS", str(max(1, (os.cpu_count() or 1) // world)))
+    dist = None
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        llmq.tp_bootstrap(lib, rank, world)
+    c = llmq.config(max_seq=max_seq, **cfg)
+    m = llmq.QLlamaModel()
+    t0 = time.time()
+    if lib.llmq_synth_model_fast_shard(C.byref(c), SEED_WEIGHTS, rank, world, C.byref(m)) != 0:
+        llmq.check(lib)
+    log(f"rank {rank}: shard built in {time.time() - t0:.1f}s")
+    t0 = time.time()
+    if lib.q_llama_model_upload(C.byref(m)) != 0:
+        llmq.check(lib)
+    log(f"rank {rank}: uploaded in {time.time() - t0:.1f}s")
+    kv = lib.q_llama_kv_create(C.byref(m))
+    llmq.check(lib)
+    nxt = -1
+    for t in prompt_ids(cfg, P):
+        nxt = lib.q_llama_decode_step_argmax(C.byref(m), C.byref(kv), int(t), None)
+    llmq.check(lib)
+    ids = (C.c_int * max(W, K, 1))()
+    if lib.q_llama_generate(C.byref(m), C.byref(kv), nxt, W, ids) != 0:
+        llmq.check(lib)
+    start_len, start_tok = kv.len, ids[W - 1]
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    if dist is not None:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        if lib.q_llama_generate(C.byref(m), C.byref(kv), start_tok, K, ids) != 0:
+            llmq.check(lib)
+        ms = max_over_ranks(float(lib.q_llama_last_step_ms()))
+    gen_ids = [ids[i] for i in range(K)]
+    value = K / (ms / 1e3)
+    # e2e: the same positions through q_llama_decode_step (host token in, whole
+    # logits row out on every rank, host argmax)
+    kv.len = start_len
+    logits = np.zeros((1, cfg["vocab"]), np.float32)
+    lt = llmq.host_tensor(logits)
+    tok, e2e_ids = start_tok, []
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(K):
+        lib.q_llama_decode_step(C.byref(m), C.byref(kv), tok, C.byref(lt))
+        tok = int(np.argmax(logits[0]))
+        e2e_ids.append(tok)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    llmq.check(lib)
+    hbm_peak = hbm_peak_gbs()
+    per_rank_bytes = weight_bytes(cfg) / world
+    achieved = per_rank_bytes / (ms / K / 1e3) / 1e9
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
+        "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic (seeded uniform int8 codes, per-column scales)",
+        "config": {"workload": wl["name"], "model": f"70b-shaped synthetic, seed {SEED_WEIGHTS}",
+                   "global_batch": 1, "prompt": P, "kv_len_start": start_len, "kv_len_end": start_len + K,
+                   "parallelism": f"tp{world}",
+                   "l2": f"inputs larger than L2: {per_rank_bytes / 1e9:.2f} GB of int8 weights per GPU per step"},
+        "e2e": {"value": round(K / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": 16 + 4 * cfg["vocab"],
+                "api": "q_llama_decode_step on every rank (host token, whole f32 logits row, host argmax)",
+                "same_tokens_as_value_run": e2e_ids == gen_ids},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                     "kernel": "whole decode step per GPU (this rank's int8 weights read once)"},
+        "cpu_baseline": None,
+        "gpu_launches": K * int(lib.llmq_kernels_per_step(C.byref(m))),
+        "clocks": clk.summary(),
+    }
+    lib.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(m))
+    if world > 1:
+        dist.barrier()
+        lib.q_llama_tp_shutdown()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def serve_cpu_baseline(lib, m, kv):
     """The reference's q_llama_decode_step on the host cores continuing one of
     the sequences (its GPU cache copied to the host arrays).  The reference
@@ -537,6 +642,11 @@ def run_reference(args, rank, world):
     ref = oracle.load_reference()
     wl = WORKLOADS[args.workload]
     cfg = wl["cfg"]
+    if wl.get("tp") or "batch" in wl:
+        print(json.dumps({"impl": "reference", "unavailable": f"workload {args.workload}: the reference CPU arm runs "
+                                                              "the single-sequence 8b / tiny workloads only"}),
+              flush=True)
+        return
     if ref is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built from the reference "
                                                             "sources (make -C oracle)"}), flush=True)
@@ -613,6 +723,8 @@ def main():
             run_reference(args, rank, world)
         elif args.workload == "serve64":
             run_serve(args, rank, world)
+        elif WORKLOADS[args.workload].get("tp"):
+            run_tp(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

@@ -218,6 +218,24 @@ int q_llama_prefill_argmax(const QLlamaModel *m, LlamaKV *kv, const int *ids, in
  * q_llama_prefill[_argmax] call (diagnostic; no reference counterpart). */
 long long llmq_last_launches(void);
 
+/* ---- Tensor parallelism (the `q_llama_tp_init` extension; the reference is
+ * single-process).  One process per GPU: select the device with
+ * q_llama_set_device, have rank 0 make an id with q_llama_tp_unique_id and
+ * hand its 128 bytes to every rank, then call q_llama_tp_init on all ranks
+ * (it returns once all have joined).  A model whose tensors are shard `rank`
+ * of `world` (llmq_synth_model_shard, q_llama_model_shard) then decodes as
+ * one: Wq/Wk/Wv/Wgate/Wup and the lm-head by columns, Wo/Wdown by rows, with
+ * an NCCL max-reduce of the activation absmax and a sum-reduce of the exact
+ * int32 partial products per row-parallel product, and a max-reduce of the
+ * argmax key.  Logits and greedy ids equal the single-GPU ones bit for bit;
+ * q_llama_decode_step returns the whole logits row on every rank, and
+ * q_llama_kv_sync_host fills only this rank's KV heads.  All ranks must make
+ * the same calls in the same order.  Returns 0 or an error code. */
+int q_llama_tp_unique_id(unsigned char *id /* 128 bytes */);
+int q_llama_tp_init(int rank, int world, const unsigned char *id);
+/* Releases the group's communicator (and the decode graphs that use it). */
+void q_llama_tp_shutdown(void);
+
 /* Copies the GPU KV cache rows [0, kv->len) into kv->k / kv->v (the
  * reference-shaped host arrays).  Returns LLMQ_OK or an error code. */
 int q_llama_kv_sync_host(const QLlamaModel *m, LlamaKV *kv);
@@ -242,6 +260,29 @@ typedef struct {
  * Returns 0 or an error code. */
 int llmq_synth_model(const LlmqConfig *cfg, uint64_t seed, float stddev, int with_bias,
                      QLlamaModel *out);
+
+/* Tensor-parallel shard `rank` of `world` of the same synthetic model (no
+ * reference counterpart): Wq/Wk/Wv and b_q/b_k/b_v keep the columns of this
+ * rank's query and KV heads, Wgate/Wup its d_ff columns, lm_head its vocab
+ * columns; Wo and Wdown keep the rows of its query dims and d_ff slice.  Every
+ * kept code and per-column scale equals the whole model's (row shards keep the
+ * scale of the whole column).  wte and the norms are whole; the config fields
+ * are the whole model's.  Needs n_heads, n_kv, d_ff and vocab divisible by
+ * world.  Returns 0 or an error code. */
+int llmq_synth_model_shard(const LlmqConfig *cfg, uint64_t seed, float stddev, int with_bias, int rank,
+                           int world, QLlamaModel *out);
+
+/* Shard `rank` of `world` of a quickly generated benchmark model: codes uniform
+ * in [-127, 127] and per-column scales uniform in [2e-4, 1e-3), seeded per
+ * element, so a shard costs only its own elements (a 70B shard in seconds).
+ * Same layout and shard rules as llmq_synth_model_shard; no reference
+ * counterpart.  Returns 0 or an error code. */
+int llmq_synth_model_fast_shard(const LlmqConfig *cfg, uint64_t seed, int rank, int world, QLlamaModel *out);
+
+/* The same shard cut from a whole model held in host memory (for instance one
+ * read by q_llama_model_load).  `out` is freed with q_llama_model_free.
+ * Returns 0 or an error code. */
+int q_llama_model_shard(const QLlamaModel *m, int rank, int world, QLlamaModel *out);
 
 /* Fills an existing QTensor with uniform codes in [-127, 127] and uniform scales
  * in [1e-3, 1e-2), seeded (the isolated matvec sweep's weights). */

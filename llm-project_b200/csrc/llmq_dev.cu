@@ -2,6 +2,8 @@
 // upload and tiling, the per-(model, cache) decode graphs, and the launchers of
 // the kernels in llmq_kernels.cuh.  Called only through llmq_internal.h.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
 #include <cmath>
@@ -102,6 +104,61 @@ void free_mat(Mat &m) {
 int g_smem_optin = 0;
 long long g_launches = 0;       // kernels launched by the running multi-row call
 long long g_last_launches = 0;  // ... by the last completed one
+
+// ------------------------------------------------------ tensor parallelism
+// One process per GPU; the ranks of a tensor-parallel group share an NCCL
+// communicator.  NCCL is loaded when the group is formed, so single-GPU use
+// never needs it.
+struct NcclApi {
+  void *h = nullptr;
+  ncclResult_t (*GetUniqueId)(ncclUniqueId *) = nullptr;
+  ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                            cudaStream_t) = nullptr;
+  ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*CommDestroy)(ncclComm_t) = nullptr;
+  const char *(*GetErrorString)(ncclResult_t) = nullptr;
+} g_nccl;
+
+struct TpGroup {
+  int rank = 0, world = 1, device = -1;
+  ncclComm_t comm = nullptr;
+} g_tp;
+
+int load_nccl() {
+  if (g_nccl.h) return 1;
+  void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+  if (!h) {
+    llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: tensor parallelism needs libnccl.so.2 (%s)", dlerror());
+    return 0;
+  }
+#define LLMQ_NCCL_SYM(field, name)                                                        \
+  g_nccl.field = reinterpret_cast<decltype(g_nccl.field)>(dlsym(h, name));              \
+  if (!g_nccl.field) {                                                                  \
+    llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: libnccl.so.2 lacks %s", name);         \
+    return 0;                                                                           \
+  }
+  LLMQ_NCCL_SYM(GetUniqueId, "ncclGetUniqueId")
+  LLMQ_NCCL_SYM(CommInitRank, "ncclCommInitRank")
+  LLMQ_NCCL_SYM(AllReduce, "ncclAllReduce")
+  LLMQ_NCCL_SYM(AllGather, "ncclAllGather")
+  LLMQ_NCCL_SYM(CommDestroy, "ncclCommDestroy")
+  LLMQ_NCCL_SYM(GetErrorString, "ncclGetErrorString")
+#undef LLMQ_NCCL_SYM
+  g_nccl.h = h;
+  return 1;
+}
+
+#define NK(call)                                                                                      \
+  do {                                                                                                \
+    const ncclResult_t r_ = (call);                                                                   \
+    if (r_ != ncclSuccess) {                                                                          \
+      llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: NCCL error %s at %s:%d", g_nccl.GetErrorString(r_), \
+                     __FILE__, __LINE__);                                                             \
+      return 0;                                                                                       \
+    }                                                                                                 \
+  } while (0)
 template <typename K>
 cudaError_t set_attr(K *fn, int smem) {
   cudaFuncAttributes fa{};
@@ -175,6 +232,9 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_EMBED_RMSNORM, EPI_QKV, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_QKV, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_RESID, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_ACC, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_row_absmax, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_tp_resid, 0);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_SWIGLU, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_LOGITS, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_attn_scores, sm);
@@ -519,6 +579,12 @@ struct DevModel {
   GemvPlan p_qkv, p_wo, p_w13, p_w2, p_lm;
   size_t attn_smem = 0;
   int max_npad = 0, max_slabs = 0;
+  // tensor parallelism: this model is shard tp_rank of tp_world (cfg holds the
+  // shard's head, d_ff and vocab counts; these keep the whole model's)
+  int tp_rank = 0, tp_world = 1, vocab_full = 0, kvd_full = 0;
+  float *tp_max = nullptr;      // reduced activation absmax of a row-parallel product
+  int *tp_acc = nullptr;        // [d_model] partial / reduced int32 sums
+  float *logits_full = nullptr; // [vocab_full] gathered logits
   std::vector<DevKV *> kvs;
   // per-kernel events while llmq_step_profile records a step outside a graph
   std::vector<cudaEvent_t> *prof = nullptr;
@@ -562,6 +628,8 @@ void release_model(DevModel *M) {
   free_mat(M->lm);
   for (auto *v : {&M->attn_norm, &M->ffn_norm, &M->bias_qkv})
     for (float *p : *v) cudaFree(p);
+  void *tp_ptrs[] = {M->tp_max, M->tp_acc, M->logits_full};
+  for (void *p : tp_ptrs) cudaFree(p);
   void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o, M->scores,
                       M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step};
   for (void *p : dev_ptrs) cudaFree(p);
@@ -609,6 +677,32 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   cfg.max_seq = m->max_seq;
   cfg.rope_base = m->rope_base;
   cfg.eps = m->eps;
+  M->vocab_full = m->vocab;
+  M->kvd_full = m->n_kv * m->head_dim;
+  {
+    // A shard of the tensor-parallel group (llmq_synth_model_shard,
+    // q_llama_model_shard) holds 1/world of the heads, d_ff and vocab columns.
+    const int Wsh = g_tp.world;
+    const bool shard = Wsh > 1 && m->n_heads % Wsh == 0 && m->blocks[0].Wq.cols == m->n_heads * m->head_dim / Wsh;
+    if (!shard && m->blocks[0].Wq.cols != m->n_heads * m->head_dim) {
+      llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: Wq has %d columns: neither the whole model nor a shard of the "
+                     "tensor-parallel group of %d", m->blocks[0].Wq.cols, Wsh);
+      return 0;
+    }
+    if (shard) {
+      if (g_tp.device != c.device) {
+        llmq_set_error(LLMQ_ERR_STATE, "libllmq_cuda: shard uploaded on device %d, group formed on %d", c.device,
+                       g_tp.device);
+        return 0;
+      }
+      M->tp_rank = g_tp.rank;
+      M->tp_world = Wsh;
+      cfg.n_heads /= Wsh;
+      cfg.n_kv /= Wsh;
+      cfg.d_ff /= Wsh;
+      cfg.vocab /= Wsh;
+    }
+  }
   const int dm = cfg.d_model, hd = cfg.head_dim, dff = cfg.d_ff, L = cfg.n_layers;
   M->qd = cfg.n_heads * hd;
   M->kvd = cfg.n_kv * hd;
@@ -718,7 +812,10 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   CK(cudaMallocHost(&M->h_step, sizeof(StepState)));
   CK(cudaMallocHost(&M->h_result, 4 * sizeof(int)));
   CK(cudaMallocHost(&M->h_tokens, (size_t)cfg.max_seq * sizeof(int)));
-  CK(cudaMallocHost(&M->h_logits, (size_t)cfg.vocab * sizeof(float)));
+  CK(cudaMallocHost(&M->h_logits, (size_t)M->vocab_full * sizeof(float)));
+  if (M->tp_world > 1 && (!dev_zeros(&M->tp_max, 1) || !dev_zeros(&M->tp_acc, dm) ||
+                          !dev_zeros(&M->logits_full, M->vocab_full)))
+    return 0;
   CK(cudaDeviceSynchronize());
   return 1;
 }
@@ -756,14 +853,15 @@ DevModel *get_model(const QLlamaModel *m) {
 // (per layer [max_seq][n_kv*hd]) and the head-major device layout
 // (per layer [n_kv][max_seq][hd]).
 int kv_transfer(DevModel *M, DevKV *K, const LlamaKV *kv, int len, cudaMemcpyKind dir) {
-  const int hd = M->cfg.head_dim, nkv = M->cfg.n_kv;
+  const int hd = M->cfg.head_dim, nkv = M->cfg.n_kv;  // this rank's KV heads
   const size_t per_layer = (size_t)K->max_seq * M->kvd;
+  const int h0 = M->tp_rank * nkv;                     // their first head in the host layout
   for (int l = 0; l < M->cfg.n_layers; ++l)
     for (int h = 0; h < nkv; ++h) {
       float *dk = K->k + l * per_layer + (size_t)h * K->max_seq * hd;
       float *dv = K->v + l * per_layer + (size_t)h * K->max_seq * hd;
-      float *hk = kv->k[l] + (size_t)h * hd, *hv = kv->v[l] + (size_t)h * hd;
-      const size_t hp = (size_t)M->kvd * sizeof(float), dp = (size_t)hd * sizeof(float);
+      float *hk = kv->k[l] + (size_t)(h0 + h) * hd, *hv = kv->v[l] + (size_t)(h0 + h) * hd;
+      const size_t hp = (size_t)M->kvd_full * sizeof(float), dp = (size_t)hd * sizeof(float);
       if (dir == cudaMemcpyHostToDevice) {
         CK(cudaMemcpy2D(dk, dp, hk, hp, dp, len, dir));
         CK(cudaMemcpy2D(dv, dp, hv, hp, dp, len, dir));
@@ -789,7 +887,7 @@ DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
     return it->second;
   }
   const LlmqConfig &cfg = M->cfg;
-  if (kv->n_layers != cfg.n_layers || kv->kv_dim != M->kvd || kv->max_seq <= 0 || kv->max_seq > cfg.max_seq) {
+  if (kv->n_layers != cfg.n_layers || kv->kv_dim != M->kvd_full || kv->max_seq <= 0 || kv->max_seq > cfg.max_seq) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: KV cache shape (%d layers, kv_dim %d, max_seq %d) does not match the model",
                    kv->n_layers, kv->kv_dim, kv->max_seq);
     return nullptr;
@@ -814,10 +912,34 @@ DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
   return K;
 }
 
+// A row-parallel product of one decode step (Wo or W2 shard, this rank's rows
+// of K): the activation scale needs the absmax of the whole row, so the ranks
+// max-reduce their local absmax first (quant.c:104-106); each rank then forms
+// its exact int32 partial sums, the ranks add them (integer adds: the result
+// equals the single-GPU sums bit for bit), and the residual update applies the
+// scales (quant.c:117, llama.c:578 / 589).
+int row_parallel(DevModel *M, const Mat &w, const GemvPlan &p, const float *in, cudaStream_t st) {
+  CK(launch_pdl(k_row_absmax, dim3(1), dim3(kThreads), 0, st, in, w.K, M->tp_max));
+  NK(g_nccl.AllReduce(M->tp_max, M->tp_max, 1, ncclFloat32, ncclMax, g_tp.comm, st));
+  GemvArgs a = base_args(w, p, M->acc, M->cnt, M->err);
+  a.in = in;
+  a.absmax_in = M->tp_max;
+  a.out = reinterpret_cast<float *>(M->tp_acc);
+  CK((launch_gemv<PRO_ABSMAX, EPI_ACC, 1>(a, p, st, true)));
+  NK(g_nccl.AllReduce(M->tp_acc, M->tp_acc, (size_t)w.N, ncclInt32, ncclSum, g_tp.comm, st));
+  CK(launch_pdl(k_tp_resid, dim3((w.N + 255) / 256), dim3(256), 0, st, M->x, static_cast<const int *>(M->tp_acc),
+                static_cast<const float *>(M->tp_max), w.ws, w.N));
+  return 1;
+}
+
 // Records one decode step into the model stream.  mode 0: token/pos come from
 // the device state (chained steps); 1: copied from h_step, result copied back;
 // 2: as 1, plus the logits.
 int record_step(DevModel *M, DevKV *K, int mode) {
+  if (M->tp_world > 1 && (!g_tp.comm || g_tp.world != M->tp_world)) {
+    llmq_set_error(LLMQ_ERR_STATE, "libllmq_cuda: the tensor-parallel group of this shard is gone");
+    return 0;
+  }
 #define PROF_MARK()                                                     \
   do {                                                                  \
     if (M->prof) {                                                      \
@@ -847,7 +969,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       if (l == 0) {
         a.wte_q = M->wte_q;
         a.wte_s = M->wte_s;
-        a.vocab = cfg.vocab;
+        a.vocab = M->vocab_full;
         a.x_out = M->x;
         CK((launch_gemv<PRO_EMBED_RMSNORM, EPI_QKV, 1>(a, M->p_qkv, st, false)));
       PROF_MARK();
@@ -875,7 +997,9 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       CK(launch_attention(a, st, true, 1));
       PROF_MARK();
     }
-    {
+    if (M->tp_world > 1) {
+      if (!row_parallel(M, M->wo[l], M->p_wo, M->o, st)) return 0;
+    } else {
       GemvArgs a = base_args(M->wo[l], M->p_wo, M->acc, M->cnt, M->err);
       a.in = M->o;
       a.out = M->x;
@@ -891,7 +1015,9 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       CK((launch_gemv<PRO_RMSNORM, EPI_SWIGLU, 1>(a, M->p_w13, st, true)));
       PROF_MARK();
     }
-    {
+    if (M->tp_world > 1) {
+      if (!row_parallel(M, M->w2[l], M->p_w2, M->h, st)) return 0;
+    } else {
       GemvArgs a = base_args(M->w2[l], M->p_w2, M->acc, M->cnt, M->err);
       a.in = M->h;
       a.out = M->x;
@@ -906,14 +1032,20 @@ int record_step(DevModel *M, DevKV *K, int mode) {
     a.eps = cfg.eps;
     a.out = M->logits;
     a.argmax = M->argmax;
+    a.idx_offset = M->tp_rank * cfg.vocab;
     CK((launch_gemv<PRO_RMSNORM, EPI_LOGITS, 1>(a, M->p_lm, st, true)));
       PROF_MARK();
+  }
+  if (M->tp_world > 1) {  // the first maximum over every shard's vocab slice (sampler.c:8-21)
+    NK(g_nccl.AllReduce(M->argmax, M->argmax, 1, ncclUint64, ncclMax, g_tp.comm, st));
+    if (mode == 2) NK(g_nccl.AllGather(M->logits, M->logits_full, (size_t)cfg.vocab, ncclFloat32, g_tp.comm, st));
   }
   CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st));
       PROF_MARK();
   if (mode > 0) CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
   if (mode == 2)
-    CK(cudaMemcpyAsync(M->h_logits, M->logits, (size_t)cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(M->h_logits, M->tp_world > 1 ? M->logits_full : M->logits,
+                       (size_t)M->vocab_full * sizeof(float), cudaMemcpyDeviceToHost, st));
 #undef PROF_MARK
   return 1;
 }
@@ -940,8 +1072,8 @@ int get_graph(DevModel *M, DevKV *K, int mode, cudaGraphExec_t *out) {
 }
 
 int check_step_inputs(DevModel *M, const LlamaKV *kv, int token, int n) {
-  if (token < 0 || token >= M->cfg.vocab) {
-    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: token id %d outside [0, %d)", token, M->cfg.vocab);
+  if (token < 0 || token >= M->vocab_full) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: token id %d outside [0, %d)", token, M->vocab_full);
     return 0;
   }
   if (kv->len < 0 || kv->len + n > kv->max_seq) {
@@ -1016,6 +1148,10 @@ int ensure_rows(DevModel *M, int rows, int lm_rows) {
 int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, float *logits_h, int *ids_h) {
   const LlmqConfig &cfg = M->cfg;
   cudaStream_t st = M->stream;
+  if (M->tp_world > 1) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: multi-row passes of a tensor-parallel shard are not supported");
+    return 0;
+  }
   const int dm = cfg.d_model, qd = M->qd, kvd = M->kvd, hd = cfg.head_dim, dff = cfg.d_ff;
   const int lm_rows = rows - lm0;
   if (!ensure_rows(M, rows, lm_rows)) return 0;
@@ -1319,7 +1455,7 @@ int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token, float *logi
   CK(cudaStreamSynchronize(M->stream));
   cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
   if (M->h_result[1]) return reset_after_device_error(M, M->h_result[1]);
-  if (logits) std::memcpy(logits, M->h_logits, (size_t)M->cfg.vocab * sizeof(float));
+  if (logits) std::memcpy(logits, M->h_logits, (size_t)M->vocab_full * sizeof(float));
   if (next) *next = M->h_result[0];
   return 1;
 }
@@ -1405,8 +1541,8 @@ int llmqd_prefill(const QLlamaModel *m, const LlamaKV *kv, const int *ids, int n
   DevKV *K = get_kv(M, kv);
   if (!K || !check_step_inputs(M, kv, 0, n)) return 0;
   for (int i = 0; i < n; ++i)
-    if (ids[i] < 0 || ids[i] >= M->cfg.vocab) {
-      llmq_set_error(LLMQ_ERR_ARG, "q_llama_prefill: token id %d at %d outside [0, %d)", ids[i], i, M->cfg.vocab);
+    if (ids[i] < 0 || ids[i] >= M->vocab_full) {
+      llmq_set_error(LLMQ_ERR_ARG, "q_llama_prefill: token id %d at %d outside [0, %d)", ids[i], i, M->vocab_full);
       return 0;
     }
   std::vector<RowDesc> rows((size_t)std::min(n, kRowsPerPass));
@@ -1546,7 +1682,85 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
 }
 
 // Number of kernels one decode step launches (for the benchmark's gpu_launches).
-LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) { return 6 * m->n_layers + 2; }
+LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  const DevModel *M = find_model(m);
+  return (M && M->tp_world > 1 ? 10 : 6) * m->n_layers + 2;  // + absmax and residual kernels per row-parallel product
+}
+
+// ------------------------------------------------- tensor-parallel group API
+LLMQ_API int q_llama_tp_unique_id(unsigned char *id) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!id) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_tp_unique_id: null buffer");
+    return LLMQ_ERR_ARG;
+  }
+  if (!load_nccl()) return q_llama_last_error();
+  ncclUniqueId u;
+  const ncclResult_t r = g_nccl.GetUniqueId(&u);
+  if (r != ncclSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "q_llama_tp_unique_id: %s", g_nccl.GetErrorString(r));
+    return LLMQ_ERR_CUDA;
+  }
+  static_assert(sizeof(u) == NCCL_UNIQUE_ID_BYTES, "NCCL id size");
+  std::memcpy(id, &u, sizeof(u));
+  return LLMQ_OK;
+}
+
+LLMQ_API int q_llama_tp_init(int rank, int world, const unsigned char *id) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (world < 1 || rank < 0 || rank >= world || (world > 1 && !id)) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_tp_init: bad rank %d / world %d", rank, world);
+    return LLMQ_ERR_ARG;
+  }
+  if (g_tp.comm) {
+    llmq_set_error(LLMQ_ERR_STATE, "q_llama_tp_init: a tensor-parallel group is already formed");
+    return LLMQ_ERR_STATE;
+  }
+  DevCtx *c = get_ctx();
+  if (!c) return q_llama_last_error();
+  if (world == 1) {
+    g_tp = TpGroup{0, 1, c->device, nullptr};
+    return LLMQ_OK;
+  }
+  if (!load_nccl()) return q_llama_last_error();
+  ncclUniqueId u;
+  std::memcpy(&u, id, sizeof(u));
+  ncclComm_t comm = nullptr;
+  ncclResult_t r = g_nccl.CommInitRank(&comm, world, u, rank);
+  if (r == ncclSuccess) {  // first collective outside any graph capture
+    int *one = nullptr;
+    if (cudaMalloc(&one, sizeof(int)) == cudaSuccess) {
+      r = g_nccl.AllReduce(one, one, 1, ncclInt32, ncclSum, comm, c->stream);
+      cudaStreamSynchronize(c->stream);
+      cudaFree(one);
+    }
+  }
+  if (r != ncclSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "q_llama_tp_init: %s", g_nccl.GetErrorString(r));
+    if (comm) g_nccl.CommDestroy(comm);
+    return LLMQ_ERR_CUDA;
+  }
+  g_tp = TpGroup{rank, world, c->device, comm};
+  return LLMQ_OK;
+}
+
+LLMQ_API void q_llama_tp_shutdown(void) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  // graphs that hold collectives of this communicator go first
+  for (auto &kv : g_models)
+    if (kv.second->tp_world > 1) {
+      cudaStreamSynchronize(kv.second->stream);
+      for (DevKV *K : kv.second->kvs)
+        for (auto &g : K->graph)
+          if (g) {
+            cudaGraphExecDestroy(g);
+            g = nullptr;
+          }
+    }
+  if (g_tp.comm) g_nccl.CommDestroy(g_tp.comm);
+  g_tp = TpGroup{};
+}
 
 }  // extern "C"
 

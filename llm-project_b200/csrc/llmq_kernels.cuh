@@ -141,7 +141,8 @@ enum Epilogue : int {
   EPI_QKV = 1,     // + bias; q and k to `out`, v appended to the cache
   EPI_RESID = 2,   // out[j] += as*ws*acc                           (Wo, W2)
   EPI_SWIGLU = 3,  // out[j] = SiLU(gate) * up                      (W1|W3)
-  EPI_LOGITS = 4   // logits + device argmax                        (lm-head)
+  EPI_LOGITS = 4,  // logits + device argmax                        (lm-head)
+  EPI_ACC = 5      // ((int *)out)[j] = acc: this rank's partial sum (row-parallel shard)
 };
 
 // Tile geometry: a tile is KT rows of k by kNT columns, stored as
@@ -180,6 +181,8 @@ struct GemvArgs {
   int qd, kvd, hd, max_seq;
   float *vcache;       // EPI_QKV: this layer's [n_kv][max_seq][hd]
   unsigned long long *argmax;
+  int idx_offset;      // EPI_LOGITS: global index of column 0 (vocab shard)
+  const float *absmax_in;  // PRO_ABSMAX: if set, the row's absmax over all shards (else computed here)
 };
 
 // Owner CTA of tile t under the contiguous split [c*T/G, (c+1)*T/G).
@@ -273,8 +276,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     for (int r = 0; r < a.rows && r < MR; ++r) {
       load_row(a.in + (size_t)r * a.K, r);
       float m = 0.0f;
-      for (int k = tid; k < a.K; k += kThreads) m = fmaxf(m, fabsf(xs[k]));
-      m = block_max<kThreads>(m, s_red);
+      if (a.absmax_in) {
+        m = a.absmax_in[r];
+      } else {
+        for (int k = tid; k < a.K; k += kThreads) m = fmaxf(m, fabsf(xs[k]));
+        m = block_max<kThreads>(m, s_red);
+      }
       const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;  // quant.c:106
       const float inv = __fdiv_rn(1.0f, as);                      // quant.c:107
       if (tid == 0) s_as[r] = as;
@@ -367,7 +374,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     __threadfence();
     // ---- fused epilogue for columns [slab*kNT, slab*kNT + kNT)
     const int p0 = static_cast<int>(slab) * kNT;
-    if (EPI == EPI_PLAIN || EPI == EPI_RESID) {
+    if (EPI == EPI_ACC) {
+      for (int r = 0; r < a.rows && r < MR; ++r)
+        for (int c = tid; c < kNT; c += kThreads) {
+          const int j = p0 + c;
+          const int v = atomicExch(a.acc + (size_t)r * a.Npad + j, 0);
+          if (j < a.N) reinterpret_cast<int *>(a.out)[(size_t)r * a.N + j] = v;
+        }
+    } else if (EPI == EPI_PLAIN || EPI == EPI_RESID) {
       for (int r = 0; r < a.rows && r < MR; ++r) {
         const float as = s_as[r];
         for (int c = tid; c < kNT; c += kThreads) {
@@ -392,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         if (j < a.N) {
           const float y = dequant(as, a.ws[j], v);
           a.out[j] = y;
-          const unsigned long long key = argmax_key(y, static_cast<uint32_t>(j));
+          const unsigned long long key = argmax_key(y, static_cast<uint32_t>(j + a.idx_offset));
           best = key > best ? key : best;
         }
       }
@@ -782,6 +796,32 @@ __global__ void k_repack_plain(const int8_t *src, int K, int N, int Kpad, int Np
     memcpy(&o, bytes, 16);
     reinterpret_cast<uint4 *>(dst)[ci] = o;
   }
+}
+
+// ---------------------------------------------------- tensor parallelism
+// Absmax of one row (quant.c:104-106), the local part of a row-parallel
+// product's activation scale; the ranks then max-reduce it.
+__global__ void __launch_bounds__(kThreads) k_row_absmax(const float *x, int n, float *out) {
+  __shared__ float s_red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  float m = 0.0f;
+  for (int k = threadIdx.x; k < n; k += kThreads) m = fmaxf(m, fabsf(x[k]));
+  m = block_max<kThreads>(m, s_red);
+  if (threadIdx.x == 0) *out = m;
+}
+
+// Residual update after the ranks' partial sums are added (exact in int32):
+// x[j] += (as * ws[j]) * acc[j] with as from the reduced absmax (quant.c:106,
+// 117; llama.c:578, 589).
+__global__ void k_tp_resid(float *x, const int *acc, const float *absmax, const float *ws, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  const float m = *absmax;
+  const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+  x[j] = __fadd_rn(x[j], dequant(as, ws[j], acc[j]));
 }
 
 // expf of a batch (tests compare this against the host libm over all inputs).

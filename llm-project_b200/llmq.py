@@ -94,6 +94,11 @@ SIGNATURES = {
     "llmq_synth_model": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_float, C.c_int,
                                    C.POINTER(QLlamaModel)]),
     "llmq_synth_qtensor": (None, [C.POINTER(QTensor), C.c_uint64]),
+    "llmq_synth_model_shard": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_float, C.c_int, C.c_int, C.c_int,
+                                         C.POINTER(QLlamaModel)]),
+    "llmq_synth_model_fast_shard": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_int, C.c_int,
+                                              C.POINTER(QLlamaModel)]),
+    "q_llama_model_shard": (C.c_int, [C.POINTER(QLlamaModel), C.c_int, C.c_int, C.POINTER(QLlamaModel)]),
     "q_llama_model_upload": (C.c_int, [C.POINTER(QLlamaModel)]),
     "q_llama_generate": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_int, c_int_p]),
     "q_llama_last_step_ms": (C.c_float, []),
@@ -112,6 +117,9 @@ SIGNATURES = {
                                               C.c_int, c_int_p]),
     "q_llama_prefill": (None, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), c_int_p, C.c_int, C.POINTER(Tensor)]),
     "llmq_last_launches": (C.c_longlong, []),
+    "q_llama_tp_unique_id": (C.c_int, [C.c_char_p]),
+    "q_llama_tp_init": (C.c_int, [C.c_int, C.c_int, C.c_char_p]),
+    "q_llama_tp_shutdown": (None, []),
     "q_llama_prefill_argmax": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), c_int_p, C.c_int,
                                          C.POINTER(Tensor)]),
 }
@@ -185,6 +193,29 @@ def kv_pointers(kvs) -> C.Array:
 
 def int_array(vals) -> C.Array:
     return (C.c_int * len(vals))(*[int(v) for v in vals])
+
+
+def tp_bootstrap(lib, rank: int, world: int) -> None:
+    """Forms the tensor-parallel group: rank 0 makes the NCCL id, the ranks'
+    torch.distributed process group (any backend) broadcasts its 128 bytes,
+    every rank joins with q_llama_tp_init.  Call after q_llama_set_device."""
+    import torch
+    import torch.distributed as dist
+    buf = C.create_string_buffer(128)
+    if rank == 0 and lib.q_llama_tp_unique_id(buf) != 0:
+        check(lib)
+    t = torch.tensor(list(buf.raw), dtype=torch.uint8)
+    dist.broadcast(t, 0)
+    if lib.q_llama_tp_init(rank, world, bytes(t.tolist())) != 0:
+        check(lib)
+
+
+def synth_shard(lib, cfg: dict, seed: int, rank: int, world: int, stddev=0.02, with_bias=False) -> QLlamaModel:
+    m = QLlamaModel()
+    c = config(**cfg)
+    if lib.llmq_synth_model_shard(C.byref(c), seed, stddev, 1 if with_bias else 0, rank, world, C.byref(m)) != 0:
+        check(lib)
+    return m
 
 
 def vec_array(t: Tensor) -> np.ndarray:

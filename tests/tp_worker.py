@@ -1,0 +1,80 @@
+"""One rank of the 2-GPU tensor-parallel parity check run by test_gpu_tp.py
+(launched with torch.distributed.run, one process per GPU).
+
+Every rank decodes its shard of the same synthetic model; rank 0 compares the
+whole logits rows (gathered by the library on every rank) and the greedy ids
+of q_llama_generate with the oracle's single-sequence decode of the whole
+model, bit for bit, and writes the verdicts to <out_dir>/tp.json."""
+from __future__ import annotations
+
+import ctypes as C
+import datetime
+import json
+import os
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+sys.path[:0] = [HERE, os.path.join(ROOT, "llm-project_b200"), os.path.join(ROOT, "oracle")]
+
+import numpy as np  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+import llmq  # noqa: E402
+import oracle  # noqa: E402
+from helpers import TINY, bits_equal, orc_decode, synth  # noqa: E402
+
+CASES = [
+    ("tiny_bias", TINY, True, [5, 77, 31999, 0, 1234, 42, 9, 17, 256, 3000]),
+    ("8b_shapes_2_layers", dict(vocab=128256, d_model=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128,
+                                d_ff=14336, max_seq=64, rope_base=500000.0, eps=1e-5), False, [17, 128000, 42]),
+]
+
+
+def main():
+    out_dir = sys.argv[1]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+    lib = llmq.load()
+    if lib.q_llama_set_device(int(os.environ["LOCAL_RANK"])) != 0:
+        llmq.check(lib)
+    llmq.tp_bootstrap(lib, rank, world)
+    verdicts = {}
+    for name, cfg, bias, ids in CASES:
+        sh = llmq.synth_shard(lib, cfg, 1234, rank, world, with_bias=bias)
+        kv = lib.q_llama_kv_create(C.byref(sh))
+        llmq.check(lib)
+        got = np.zeros((len(ids), cfg["vocab"]), np.float32)
+        row = np.zeros((1, cfg["vocab"]), np.float32)
+        t = llmq.host_tensor(row)
+        for i, tok in enumerate(ids):
+            lib.q_llama_decode_step(C.byref(sh), C.byref(kv), int(tok), C.byref(t))
+            llmq.check(lib)
+            got[i] = row[0]
+        n_gen = 6
+        gen = (C.c_int * n_gen)()
+        if lib.q_llama_generate(C.byref(sh), C.byref(kv), int(np.argmax(got[-1])), n_gen, gen) != 0:
+            llmq.check(lib)
+        if rank == 0:
+            orc = oracle.load_oracle()
+            full = synth(lib, cfg, seed=1234, with_bias=bias)
+            greedy = [int(np.argmax(got[-1]))]
+            for _ in range(n_gen):
+                greedy.append(int(np.argmax(orc_decode(orc, full, ids + greedy)[0][-1])))
+            want, _ = orc_decode(orc, full, ids)
+            verdicts[name + ".logits"] = bits_equal(got, want)
+            verdicts[name + ".generate"] = list(gen) == greedy[1:]
+            lib.q_llama_model_free(C.byref(full))
+        dist.barrier()
+        lib.llama_kv_free(C.byref(kv))
+        lib.q_llama_model_free(C.byref(sh))
+    dist.barrier()
+    lib.q_llama_tp_shutdown()
+    if rank == 0:
+        with open(os.path.join(out_dir, "tp.json"), "w") as f:
+            json.dump(verdicts, f)
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
