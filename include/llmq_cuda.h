@@ -138,7 +138,8 @@ void qmatmul(const Tensor *A, const QTensor *W, Tensor *C);
 /* Replaces llama.c:610-657 (llama.h:136).  Reads an LLMQ v2 checkpoint into
  * host memory exactly like the reference (0 on success, 1 with a message on
  * stderr on any error; the model is freed on failure) and uploads it to the
- * current GPU. */
+ * current GPU.  With a tensor-parallel group formed (q_llama_tp_init) it only
+ * reads: the whole model is then meant to be cut with q_llama_model_shard. */
 int q_llama_model_load(const char *path, QLlamaModel *out);
 
 /* Replaces llama.c:483-488 (llama.h:129).  Frees host arrays and the device copy

@@ -1578,6 +1578,8 @@ int llmqd_kv_download(const QLlamaModel *m, const LlamaKV *kv, int len) {
 
 float llmqd_last_ms(void) { return g_last_ms; }
 
+int llmqd_tp_world(void) { return g_tp.world; }
+
 // ---- diagnostics exported for tests and the benchmark (declared in llmq_cuda.h)
 LLMQ_API long long llmq_last_launches(void) { return g_last_launches; }
 

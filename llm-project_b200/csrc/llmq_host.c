@@ -253,7 +253,9 @@ LLMQ_API int q_llama_model_load(const char *path, QLlamaModel *out) {
     q_llama_model_free(out);
     return 1;
   }
-  if (!llmqd_model_upload(out)) {
+  /* with a tensor-parallel group formed the whole model is only read: it is
+   * meant to be cut with q_llama_model_shard, and each shard uploads itself */
+  if (llmqd_tp_world() <= 1 && !llmqd_model_upload(out)) {
     fprintf(stderr, "Error: '%s' could not be placed on the GPU (%s)\n", path, q_llama_last_error_message());
     q_llama_model_free(out);
     return 1;

@@ -46,6 +46,8 @@ LLMQ_HIDDEN int llmqd_decode_rows(const QLlamaModel *m, LlamaKV *const *kvs, con
 LLMQ_HIDDEN int llmqd_prefill(const QLlamaModel *m, const LlamaKV *kv, const int *ids, int n, float *logits,
                               int *next);
 LLMQ_HIDDEN float llmqd_last_ms(void);
+/* Size of this process's tensor-parallel group (1 if none). */
+LLMQ_HIDDEN int llmqd_tp_world(void);
 
 #ifdef __cplusplus
 }
