@@ -482,7 +482,14 @@ size_t scores_smem(const AttnArgs &a) {
   const int hd4 = (a.hd + 3) & ~3, stride = (a.hd & 3) == 0 ? a.hd + 4 : a.hd + 1;
   return ((size_t)(a.n_heads / a.n_kv) * hd4 + (size_t)kScoreChunk * stride) * sizeof(float);
 }
+// Shared memory of k_attn_pv: the weights, then the value ring or, when the
+// whole value slice fits in kPVWholeLimit, the whole slice.
+constexpr size_t kPVWholeLimit = 200 * 1024;
+size_t pv_whole_bytes(int max_seq) {
+  return ((((size_t)max_seq + 3) & ~size_t(3)) + (size_t)max_seq * kPVSlice) * sizeof(float);
+}
 size_t pv_smem(const AttnArgs &a) {
+  if (a.pv_whole) return pv_whole_bytes(a.max_seq);
   return ((((size_t)a.max_seq + 3) & ~size_t(3)) + (size_t)kPVRing * kPVChunk * kPVSlice) * sizeof(float);
 }
 
@@ -787,6 +794,7 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
     probe.n_kv = cfg.n_kv;
     probe.hd = hd;
     probe.max_seq = cfg.max_seq;
+    probe.pv_whole = pv_whole_bytes(cfg.max_seq) <= kPVWholeLimit;
     M->attn_smem = std::max(scores_smem(probe), pv_smem(probe));
   }
   if (!dev_zeros(&M->scores, (size_t)cfg.n_heads * cfg.max_seq)) return 0;
@@ -992,6 +1000,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       a.n_kv = cfg.n_kv;
       a.hd = cfg.head_dim;
       a.max_seq = K->max_seq;
+      a.pv_whole = pv_whole_bytes(K->max_seq) <= kPVWholeLimit;
       CK(launch_attention(a, st, true, 0));
       PROF_MARK();
       CK(launch_attention(a, st, true, 1));
@@ -1638,6 +1647,7 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
     at.n_kv = M->cfg.n_kv;
     at.hd = M->cfg.head_dim;
     at.max_seq = K->max_seq;
+    at.pv_whole = pv_whole_bytes(K->max_seq) <= kPVWholeLimit;
     launch = [&]() {
       const cudaError_t e = launch_attention(at, st, false, 0);
       return e != cudaSuccess ? e : launch_attention(at, st, false, 1);

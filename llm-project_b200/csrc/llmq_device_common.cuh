@@ -99,18 +99,104 @@ __device__ __forceinline__ float seq_sum(const float *v, int stride, int n, floa
 }
 
 // Sequential f32 dot product acc + a[0]*b[0] + a[1]*b[sb] + ..., each product
-// and each sum rounded on its own in C order; the 8 products of a group are
-// formed back to back (independent), then added one after another.
+// and each sum rounded on its own in C order.  Software-pipelined: the loads of
+// the next group of 8 are issued before the 8 adds of the current group, so
+// the chain advances at the add latency; products are independent and formed
+// back to back.  The arithmetic is the plain sequential loop's.
 __device__ __forceinline__ float seq_dot(const float *a, const float *b, int sb, int n, float acc) {
   int i = 0;
-  for (; i + 8 <= n; i += 8) {
-    float p[8];
+  if (n >= 8) {
+    float ca[8], cb[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) p[u] = __fmul_rn(a[i + u], b[(size_t)(i + u) * sb]);
+    for (int u = 0; u < 8; ++u) {
+      ca[u] = a[u];
+      cb[u] = b[(size_t)u * sb];
+    }
+    for (i = 8; i + 8 <= n; i += 8) {
+      float na[8], nb[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, p[u]);
+      for (int u = 0; u < 8; ++u) {
+        na[u] = a[i + u];
+        nb[u] = b[(size_t)(i + u) * sb];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(ca[u], cb[u]));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        ca[u] = na[u];
+        cb[u] = nb[u];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(ca[u], cb[u]));
   }
   for (; i < n; ++i) acc = __fadd_rn(acc, __fmul_rn(a[i], b[(size_t)i * sb]));
+  return acc;
+}
+
+// As seq_dot with 16-byte shared-memory loads: a and b 16-byte aligned, n a
+// multiple of 4.
+__device__ __forceinline__ float seq_dot_v4(const float *a, const float *b, int n, float acc) {
+  const float4 *a4 = reinterpret_cast<const float4 *>(a), *b4 = reinterpret_cast<const float4 *>(b);
+  const int n4 = n >> 2;
+  auto add4 = [&](const float4 x, const float4 y) {
+    const float p0 = __fmul_rn(x.x, y.x), p1 = __fmul_rn(x.y, y.y), p2 = __fmul_rn(x.z, y.z),
+                p3 = __fmul_rn(x.w, y.w);
+    acc = __fadd_rn(acc, p0);
+    acc = __fadd_rn(acc, p1);
+    acc = __fadd_rn(acc, p2);
+    acc = __fadd_rn(acc, p3);
+  };
+  int i = 0;
+  if (n4 >= 2) {
+    float4 x0 = a4[0], y0 = b4[0], x1 = a4[1], y1 = b4[1];
+    for (i = 2; i + 2 <= n4; i += 2) {
+      const float4 nx0 = a4[i], ny0 = b4[i], nx1 = a4[i + 1], ny1 = b4[i + 1];
+      add4(x0, y0);
+      add4(x1, y1);
+      x0 = nx0;
+      y0 = ny0;
+      x1 = nx1;
+      y1 = ny1;
+    }
+    add4(x0, y0);
+    add4(x1, y1);
+  }
+  if (i < n4) add4(a4[i], b4[i]);
+  return acc;
+}
+
+// Sequential dot product acc + (e[0]*s)*b[0] + (e[1]*s)*b[sb] + ..., each
+// product rounded as written, then added in index order (the weights
+// w = e * s of a softmax formed on the fly); pipelined as seq_dot.
+__device__ __forceinline__ float seq_dot_scaled(const float *e, float sc, const float *b, int sb, int n, float acc) {
+  int i = 0;
+  if (n >= 8) {
+    float cw[8], cb[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      cw[u] = __fmul_rn(e[u], sc);
+      cb[u] = b[(size_t)u * sb];
+    }
+    for (i = 8; i + 8 <= n; i += 8) {
+      float ne[8], nb[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        ne[u] = e[i + u];
+        nb[u] = b[(size_t)(i + u) * sb];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(cw[u], cb[u]));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        cw[u] = __fmul_rn(ne[u], sc);
+        cb[u] = nb[u];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = __fadd_rn(acc, __fmul_rn(cw[u], cb[u]));
+  }
+  for (; i < n; ++i) acc = __fadd_rn(acc, __fmul_rn(__fmul_rn(e[i], sc), b[(size_t)i * sb]));
   return acc;
 }
 

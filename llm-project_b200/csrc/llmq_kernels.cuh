@@ -234,21 +234,28 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   const int n = static_cast<int>(t_end - t_begin);
 
   if (tid == 0) {
-    for (int s = 0; s <= S; ++s) mbar_init(&bars[s], 1);  // S weight stages + the input row
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);  // one per weight stage
     fence_mbar_init();
     s_abort = 0;
   }
   __syncthreads();
   // Weights never depend on the previous kernel: start streaming them now.
+  // Only the first two stages go out before the wait: the input row is on the
+  // critical path (the RMSNorm chain needs all of it), so its loads must not
+  // queue behind the whole ring's copies.  The rest of the ring is issued
+  // right after the row's loads.
   int issued = 0;
-  if (tid == 0) {
-    const int first = n < S ? n : S;
-    for (; issued < first; ++issued) {
-      mbar_expect_tx(&bars[issued], kTileBytes);
-      bulk_load(stage0 + (size_t)issued * kTileBytes, a.w + (size_t)(t_begin + issued) * kTileBytes,
-                kTileBytes, &bars[issued]);
+  auto issue_to = [&](int upto) {
+    if (tid == 0) {
+      const int first = n < upto ? n : upto;
+      for (; issued < first; ++issued) {
+        mbar_expect_tx(&bars[issued], kTileBytes);
+        bulk_load(stage0 + (size_t)issued * kTileBytes, a.w + (size_t)(t_begin + issued) * kTileBytes,
+                  kTileBytes, &bars[issued]);
+      }
     }
-  }
+  };
+  issue_to(2);
   LLMQ_TSTAMP(1);
   pdl_launch_dependents();
   pdl_wait();
@@ -258,23 +265,20 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   // The input rows come from the previous kernel: copied into xs with one bulk
   // copy per row once that kernel's writes are visible (plain loads when the
   // row is not 16-byte sized and aligned).
-  uint64_t *bar_in = bars + S;
-  const bool bulk_in = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.in) & 15) == 0;
-  auto load_row = [&](const float *src, int phase) {
-    if (bulk_in && a.K > 0) {
-      if (tid == 0) {
-        mbar_expect_tx(bar_in, static_cast<uint32_t>(a.K) * 4u);
-        bulk_load(xs, src, static_cast<uint32_t>(a.K) * 4u, bar_in);
-      }
-      if (!mbar_wait_bounded(bar_in, static_cast<uint32_t>(phase & 1))) s_abort = 1;
+  const bool vec_in = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.in) & 15) == 0;
+  auto load_row = [&](const float *src) {
+    if (vec_in) {
+      const float4 *s4 = reinterpret_cast<const float4 *>(src);
+      for (int k = tid; k < a.K / 4; k += kThreads) reinterpret_cast<float4 *>(xs)[k] = s4[k];
     } else {
       for (int k = tid; k < a.K; k += kThreads) xs[k] = src[k];
     }
+    issue_to(S);
     __syncthreads();
   };
   if (PRO == PRO_ABSMAX) {
     for (int r = 0; r < a.rows && r < MR; ++r) {
-      load_row(a.in + (size_t)r * a.K, r);
+      load_row(a.in + (size_t)r * a.K);
       float m = 0.0f;
       if (a.absmax_in) {
         m = a.absmax_in[r];
@@ -304,9 +308,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         xs[k] = v;
         if (blockIdx.x == 0) a.x_out[k] = v;
       }
+      issue_to(S);
       __syncthreads();
     } else {
-      load_row(a.in, 0);
+      load_row(a.in);
     }
     LLMQ_TSTAMP(3);
     // The sum of squares (rmsnorm.c:15): the products are independent, so all
@@ -488,7 +493,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         }
       }
     }
-    __syncthreads();
+    // Stage s is refilled (after every thread has read it) only while tiles
+    // remain to be issued: i + S < n.  Without a refill there is nothing to wait
+    // for, which is the common case for matrices that fit in the ring.
+    if (i + S < n) __syncthreads();
     done = i + 1;
     if (s_abort) break;
     if (tid == 0 && issued < n) {
@@ -507,7 +515,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     if (tid == 0) {
       atomicOr(a.err, ERR_TIMEOUT);
       for (int i = done; i < issued; ++i) mbar_wait_bounded(&bars[i % S], static_cast<uint32_t>((i / S) & 1));
-      mbar_wait_bounded(bar_in, static_cast<uint32_t>((PRO == PRO_ABSMAX ? (a.rows - 1) : 0) & 1));
     }
     return;
   }
@@ -528,10 +535,11 @@ struct AttnArgs {
   const StepState *step;
   const float *rope_cos, *rope_sin;  // [max_seq][hd/2]
   int n_heads, n_kv, hd, max_seq;
+  int pv_whole;  // k_attn_pv stages the whole value slice at once (it fits in shared memory)
 };
 
-constexpr int kScoreChunk = 64;    // key positions per scores CTA
-constexpr int kScoreThreads = 256;
+constexpr int kScoreChunk = 32;    // key positions per scores CTA
+constexpr int kScoreThreads = 128;
 constexpr int kPVSlice = 32;       // output dims per softmax-V CTA
 constexpr int kPVThreads = 256;
 constexpr int kPVChunk = 128;      // value positions per staged chunk
@@ -616,7 +624,9 @@ __global__ void __launch_bounds__(kScoreThreads) k_attn_scores(const AttnArgs a)
     if (p0 + p >= p1) continue;
     const float *kr = ks + (size_t)p * stride;
     const float *qr = qs + (size_t)g * hd4;
-    const float dot = seq_dot(qr, kr, 1, hd, 0.0f);  // llama.c:561
+    // 16-byte loads when the rows allow (rows of hd + 4 floats: the 8 threads
+    // of a load phase, 8 consecutive keys, hit distinct banks)
+    const float dot = (hd & 3) == 0 ? seq_dot_v4(qr, kr, hd, 0.0f) : seq_dot(qr, kr, 1, hd, 0.0f);  // llama.c:561
     a.scores[(size_t)(kvh * group + g) * a.max_seq + p0 + p] = __fmul_rn(dot, scale);
   }
 }
@@ -645,6 +655,34 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
   float *ring = sm_v + (((size_t)a.max_seq + 3) & ~size_t(3));  // [kPVRing][kPVChunk][kPVSlice]
   const float *vc = a.vcache + (size_t)kvh * a.max_seq * hd;
   const int nchunks = (np + kPVChunk - 1) / kPVChunk;
+  if (a.pv_whole) {
+    // The whole slice [0, np) x [d0, d0 + w) is staged while the softmax runs;
+    // then one uninterrupted chain per output dimension, with w = e * (1/sum)
+    // formed inside it (same rounded products, no separate pass).
+    float *vs = ring;  // [np][kPVSlice]
+    stage_rows(vs, kPVSlice, vc, hd, 0, np, d0, w, tid, kPVThreads);
+    cp_async_commit();
+    const float *sc = a.scores + (size_t)h * a.max_seq;
+    float m = -INFINITY;
+    for (int p = tid; p < np; p += kPVThreads) {
+      const float sv = sc[p];
+      wts[p] = sv;
+      m = fmaxf(m, sv);
+    }
+    m = block_max<kPVThreads>(m, s_red);
+    LLMQ_TSTAMP(1);
+    for (int p = tid; p < np; p += kPVThreads) wts[p] = libm_expf(__fsub_rn(wts[p], m));
+    __syncthreads();
+    LLMQ_TSTAMP(2);
+    if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum(wts, 1, np, 0.0f));  // llama.c:567
+    LLMQ_TSTAMP(3);
+    cp_async_wait<0>();
+    __syncthreads();
+    LLMQ_TSTAMP(4);
+    if (tid < w) a.out[(size_t)h * hd + d0 + tid] = seq_dot_scaled(wts, s_inv, vs + tid, kPVSlice, np, 0.0f);
+    LLMQ_TSTAMP(5);
+    return;
+  }
   // start streaming the value rows while the softmax runs
   for (int c = 0; c < kPVRing; ++c) {
     if (c < nchunks)

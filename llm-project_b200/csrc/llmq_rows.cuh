@@ -128,37 +128,6 @@ __global__ void __launch_bounds__(256) k_rows_append(const RowAttnArgs a) {
   }
 }
 
-// Sequential dot product acc + a[0]*b[0] + ... + a[n-1]*b[n-1] (each product
-// rounded, then added in index order) with 16-byte shared-memory loads; a and b
-// 16-byte aligned, n a multiple of 4.
-__device__ __forceinline__ float seq_dot_v4(const float *a, const float *b, int n, float acc) {
-  const float4 *a4 = reinterpret_cast<const float4 *>(a), *b4 = reinterpret_cast<const float4 *>(b);
-  const int n4 = n >> 2;
-  int i = 0;
-  for (; i + 2 <= n4; i += 2) {
-    const float4 x0 = a4[i], y0 = b4[i], x1 = a4[i + 1], y1 = b4[i + 1];
-    const float p0 = __fmul_rn(x0.x, y0.x), p1 = __fmul_rn(x0.y, y0.y), p2 = __fmul_rn(x0.z, y0.z),
-                p3 = __fmul_rn(x0.w, y0.w), p4 = __fmul_rn(x1.x, y1.x), p5 = __fmul_rn(x1.y, y1.y),
-                p6 = __fmul_rn(x1.z, y1.z), p7 = __fmul_rn(x1.w, y1.w);
-    acc = __fadd_rn(acc, p0);
-    acc = __fadd_rn(acc, p1);
-    acc = __fadd_rn(acc, p2);
-    acc = __fadd_rn(acc, p3);
-    acc = __fadd_rn(acc, p4);
-    acc = __fadd_rn(acc, p5);
-    acc = __fadd_rn(acc, p6);
-    acc = __fadd_rn(acc, p7);
-  }
-  if (i < n4) {
-    const float4 x0 = a4[i], y0 = b4[i];
-    acc = __fadd_rn(acc, __fmul_rn(x0.x, y0.x));
-    acc = __fadd_rn(acc, __fmul_rn(x0.y, y0.y));
-    acc = __fadd_rn(acc, __fmul_rn(x0.z, y0.z));
-    acc = __fadd_rn(acc, __fmul_rn(x0.w, y0.w));
-  }
-  return acc;
-}
-
 // Scores of one row's query group (one KV head) over one chunk of key
 // positions [p0, min(p0 + 64, pos + 1)) of its cache (llama.c:558-565): each a
 // sequential dot product over the head dimension, times 1/sqrt(hd).  The keys

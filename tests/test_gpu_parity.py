@@ -143,6 +143,17 @@ def test_decode_8b_shapes_two_layers_vs_oracle(lib, orc):
     lib.q_llama_model_free(C.byref(m))
 
 
+def test_decode_long_cache_vs_oracle(lib, orc):
+    """max_seq 2048: the softmax-V kernel streams the value rows through its
+    ring (shorter caches stage the whole value slice at once)."""
+    m = synth(lib, dict(TINY, max_seq=2048), seed=31, with_bias=True)
+    ids = np.random.default_rng(2).integers(0, TINY["vocab"], 140).tolist()
+    ologits, _ = orc_decode(orc, m, ids)
+    glogits, _ = gpu_decode(lib, m, ids)
+    assert bits_equal(glogits, ologits)
+    lib.q_llama_model_free(C.byref(m))
+
+
 def test_generate_matches_stepwise_argmax(lib):
     m = synth(lib, TINY, seed=77)
     kv1 = lib.q_llama_kv_create(C.byref(m))
