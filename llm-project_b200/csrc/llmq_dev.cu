@@ -42,9 +42,13 @@ int roundup(int v, int m) { return (v + m - 1) / m * m; }
 
 // Tile depth: 32 KB tiles (KT 128) once a matrix spans at least 16 of them per
 // SM, else 16 KB tiles (KT 64) so the contiguous split stays balanced.
-int choose_kt(int K, int Npad) {
-  const double bytes = (double)std::max(roundup(K, 64), 64) * Npad;
-  return bytes >= 148.0 * 16 * 32768 ? 128 : 64;
+// Tile depth: 32 KB tiles (KT 128) whenever a GEMV of `rows` rows still fits
+// two of them in shared memory next to its codes and input row, else 16 KB
+// tiles (KT 64).  Deeper tiles halve the per-tile costs of the ring.
+int choose_kt(int K, int rows) {
+  if (K < 128) return 64;
+  const size_t need = (size_t)rows * roundup(K, 128) + 8 * (size_t)roundup(K, 4) + 2 * (32768 + 16) + 4096;
+  return need <= 220 * 1024 ? 128 : 64;
 }
 
 // ------------------------------------------------------------------ context
@@ -279,12 +283,12 @@ int ensure(T **p, size_t *have, size_t need, bool zero) {
 // Builds the tiled copy of a (K, N) matrix whose physical column p is column
 // colsrc[p] & 0xffffff of source colsrc[p] >> 24 (-1 = zero padding).
 int build_mat(Mat &out, int K, int Nlog, int NT, const std::vector<int> &colsrc, const signed char *const src[3],
-              const int srcN[3], const float *const srcScale[3]) {
+              const int srcN[3], const float *const srcScale[3], int rows = 1) {
   out = Mat{};
   out.K = K;
   out.N = Nlog;
   out.NT = NT;
-  out.KT = choose_kt(K, (int)colsrc.size());
+  out.KT = choose_kt(K, rows);
   out.Kpad = std::max(roundup(K, out.KT), out.KT);
   out.Npad = static_cast<int>(colsrc.size());
   out.n_slabs = out.Npad / NT;
@@ -320,7 +324,7 @@ int build_mat(Mat &out, int K, int Nlog, int NT, const std::vector<int> &colsrc,
   return 1;
 }
 
-int build_plain(Mat &out, const QTensor &W) {
+int build_plain(Mat &out, const QTensor &W, int rows = 1) {
   const int NT = 256;
   const int Npad = std::max(roundup(W.cols, NT), NT);
   std::vector<int> colsrc(Npad, -1);
@@ -328,7 +332,7 @@ int build_plain(Mat &out, const QTensor &W) {
   const signed char *src[3] = {W.q, nullptr, nullptr};
   const int srcN[3] = {W.cols, 0, 0};
   const float *sc[3] = {W.scale, nullptr, nullptr};
-  return build_mat(out, W.rows, W.cols, NT, colsrc, src, srcN, sc);
+  return build_mat(out, W.rows, W.cols, NT, colsrc, src, srcN, sc, rows);
 }
 
 // --------------------------------------------------------------- GEMV launch
@@ -348,16 +352,16 @@ int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
   xs = std::max<size_t>(xs, (size_t)(pro == PRO_ABSMAX ? 1 : 2) * (((size_t)m.K + 3) & ~size_t(3)) * 4);
   const size_t fixed = codes + align16(xs);
   const size_t budget = (size_t)c.max_smem;
-  if (fixed + 2 * (tile + 8) + 16 > budget) {
+  if (fixed + 2 * (tile + 16) + 16 > budget) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: GEMV K=%d x %d rows does not fit in shared memory", m.K, rows);
     return 0;
   }
-  int S = static_cast<int>((budget - fixed - 24) / (tile + 8));
+  int S = static_cast<int>((budget - fixed - 16) / (tile + 16));
   S = std::min(S, 12);
   const long long T = (long long)m.n_slabs * m.n_ktiles;
   p.kt = m.KT;
   p.stages = S;
-  p.smem = align16((size_t)S * tile + 8 * (size_t)(S + 1)) + codes + align16(xs);
+  p.smem = align16((size_t)S * tile + 16 * (size_t)S) + codes + align16(xs);
   p.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(T, c.num_sms)));
   return 1;
 }
@@ -1345,7 +1349,7 @@ int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
   m.K = K;
   m.N = N;
   m.NT = 256;
-  m.KT = choose_kt(K, std::max(roundup(N, kNT), kNT));
+  m.KT = choose_kt(K, M > 8 ? 1 : M);
   m.Kpad = std::max(roundup(K, m.KT), m.KT);
   m.Npad = std::max(roundup(N, m.NT), m.NT);
   m.n_slabs = m.Npad / m.NT;
@@ -1841,7 +1845,7 @@ extern "C" LLMQ_API int llmq_bench_qmatmul(const QTensor *W, int M, int iters, f
     return LLMQ_ERR_ARG;
   }
   Mat m;
-  if (!build_plain(m, *W)) return q_llama_last_error();
+  if (!build_plain(m, *W, M > 8 ? 1 : M)) return q_llama_last_error();
   const int K = W->rows, N = W->cols;
   std::vector<float> hA((size_t)M * K);
   uint64_t st64 = 0x9E3779B97F4A7C15ull;

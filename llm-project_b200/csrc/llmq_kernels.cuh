@@ -50,6 +50,9 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
@@ -222,8 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   const int tid = threadIdx.x;
   const int S = a.stages;
   uint8_t *stage0 = sm;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + (size_t)S * kTileBytes);
-  int8_t *codes = reinterpret_cast<int8_t *>(sm + (((size_t)S * kTileBytes + 8 * (S + 1) + 15) & ~size_t(15)));
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + (size_t)S * kTileBytes);  // full[S], then empty[S]
+  uint64_t *empty = bars + S;
+  int8_t *codes = reinterpret_cast<int8_t *>(sm + (((size_t)S * kTileBytes + 16 * S + 15) & ~size_t(15)));
   float *xs = reinterpret_cast<float *>(codes + (((size_t)a.rows * a.Kpad + 15) & ~size_t(15)));
   float *ebuf = xs;  // epilogue exchange buffer (prologue vector is dead by then)
 
@@ -234,7 +238,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   const int n = static_cast<int>(t_end - t_begin);
 
   if (tid == 0) {
-    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);  // one per weight stage
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&bars[s], 1);               // the stage's copy landed
+      mbar_init(&empty[s], kThreads / 32);  // every warp has read the stage
+    }
     fence_mbar_init();
     s_abort = 0;
   }
@@ -460,11 +467,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   long long slab = t_begin / a.n_ktiles;
   int kt = static_cast<int>(t_begin - slab * a.n_ktiles);
   long long cur = n > 0 ? slab : -1;
-  int done = 0, s = 0;
-  uint32_t phase = 0;
+  int done = 0, s = 0, ps = 0;
+  uint32_t phase = 0, pphase = 0;  // ring position of tile i and of tile i - 1
   const uint8_t *tile_base = stage0 + ((size_t)part * kChunksPerPart * kNT + col) * 16;
   const int8_t *code_base = codes + part * (kChunksPerPart * 16);
   for (int i = 0; i < n; ++i) {
+    if (*reinterpret_cast<volatile int *>(&s_abort)) break;  // thread 0 gave up refilling
     if (i > 0 && ++kt == a.n_ktiles) {
       kt = 0;
       ++slab;
@@ -493,18 +501,26 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         }
       }
     }
-    // Stage s is refilled (after every thread has read it) only while tiles
-    // remain to be issued: i + S < n.  Without a refill there is nothing to wait
-    // for, which is the common case for matrices that fit in the ring.
-    if (i + S < n) __syncthreads();
+    // This warp is done with stage s.  Thread 0 then refills the stage of the
+    // previous tile (read by all warps by now, or soon: it waits on that
+    // stage's empty barrier) with tile i - 1 + S; no warp waits for another
+    // at a block barrier.
+    __syncwarp();
+    if ((tid & 31) == 0) mbar_arrive(&empty[s]);
     done = i + 1;
     if (s_abort) break;
-    if (tid == 0 && issued < n) {
-      mbar_expect_tx(&bars[s], kTileBytes);
-      bulk_load(stage0 + (size_t)s * kTileBytes, a.w + (size_t)(t_begin + issued) * kTileBytes, kTileBytes,
-                &bars[s]);
+    if (tid == 0 && i > 0 && issued < n) {
+      if (!mbar_wait_bounded(&empty[ps], pphase)) {
+        s_abort = 1;
+        break;
+      }
+      mbar_expect_tx(&bars[ps], kTileBytes);
+      bulk_load(stage0 + (size_t)ps * kTileBytes, a.w + (size_t)(t_begin + issued) * kTileBytes, kTileBytes,
+                &bars[ps]);
       ++issued;
     }
+    ps = s;
+    pphase = phase;
     if (++s == S) {
       s = 0;
       phase ^= 1u;
