@@ -1206,7 +1206,7 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   aa.err = M->err;
   const int group = cfg.n_heads / cfg.n_kv;
   const size_t sc_sm = rows_scores_smem(group, hd), pv_sm = rows_pv_smem(group, hd, cfg.max_seq);
-  const int attn_threads = (group * hd + 31) / 32 * 32;
+  const int attn_threads = (group * hd / 2 + 31) / 32 * 32;  // k_rows_pv: two output dims per thread
   if (hd % 4 != 0 || group > kAttnMaxGroup || attn_threads > 1024 || pv_sm + 4096 > (size_t)g_smem_optin) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: batched attention needs head_dim %% 4 == 0, group <= %d, "
                    "group*head_dim <= 1024 and max_seq %d short enough for shared memory", kAttnMaxGroup,

@@ -200,4 +200,75 @@ __device__ __forceinline__ float seq_dot_scaled(const float *e, float sc, const 
   return acc;
 }
 
+// ---- packed pairs of independent f32 chains (Blackwell f32x2 arithmetic):
+// each lane is rounded exactly as the scalar __fmul_rn / __fadd_rn would, so
+// two chains advance with one instruction stream and unchanged results.
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+  return (static_cast<unsigned long long>(__float_as_uint(v.y)) << 32) | __float_as_uint(v.x);
+}
+__device__ __forceinline__ float2 f2_from(unsigned long long b) {
+  return make_float2(__uint_as_float(static_cast<uint32_t>(b)), __uint_as_float(static_cast<uint32_t>(b >> 32)));
+}
+__device__ __forceinline__ float2 f2_mul_rn(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(r);
+}
+__device__ __forceinline__ float2 f2_add_rn(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(r);
+}
+
+// acc + a*b per lane with the product rounded on its own.  ptxas contracts a
+// packed mul.rn whose only use is a packed add into a fused multiply-add (so
+// the product would not be rounded); the product therefore goes through an
+// add of +0.0 first: fused or not, that yields round(a*b) exactly (the sign of
+// a zero product can change, which a sum starting from +0 never sees).
+__device__ __forceinline__ float2 f2_madd_rn(float2 acc, float2 a, float2 b) {
+  return f2_add_rn(acc, f2_add_rn(f2_mul_rn(a, b), make_float2(0.0f, 0.0f)));
+}
+
+// Two sequential dot products at once: acc.x + w[0]*b[0].x + w[1]*b[sb].x + ...
+// and the same with .y, where w[i] = e[i] * sc if `scaled`, else e[i]; every
+// product and sum rounded on its own in index order (the weighted sums of
+// values of two adjacent output dimensions).  Pipelined as seq_dot.
+template <bool scaled>
+__device__ __forceinline__ float2 seq_dot2(const float *e, float sc, const float2 *b, int sb, int n, float2 acc) {
+  auto wt = [&](float v) { return scaled ? __fmul_rn(v, sc) : v; };
+  int i = 0;
+  if (n >= 8) {
+    float cw[8];
+    float2 cb[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      cw[u] = wt(e[u]);
+      cb[u] = b[(size_t)u * sb];
+    }
+    for (i = 8; i + 8 <= n; i += 8) {
+      float ne[8];
+      float2 nb[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        ne[u] = e[i + u];
+        nb[u] = b[(size_t)(i + u) * sb];
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc = f2_madd_rn(acc, make_float2(cw[u], cw[u]), cb[u]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        cw[u] = wt(ne[u]);
+        cb[u] = nb[u];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) acc = f2_madd_rn(acc, make_float2(cw[u], cw[u]), cb[u]);
+  }
+  for (; i < n; ++i) {
+    const float w = wt(e[i]);
+    acc = f2_madd_rn(acc, make_float2(w, w), b[(size_t)i * sb]);
+  }
+  return acc;
+}
+
 }  // namespace llmq

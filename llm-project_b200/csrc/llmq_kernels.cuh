@@ -695,7 +695,11 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
     cp_async_wait<0>();
     __syncthreads();
     LLMQ_TSTAMP(4);
-    if (tid < w) a.out[(size_t)h * hd + d0 + tid] = seq_dot_scaled(wts, s_inv, vs + tid, kPVSlice, np, 0.0f);
+    if (2 * tid < w) {  // dims d0 + 2 tid and d0 + 2 tid + 1, two chains in packed lanes (hd is even)
+      const float2 o2 = seq_dot2<true>(wts, s_inv, reinterpret_cast<const float2 *>(vs) + tid, kPVSlice / 2, np,
+                                       make_float2(0.0f, 0.0f));
+      *reinterpret_cast<float2 *>(a.out + (size_t)h * hd + d0 + 2 * tid) = o2;
+    }
     LLMQ_TSTAMP(5);
     return;
   }

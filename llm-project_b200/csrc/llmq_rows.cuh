@@ -169,12 +169,13 @@ __global__ void __launch_bounds__(kRowScoreThreads) k_rows_scores(const RowAttnA
 }
 
 // Softmax and values of one row for one KV head and its whole query group
-// (llama.c:566-575), in one CTA of group * hd threads (rounded up to a warp):
+// (llama.c:566-575), in one CTA of group * hd / 2 threads (rounded up to a warp):
 // the group's scores come into shared memory; per head the max, expf(s - max),
 // the sequential sum of the exponentials (one thread per head) and
 // w = e * (1/sum); then the values [0, pos] stream through a ring
-// (kPvStages stages of kPvKeys positions, one bulk copy each) and thread (g, e)
-// forms out[g][e] = sum_p w[g][p] * v[p][e] sequentially in position order.
+// (kPvStages stages of kPvKeys positions, one bulk copy each) and thread (g, e2)
+// forms out[g][e] = sum_p w[g][p] * v[p][e] for e = 2 e2, 2 e2 + 1, each
+// sequentially in position order (two chains in packed f32x2 lanes).
 // Each value row is read once for the whole group.  Grid (n_kv, rows); dynamic
 // shared memory rows_pv_smem().
 constexpr int kPvKeys = 64;
@@ -251,10 +252,12 @@ __global__ void __launch_bounds__(1024) k_rows_pv(const RowAttnArgs a) {
     wts[(size_t)g * smax4 + p] = __fmul_rn(wts[(size_t)g * smax4 + p], s_inv[g]);
   }
   __syncthreads();
-  // ---- weighted sum of the values (llama.c:573-575)
-  const int g = tid / hd, e = tid - g * hd;
+  // ---- weighted sum of the values (llama.c:573-575): thread (g, e2) carries
+  // dims 2 e2 and 2 e2 + 1 as two chains in packed lanes
+  const int hd2 = hd / 2;
+  const int g = tid / hd2, e = 2 * (tid - g * hd2);
   const float *wg = wts + (size_t)min(g, group - 1) * smax4;
-  float o = 0.0f;
+  float2 o = make_float2(0.0f, 0.0f);
   int c = 0;
   for (; c < nch; ++c) {
     const int st = c % kPvStages;
@@ -262,28 +265,8 @@ __global__ void __launch_bounds__(1024) k_rows_pv(const RowAttnArgs a) {
     if (!got) s_abort = 1;
     const float *buf = ring + (size_t)st * kPvKeys * hd + e;
     const int c0 = c * kPvKeys, cnt = min(kPvKeys, np - c0);
-    if (g < group && got) {
-      const float4 *w4 = reinterpret_cast<const float4 *>(wg + c0);
-      int p = 0;
-      for (; p + 8 <= cnt; p += 8) {
-        const float4 wa = w4[p >> 2], wb = w4[(p >> 2) + 1];
-        const float v0 = buf[(size_t)(p + 0) * hd], v1 = buf[(size_t)(p + 1) * hd], v2 = buf[(size_t)(p + 2) * hd],
-                    v3 = buf[(size_t)(p + 3) * hd], v4 = buf[(size_t)(p + 4) * hd], v5 = buf[(size_t)(p + 5) * hd],
-                    v6 = buf[(size_t)(p + 6) * hd], v7 = buf[(size_t)(p + 7) * hd];
-        const float q0 = __fmul_rn(wa.x, v0), q1 = __fmul_rn(wa.y, v1), q2 = __fmul_rn(wa.z, v2),
-                    q3 = __fmul_rn(wa.w, v3), q4 = __fmul_rn(wb.x, v4), q5 = __fmul_rn(wb.y, v5),
-                    q6 = __fmul_rn(wb.z, v6), q7 = __fmul_rn(wb.w, v7);
-        o = __fadd_rn(o, q0);
-        o = __fadd_rn(o, q1);
-        o = __fadd_rn(o, q2);
-        o = __fadd_rn(o, q3);
-        o = __fadd_rn(o, q4);
-        o = __fadd_rn(o, q5);
-        o = __fadd_rn(o, q6);
-        o = __fadd_rn(o, q7);
-      }
-      for (; p < cnt; ++p) o = __fadd_rn(o, __fmul_rn(wg[c0 + p], buf[(size_t)p * hd]));  // llama.c:574
-    }
+    if (g < group && got)
+      o = seq_dot2<false>(wg + c0, 0.0f, reinterpret_cast<const float2 *>(buf), hd2, cnt, o);  // llama.c:574
     __syncthreads();
     if (s_abort) break;  // chunk c stays counted as outstanding
     if (tid == 0 && issued < nch) issue(issued++);
@@ -295,7 +278,7 @@ __global__ void __launch_bounds__(1024) k_rows_pv(const RowAttnArgs a) {
     }
     return;
   }
-  if (g < group) a.out[(size_t)r * qd + (size_t)(kvh * group + g) * hd + e] = o;
+  if (g < group) *reinterpret_cast<float2 *>(a.out + (size_t)r * qd + (size_t)(kvh * group + g) * hd + e) = o;
 }
 
 // Greedy ids of the rows (first maximum: sampler.c:8-21) from the lm-head
