@@ -246,6 +246,7 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<64>, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<128>, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_act_codes, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_rows_absmax, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_tc_epilogue, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_norm_codes, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_append, 0);
@@ -410,7 +411,7 @@ int launch_act_codes(DevCtx &c, const Mat &m, const float *dA, int rows, cudaStr
   if (!ensure(&c.tc_codes, &c.tc_codes_n, (size_t)m.Kpad * kTcRows * n_rb, false) ||
       !ensure(&c.tc_as, &c.tc_as_n, (size_t)n_rb * kTcRows, false))
     return 0;
-  k_act_codes<<<rows, 256, 0, st>>>(dA, rows, m.K, m.Kpad, m.KT, c.tc_codes, c.tc_as);
+  k_act_codes<<<rows, 256, 0, st>>>(dA, rows, m.K, m.Kpad, m.KT, c.tc_codes, c.tc_as, nullptr);
   CK(cudaGetLastError());
   return 1;
 }
@@ -418,7 +419,7 @@ int launch_act_codes(DevCtx &c, const Mat &m, const float *dA, int rows, cudaStr
 // Fills a TcArgs for `rows` activation rows (codes and scales as written by
 // launch_act_codes) times the tiled matrix m; the split count keeps the grid
 // within two CTAs per SM.
-int plan_tc(DevCtx &c, const Mat &m, int rows, TcArgs &a) {
+int plan_tc(DevCtx &c, const Mat &m, int rows, TcArgs &a, bool acc_only = false) {
   const size_t SB = (size_t)(kNT + kTcRows) * m.KT;
   const int n_rb = (rows + kTcRows - 1) / kTcRows;
   const int tiles = m.n_slabs * n_rb;
@@ -437,8 +438,25 @@ int plan_tc(DevCtx &c, const Mat &m, int rows, TcArgs &a) {
   a.stages = (int)std::max<size_t>((kTcStageBytes + SB - 1) / SB, std::min<size_t>(kTcMaxStages, kTcRingBytes / SB));
   a.rows = rows;
   a.err = c.err;
-  if (splits > 1 && !ensure(&c.tc_acc, &c.tc_acc_n, (size_t)rows * m.Npad, true)) return 0;
+  a.acc_only = acc_only ? 1 : 0;
+  if ((splits > 1 || acc_only) && !ensure(&c.tc_acc, &c.tc_acc_n, (size_t)rows * m.Npad, true)) return 0;
   a.acc = c.tc_acc;
+  return 1;
+}
+
+// The epilogue of a product whose int32 sums are in a.acc (k_tc_epilogue).
+int launch_tc_epilogue(const TcArgs &a, cudaStream_t st) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((a.rows * a.n_slabs + 3) / 4);
+  cfg.blockDim = dim3(128);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  ++g_launches;
+  CK(cudaLaunchKernelEx(&cfg, k_tc_epilogue, a));
   return 1;
 }
 
@@ -457,14 +475,7 @@ int launch_tc_gemm(const TcArgs &a, int KT, cudaStream_t st, bool pdl) {
   cfg.numAttrs = pdl ? 1 : 0;
   CK(KT == 128 ? cudaLaunchKernelEx(&cfg, k_tc_gemm<128>, a) : cudaLaunchKernelEx(&cfg, k_tc_gemm<64>, a));
   ++g_launches;
-  if (a.splits > 1) {
-    ++g_launches;
-    cfg.gridDim = dim3((a.rows * a.n_slabs + 3) / 4);
-    cfg.blockDim = dim3(128);
-    cfg.dynamicSmemBytes = 0;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    CK(cudaLaunchKernelEx(&cfg, k_tc_epilogue, a));
-  }
+  if (a.splits > 1 && !a.acc_only) return launch_tc_epilogue(a, st);
   return 1;
 }
 
@@ -603,7 +614,8 @@ struct DevModel {
   struct Rows {
     int cap = 0, lm_cap = 0;
     float *x = nullptr, *qkv = nullptr, *qr = nullptr, *ao = nullptr, *h = nullptr, *scores = nullptr;
-    float *logits = nullptr;
+    float *logits = nullptr, *logits_all = nullptr;  // logits_all: gathered shards (tensor parallel)
+    float *tp_max = nullptr;                         // [rows] reduced absmax (tensor parallel)
     RowDesc *rd = nullptr;
     int *ids = nullptr;
     unsigned long long *argmax = nullptr;
@@ -646,7 +658,7 @@ void release_model(DevModel *M) {
   for (void *p : dev_ptrs) cudaFree(p);
   {
     auto &R = M->rows;
-    void *rp[] = {R.x, R.qkv, R.qr, R.ao, R.h, R.scores, R.logits, R.rd, R.ids, R.argmax};
+    void *rp[] = {R.x, R.qkv, R.qr, R.ao, R.h, R.scores, R.logits, R.logits_all, R.tp_max, R.rd, R.ids, R.argmax};
     for (void *p : rp) cudaFree(p);
     cudaFreeHost(R.h_rd);
     cudaFreeHost(R.h_ids);
@@ -1116,10 +1128,10 @@ int ensure_rows(DevModel *M, int rows, int lm_rows) {
   auto &R = M->rows;
   const LlmqConfig &cfg = M->cfg;
   if (rows > R.cap) {
-    void *old[] = {R.x, R.qkv, R.qr, R.ao, R.h, R.scores, R.rd};
+    void *old[] = {R.x, R.qkv, R.qr, R.ao, R.h, R.scores, R.rd, R.tp_max};
     for (void *p : old) cudaFree(p);
     cudaFreeHost(R.h_rd);
-    R.x = R.qkv = R.qr = R.ao = R.h = R.scores = nullptr;
+    R.x = R.qkv = R.qr = R.ao = R.h = R.scores = R.tp_max = nullptr;
     R.rd = nullptr;
     R.h_rd = nullptr;
     R.cap = 0;
@@ -1131,11 +1143,14 @@ int ensure_rows(DevModel *M, int rows, int lm_rows) {
     CK(cudaMalloc(&R.h, n * cfg.d_ff * sizeof(float)));
     CK(cudaMalloc(&R.scores, n * cfg.n_heads * cfg.max_seq * sizeof(float)));
     CK(cudaMalloc(&R.rd, n * sizeof(RowDesc)));
+    CK(cudaMalloc(&R.tp_max, n * sizeof(float)));
     CK(cudaMallocHost(&R.h_rd, n * sizeof(RowDesc)));
     R.cap = rows;
   }
   if (lm_rows > R.lm_cap) {
     cudaFree(R.logits);
+    cudaFree(R.logits_all);
+    R.logits_all = nullptr;
     cudaFree(R.ids);
     cudaFree(R.argmax);
     cudaFreeHost(R.h_ids);
@@ -1145,6 +1160,7 @@ int ensure_rows(DevModel *M, int rows, int lm_rows) {
     R.h_ids = nullptr;
     R.lm_cap = 0;
     CK(cudaMalloc(&R.logits, (size_t)lm_rows * cfg.vocab * sizeof(float)));
+    if (M->tp_world > 1) CK(cudaMalloc(&R.logits_all, (size_t)lm_rows * M->vocab_full * sizeof(float)));
     CK(cudaMalloc(&R.ids, (size_t)lm_rows * sizeof(int)));
     if (!dev_zeros(&R.argmax, (size_t)lm_rows)) return 0;
     CK(cudaMallocHost(&R.h_ids, (size_t)lm_rows * sizeof(int)));
@@ -1161,10 +1177,7 @@ int ensure_rows(DevModel *M, int rows, int lm_rows) {
 int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, float *logits_h, int *ids_h) {
   const LlmqConfig &cfg = M->cfg;
   cudaStream_t st = M->stream;
-  if (M->tp_world > 1) {
-    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: multi-row passes of a tensor-parallel shard are not supported");
-    return 0;
-  }
+
   const int dm = cfg.d_model, qd = M->qd, kvd = M->kvd, hd = cfg.head_dim, dff = cfg.d_ff;
   const int lm_rows = rows - lm0;
   if (!ensure_rows(M, rows, lm_rows)) return 0;
@@ -1184,7 +1197,7 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   na.x_out = R.x;
   na.wte_q = M->wte_q;
   na.wte_s = M->wte_s;
-  na.vocab = cfg.vocab;
+  na.vocab = M->vocab_full;  // token ids index the whole embedding
   na.eps = cfg.eps;
   na.K = dm;
   na.codes = c.tc_codes;
@@ -1221,7 +1234,8 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
     return launch_pdl(k_rows_norm_codes, dim3(nrows), dim3(kRowThreads), norm_smem, st, na);
   };
   auto codes = [&](const float *in, int K, const Mat &m) {
-    return launch_pdl(k_act_codes, dim3(rows), dim3(256), 0, st, in, rows, K, m.Kpad, m.KT, c.tc_codes, c.tc_as);
+    return launch_pdl(k_act_codes, dim3(rows), dim3(256), 0, st, in, rows, K, m.Kpad, m.KT, c.tc_codes, c.tc_as,
+                      static_cast<const float *>(nullptr));
   };
   auto gemm = [&](const Mat &m, int nrows, int epi, const float *bias, float *out, int ld,
                   unsigned long long *am) -> int {
@@ -1233,7 +1247,27 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
     t.ld = ld;
     t.err = M->err;
     t.argmax = am;
+    t.idx_offset = M->tp_rank * cfg.vocab;  // vocab shard of the lm-head
     return launch_tc_gemm(t, m.KT, st, pdl_enabled());
+  };
+  // A row-parallel product of a tensor-parallel shard (Wo, W2: this rank's
+  // rows of K), with residual epilogue into x: the rows' absmax max-reduced
+  // over the ranks, codes with that scale, the exact int32 partial sums
+  // sum-reduced, then as * ws * acc + x (quant.c:104-117, llama.c:578 / 589).
+  auto row_parallel_rows = [&](const Mat &m, const float *in) -> int {
+    CK(launch_pdl(k_rows_absmax, dim3(rows), dim3(256), 0, st, in, m.K, R.tp_max));
+    NK(g_nccl.AllReduce(R.tp_max, R.tp_max, (size_t)rows, ncclFloat32, ncclMax, g_tp.comm, st));
+    CK(launch_pdl(k_act_codes, dim3(rows), dim3(256), 0, st, in, rows, m.K, m.Kpad, m.KT, c.tc_codes, c.tc_as,
+                  static_cast<const float *>(R.tp_max)));
+    TcArgs t;
+    if (!plan_tc(c, m, rows, t, true)) return 0;
+    t.epi = TC_RESID;
+    t.out = R.x;
+    t.ld = dm;
+    t.err = M->err;
+    if (!launch_tc_gemm(t, m.KT, st, pdl_enabled())) return 0;
+    NK(g_nccl.AllReduce(t.acc, t.acc, (size_t)rows * m.Npad, ncclInt32, ncclSum, g_tp.comm, st));
+    return launch_tc_epilogue(t, st);
   };
   for (int l = 0; l < cfg.n_layers; ++l) {
     CK(norm(l == 0 ? nullptr : R.x, M->attn_norm[l], M->qkv[l], rows));
@@ -1243,21 +1277,41 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
     CK(launch_pdl(k_rows_scores, dim3((cfg.max_seq + kRowScoreKeys - 1) / kRowScoreKeys, cfg.n_kv, rows),
                   dim3(kRowScoreThreads), sc_sm, st, aa));
     CK(launch_pdl(k_rows_pv, dim3(cfg.n_kv, rows), dim3(attn_threads), pv_sm, st, aa));
-    CK(codes(R.ao, qd, M->wo[l]));
-    if (!gemm(M->wo[l], rows, TC_RESID, nullptr, R.x, dm, nullptr)) return 0;
+    if (M->tp_world > 1) {
+      if (!row_parallel_rows(M->wo[l], R.ao)) return 0;
+    } else {
+      CK(codes(R.ao, qd, M->wo[l]));
+      if (!gemm(M->wo[l], rows, TC_RESID, nullptr, R.x, dm, nullptr)) return 0;
+    }
     CK(norm(R.x, M->ffn_norm[l], M->w13[l], rows));
     if (!gemm(M->w13[l], rows, TC_SWIGLU, nullptr, R.h, dff, nullptr)) return 0;
-    CK(codes(R.h, dff, M->w2[l]));
-    if (!gemm(M->w2[l], rows, TC_RESID, nullptr, R.x, dm, nullptr)) return 0;
+    if (M->tp_world > 1) {
+      if (!row_parallel_rows(M->w2[l], R.h)) return 0;
+    } else {
+      CK(codes(R.h, dff, M->w2[l]));
+      if (!gemm(M->w2[l], rows, TC_RESID, nullptr, R.x, dm, nullptr)) return 0;
+    }
   }
   if (lm_rows > 0) {
     CK(norm(R.x + (size_t)lm0 * dm, M->final_norm, M->lm, lm_rows));
     if (!gemm(M->lm, lm_rows, TC_LOGITS, nullptr, R.logits, cfg.vocab, R.argmax)) return 0;
+    if (M->tp_world > 1)  // the first maximum over every shard's vocab slice (sampler.c:8-21)
+      NK(g_nccl.AllReduce(R.argmax, R.argmax, (size_t)lm_rows, ncclUint64, ncclMax, g_tp.comm, st));
     CK(launch_pdl(k_rows_finish, dim3(1), dim3(256), 0, st, R.argmax, lm_rows, R.ids));
     CK(cudaMemcpyAsync(R.h_ids, R.ids, (size_t)lm_rows * sizeof(int), cudaMemcpyDeviceToHost, st));
-    if (logits_h)
+    if (logits_h && M->tp_world > 1) {
+      // gathered as [rank][rows][vocab slice]: each rank's block lands in its
+      // columns of the caller's [rows][vocab] rows
+      const size_t blk = (size_t)lm_rows * cfg.vocab;
+      NK(g_nccl.AllGather(R.logits, R.logits_all, blk, ncclFloat32, g_tp.comm, st));
+      for (int r = 0; r < M->tp_world; ++r)
+        CK(cudaMemcpy2DAsync(logits_h + (size_t)r * cfg.vocab, (size_t)M->vocab_full * sizeof(float),
+                             R.logits_all + r * blk, (size_t)cfg.vocab * sizeof(float), (size_t)cfg.vocab * sizeof(float),
+                             lm_rows, cudaMemcpyDeviceToHost, st));
+    } else if (logits_h) {
       CK(cudaMemcpyAsync(logits_h, R.logits, (size_t)lm_rows * cfg.vocab * sizeof(float), cudaMemcpyDeviceToHost,
                          st));
+    }
   }
   CK(cudaMemcpyAsync(R.h_err, M->err, sizeof(int), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
@@ -1531,7 +1585,7 @@ int llmqd_decode_rows(const QLlamaModel *m, LlamaKV *const *kvs, const int *toke
   CK(cudaEventRecord(M->ev0, M->stream));
   for (int off = 0; off < B; off += kRowsPerPass) {
     const int n = std::min(kRowsPerPass, B - off);
-    if (!run_rows(*c, M, rows.data() + off, n, 0, logits ? logits + (size_t)off * M->cfg.vocab : nullptr, ids + off))
+    if (!run_rows(*c, M, rows.data() + off, n, 0, logits ? logits + (size_t)off * M->vocab_full : nullptr, ids + off))
       return 0;
   }
   CK(cudaEventRecord(M->ev1, M->stream));

@@ -95,9 +95,10 @@ __device__ __forceinline__ int4 tc_pack16(const float *x, int k0, int K, float i
 }
 
 // Per-row activation quantisation (quant.c:104-113) of rows [0, rows) of a
-// (row stride K), written as tcgen05 A tiles.  One CTA per row.
+// (row stride K), written as tcgen05 A tiles; the row's absmax comes from
+// absmax_in when given.  One CTA per row.
 __global__ void __launch_bounds__(256) k_act_codes(const float *a, int rows, int K, int Kpad, int KT, int8_t *codes,
-                                                   float *as_out) {
+                                                   float *as_out, const float *absmax_in) {
   __shared__ float s_red[32];
   pdl_launch_dependents();
   pdl_wait();
@@ -105,13 +106,30 @@ __global__ void __launch_bounds__(256) k_act_codes(const float *a, int rows, int
   const int tid = threadIdx.x;
   const float *row = a + (size_t)m * K;
   float mx = 0.0f;
-  for (int k = tid; k < K; k += 256) mx = fmaxf(mx, fabsf(row[k]));
-  mx = block_max<256>(mx, s_red);
+  if (absmax_in) {  // a row-parallel shard: the absmax of the whole row, reduced over the ranks
+    mx = absmax_in[m];
+  } else {
+    for (int k = tid; k < K; k += 256) mx = fmaxf(mx, fabsf(row[k]));
+    mx = block_max<256>(mx, s_red);
+  }
   const float as = mx > 0.0f ? __fdiv_rn(mx, 127.0f) : 1.0f;
   const float inv = __fdiv_rn(1.0f, as);
   if (tid == 0) as_out[m] = as;
   for (int ch = tid; ch < Kpad / 16; ch += 256)
     *reinterpret_cast<int4 *>(codes + tc_code_offset(m, ch, Kpad, KT)) = tc_pack16(row, ch * 16, K, inv);
+}
+
+// Absmax of each row of a (row stride K), the local part of a row-parallel
+// product's activation scale (quant.c:104-106).  One CTA per row.
+__global__ void __launch_bounds__(256) k_rows_absmax(const float *a, int K, float *out) {
+  __shared__ float s_red[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const float *row = a + (size_t)blockIdx.x * K;
+  float mx = 0.0f;
+  for (int k = threadIdx.x; k < K; k += 256) mx = fmaxf(mx, fabsf(row[k]));
+  mx = block_max<256>(mx, s_red);
+  if (threadIdx.x == 0) out[blockIdx.x] = mx;
 }
 
 // ------------------------------------------------------------------- GEMM
@@ -136,6 +154,8 @@ struct TcArgs {
   int *acc;               // splits > 1: [rows][Npad] int32, zero before and after (k_tc_epilogue)
   int *err;
   unsigned long long *argmax;  // TC_LOGITS: [rows] keys, zero before the launch
+  int idx_offset;         // TC_LOGITS: global index of column 0 (vocab shard)
+  int acc_only;           // leave the int32 sums in `acc` (a row-parallel shard's partials)
   float *out;             // [rows][ld]
   int ld;                 // row stride of out
 };
@@ -172,7 +192,7 @@ __device__ __forceinline__ void tc_epilogue_lane(const TcArgs &a, int m, int sla
       } else {
         orow[j] = y;
         if (a.epi == TC_LOGITS) {
-          const unsigned long long key = argmax_key(y, static_cast<uint32_t>(j));
+          const unsigned long long key = argmax_key(y, static_cast<uint32_t>(j + a.idx_offset));
           best = key > best ? key : best;
         }
       }
@@ -298,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads) k_tc_gemm(const TcArgs a) {
   tc_fence_after();
   __syncthreads();  // s_abort is final; the ring is free for staging
   const bool ok = !s_abort;
-  const bool direct = a.splits == 1;
+  const bool direct = a.splits == 1 && !a.acc_only;
   int *stg = reinterpret_cast<int *>(sm);  // [64][kLd]
   const int p0 = slab * kNT;
   for (int g = 0; g < 2 && g * 64 < rows_here; ++g) {

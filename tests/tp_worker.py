@@ -68,6 +68,43 @@ def main():
         dist.barrier()
         lib.llama_kv_free(C.byref(kv))
         lib.q_llama_model_free(C.byref(sh))
+    # batched passes on the shards: three prompts of different lengths
+    # prefilled, then three batched steps with logits; every row equals the
+    # oracle's single-sequence decode of the whole model
+    cfg = TINY
+    sh = llmq.synth_shard(lib, cfg, 1234, rank, world, with_bias=True)
+    rng = np.random.default_rng(9)
+    lens, steps = [5, 1, 12], 3
+    seqs = [rng.integers(0, cfg["vocab"], n + steps).tolist() for n in lens]
+    kvs = [lib.q_llama_kv_create(C.byref(sh)) for _ in lens]
+    llmq.check(lib)
+    firsts = []
+    for kv, sq, n in zip(kvs, seqs, lens):
+        firsts.append(lib.q_llama_prefill_argmax(C.byref(sh), C.byref(kv), llmq.int_array(sq[:n]), n, None))
+        llmq.check(lib)
+    got = np.zeros((len(lens), steps, cfg["vocab"]), np.float32)
+    for i in range(steps):
+        out = np.zeros((len(lens), cfg["vocab"]), np.float32)
+        t = llmq.host_tensor(out)
+        lib.q_llama_decode_batch(C.byref(sh), llmq.kv_pointers(kvs), llmq.int_array([sq[n + i] for sq, n in zip(seqs, lens)]),
+                                 len(lens), C.byref(t))
+        llmq.check(lib)
+        got[:, i] = out
+    if rank == 0:
+        orc = oracle.load_oracle()
+        full = synth(lib, cfg, seed=1234, with_bias=True)
+        ok_rows, ok_first = True, True
+        for b, (sq, n) in enumerate(zip(seqs, lens)):
+            want, _ = orc_decode(orc, full, sq)
+            ok_rows &= bits_equal(got[b], want[n:])
+            ok_first &= firsts[b] == int(np.argmax(want[n - 1]))
+        verdicts["tiny_bias.batch_logits"] = bool(ok_rows)
+        verdicts["tiny_bias.prefill_ids"] = bool(ok_first)
+        lib.q_llama_model_free(C.byref(full))
+    dist.barrier()
+    for kv in kvs:
+        lib.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(sh))
     dist.barrier()
     lib.q_llama_tp_shutdown()
     if rank == 0:
