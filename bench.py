@@ -1,7 +1,7 @@
 """Benchmark: int8 (W8A8) LLaMA-family KV-cache decode on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload 8b|8b2|tiny|serve64|70b|sweep]
+                    [--workload 8b|8b2|tiny|serve64|serve64-tp|70b|70b-bs32|sweep]
 
 Default workload: LLaMA-3-8B-shaped int8 model
 (dm 4096, 32 layers, 32/8 heads, hd 128, dff 14336, vocab 128256, rope 5e5),
@@ -51,9 +51,18 @@ WORKLOADS = {
                     name="llama3-8b-shaped int8 W8A8 batched serving: 64 sequences, 2048-id prompts prefilled, "
                          "then batched greedy decode"),
     "70b": dict(cfg=dict(vocab=128256, d_model=8192, n_layers=80, n_heads=64, n_kv=8, head_dim=128, d_ff=28672,
-                         rope_base=500000.0, eps=1e-5), prompt=1024, gen=256, tp=True,
+                         rope_base=500000.0, eps=1e-5), prompt=1024, gen=256, tp=True, fast=True,
                 name="llama3-70b-shaped int8 W8A8, batch 1, tensor-parallel over all GPUs: 1024-id prompt then "
                      "greedy decode"),
+    "serve64-tp": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=32, n_heads=32, n_kv=8, head_dim=128,
+                                d_ff=14336, rope_base=500000.0, eps=1e-5), prompt=2048, gen=128, batch=64, tp=True,
+                       name="llama3-8b-shaped int8 W8A8 batched serving, tensor-parallel over all GPUs: 64 sequences, "
+                            "2048-id prompts prefilled, then batched greedy decode"),
+    "70b-bs32": dict(cfg=dict(vocab=128256, d_model=8192, n_layers=80, n_heads=64, n_kv=8, head_dim=128,
+                              d_ff=28672, rope_base=500000.0, eps=1e-5), prompt=1024, gen=256, batch=32, tp=True,
+                     fast=True,
+                     name="llama3-70b-shaped int8 W8A8, batch 32, tensor-parallel over all GPUs: 1024-id prompts "
+                          "prefilled, then batched greedy decode"),
     "tiny": dict(cfg=dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768,
                           rope_base=10000.0, eps=1e-5), prompt=16, gen=240,
                  name="tiny llama int8 W8A8, batch 1: 16-id prompt then greedy decode"),
@@ -303,9 +312,23 @@ def run_serve(args, rank, world):
     cfg = wl["cfg"]
     B, P, W, K = wl["batch"], args.prompt or wl["prompt"], args.warmup, args.steps
     max_seq = P + W + K
+    tp = bool(wl.get("tp")) and world > 1
     if world > 1:
         os.environ.setdefault("LLMQ_THREADS", str(max(1, (os.cpu_count() or 1) // world)))
-    m = make_model(lib, cfg, max_seq)
+    if tp:  # one tensor-parallel group over all ranks; each rank builds its shard
+        llmq.tp_bootstrap(lib, rank, world)
+    if tp or wl.get("fast"):
+        c = llmq.config(max_seq=max_seq, **cfg)
+        m = llmq.QLlamaModel()
+        r_, w_ = (rank, world) if tp else (0, 1)
+        if wl.get("fast"):
+            rc = lib.llmq_synth_model_fast_shard(C.byref(c), SEED_WEIGHTS, r_, w_, C.byref(m))
+        else:
+            rc = lib.llmq_synth_model_shard(C.byref(c), SEED_WEIGHTS, 0.02, 0, r_, w_, C.byref(m))
+        if rc != 0:
+            llmq.check(lib)
+    else:
+        m = make_model(lib, cfg, max_seq)
     if lib.q_llama_model_upload(C.byref(m)) != 0:
         raise RuntimeError(lib.q_llama_last_error_message().decode())
     kvs = []
@@ -351,11 +374,12 @@ def run_serve(args, rank, world):
         wall = time.perf_counter() - t0
     if dist is not None:
         import torch
-        t = torch.tensor([dev_ms, wall], dtype=torch.float64)
+        t = torch.tensor([dev_ms, wall, pre_ms], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_ms, wall = float(t[0]), float(t[1])
-    value = world * B * K / (dev_ms / 1e3)
-    e2e = world * B * K / wall
+        dev_ms, wall, pre_ms = float(t[0]), float(t[1]), float(t[2])
+    groups = 1 if tp else world  # replicas each serve their own B sequences
+    value = groups * B * K / (dev_ms / 1e3)
+    e2e = groups * B * K / wall
     peaks = {}
     try:
         peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
@@ -368,20 +392,23 @@ def run_serve(args, rank, world):
     mean_pos = P + W + (K - 1) / 2.0
     kv_bytes = B * cfg["n_layers"] * 2 * (mean_pos + 1) * kvd * 4
     step_bytes = weight_bytes(cfg) + kv_bytes
+    if tp:  # per GPU: its shard of the weights and of the KV heads
+        step_bytes /= world
+        kv_bytes /= world
     achieved = step_bytes / (dev_ms / K / 1e3) / 1e9
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not wl.get("fast"):
         cpu = serve_cpu_baseline(lib, m, kvs[0])
     line = {
-        "metric": "int8-weight decode tok/s (bs64)", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
+        "metric": f"int8-weight decode tok/s (bs{B})", "value": round(value, 1), "unit": "tok/s", "n_gpus": world,
         "steps": K, "warmup": W, "ms_per_step": round(dev_ms / K, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": wl["name"], "model": f"8b-shaped synthetic, seed {SEED_WEIGHTS}",
-                   "global_batch": B * world, "batch_per_gpu": B, "prompt": P,
-                   "kv_len_start": P + W, "kv_len_end": P + W + K, "parallelism": "single GPU per replica",
-                   "l2": f"inputs larger than L2: {weight_bytes(cfg) / 1e9:.2f} GB weights + "
-                         f"{kv_bytes / 1e9:.1f} GB KV per step"},
-        "prefill": {"tok_per_s": round(world * B * P / (pre_ms / 1e3), 1), "gpu_ms": round(pre_ms, 1),
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic (seeded uniform int8 codes, per-column scales)" if wl.get("fast") else "synthetic",
+        "config": {"workload": wl["name"], "model": f"{args.workload}-shaped synthetic, seed {SEED_WEIGHTS}",
+                   "global_batch": B * groups, "prompt": P, "kv_len_start": P + W, "kv_len_end": P + W + K,
+                   "parallelism": f"tp{world}" if tp else "single GPU per replica",
+                   "l2": f"inputs larger than L2: {step_bytes / 1e9:.1f} GB of weights and KV per GPU per step"},
+        "prefill": {"tok_per_s": round(groups * B * P / (pre_ms / 1e3), 1), "gpu_ms": round(pre_ms, 1),
                     "wall_s": round(pre_wall, 2), "api": "q_llama_prefill_argmax, one sequence per call"},
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": B * (4 + 32),
                 "d2h_bytes_per_step": B * 4 + 4,
@@ -397,6 +424,9 @@ def run_serve(args, rank, world):
     for kv in kvs:
         lib.llama_kv_free(C.byref(kv))
     lib.q_llama_model_free(C.byref(m))
+    if tp:
+        dist.barrier()
+        lib.q_llama_tp_shutdown()
     if rank == 0:
         print(json.dumps(line), flush=True)
 
@@ -705,7 +735,8 @@ def main():
     ap.add_argument("--prompt", type=int, default=0, help="override the prompt length (profiling runs)")
     args = ap.parse_args()
     if args.steps is None:
-        args.steps = 128 - args.warmup if args.workload == "serve64" else 240
+        wl = WORKLOADS.get(args.workload, {})
+        args.steps = wl["gen"] - args.warmup if "batch" in wl else 240
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -721,7 +752,7 @@ def main():
                 run_sweep(args)
         elif args.impl == "reference":
             run_reference(args, rank, world)
-        elif args.workload == "serve64":
+        elif "batch" in WORKLOADS[args.workload]:
             run_serve(args, rank, world)
         elif WORKLOADS[args.workload].get("tp"):
             run_tp(args, rank, world)
