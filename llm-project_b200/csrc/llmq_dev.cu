@@ -236,9 +236,8 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_EMBED_RMSNORM, EPI_QKV, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_QKV, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_RESID, 1>(sm);
-  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_ACC, 1>(sm);
-  ea = ea != cudaSuccess ? ea : set_attr(k_row_absmax, 0);
-  ea = ea != cudaSuccess ? ea : set_attr(k_tp_resid, 0);
+  ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_ABSMAX, EPI_TP_RESID, 1>(sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_tp_absmax, 0);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_SWIGLU, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_LOGITS, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_attn_scores, sm);
@@ -531,7 +530,7 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl, int p
 }
 
 cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
-                          int max_seq, cudaStream_t st) {
+                          int max_seq, cudaStream_t st, unsigned *tp_seq = nullptr, unsigned tp_products = 0) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(1);
@@ -541,7 +540,7 @@ cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_step_finish, step, argmax, err, result, tokens, max_seq);
+  return cudaLaunchKernelEx(&cfg, k_step_finish, step, argmax, err, result, tokens, max_seq, tp_seq, tp_products);
 }
 
 // Launches `kern` with programmatic dependent launch (the kernel itself waits
@@ -607,6 +606,11 @@ struct DevModel {
   float *tp_max = nullptr;      // reduced activation absmax of a row-parallel product
   int *tp_acc = nullptr;        // [d_model] partial / reduced int32 sums
   float *logits_full = nullptr; // [vocab_full] gathered logits
+  // peer-memory exchange of the single-sequence step (see TpExchange)
+  char *tpx = nullptr;               // this rank's region
+  std::vector<char *> tpx_peer;      // every rank's region, mapped here (own included)
+  char **tpx_peers_dev = nullptr;    // the same, in device memory
+  unsigned *tp_seq = nullptr;        // row-parallel products completed
   std::vector<DevKV *> kvs;
   // per-kernel events while llmq_step_profile records a step outside a graph
   std::vector<cudaEvent_t> *prof = nullptr;
@@ -651,7 +655,9 @@ void release_model(DevModel *M) {
   free_mat(M->lm);
   for (auto *v : {&M->attn_norm, &M->ffn_norm, &M->bias_qkv})
     for (float *p : *v) cudaFree(p);
-  void *tp_ptrs[] = {M->tp_max, M->tp_acc, M->logits_full};
+  for (int q = 0; q < (int)M->tpx_peer.size(); ++q)
+    if (q != M->tp_rank && M->tpx_peer[q]) cudaIpcCloseMemHandle(M->tpx_peer[q]);
+  void *tp_ptrs[] = {M->tp_max, M->tp_acc, M->logits_full, M->tpx, M->tpx_peers_dev, M->tp_seq};
   for (void *p : tp_ptrs) cudaFree(p);
   void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o, M->scores,
                       M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step};
@@ -685,6 +691,43 @@ template <typename T>
 int dev_zeros(T **dst, size_t n) {
   CK(cudaMalloc(dst, std::max<size_t>(n, 1) * sizeof(T)));
   CK(cudaMemset(*dst, 0, std::max<size_t>(n, 1) * sizeof(T)));
+  return 1;
+}
+
+// The peer-memory exchange region of a shard (TpExchange): allocated here,
+// shared with the other ranks through CUDA IPC handles that the ranks
+// all-gather over NCCL (every rank uploads its shard in the same order).
+int tp_map_peers(DevModel *M) {
+  const int W = M->tp_world, dm = M->cfg.d_model;
+  if (!dev_zeros(&M->tpx, tpx_bytes(W, dm)) || !dev_zeros(&M->tp_seq, 1)) return 0;
+  cudaIpcMemHandle_t mine;
+  CK(cudaIpcGetMemHandle(&mine, M->tpx));
+  std::vector<cudaIpcMemHandle_t> all(W);
+  unsigned char *dh = nullptr;
+  CK(cudaMalloc(&dh, sizeof(cudaIpcMemHandle_t) * (size_t)(W + 1)));
+  CK(cudaMemcpy(dh, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+  const ncclResult_t r = g_nccl.AllGather(dh, dh + sizeof(mine), sizeof(mine), ncclUint8, g_tp.comm, M->stream);
+  const cudaError_t es = cudaStreamSynchronize(M->stream);
+  const cudaError_t ec = cudaMemcpy(all.data(), dh + sizeof(mine), sizeof(mine) * (size_t)W, cudaMemcpyDeviceToHost);
+  cudaFree(dh);
+  if (r != ncclSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: NCCL all-gather of exchange handles: %s", g_nccl.GetErrorString(r));
+    return 0;
+  }
+  CK(es);
+  CK(ec);
+  M->tpx_peer.assign(W, nullptr);
+  for (int q = 0; q < W; ++q) {
+    if (q == M->tp_rank) {
+      M->tpx_peer[q] = M->tpx;
+      continue;
+    }
+    void *p = nullptr;
+    CK(cudaIpcOpenMemHandle(&p, all[q], cudaIpcMemLazyEnablePeerAccess));
+    M->tpx_peer[q] = static_cast<char *>(p);
+  }
+  CK(cudaMalloc(&M->tpx_peers_dev, sizeof(char *) * (size_t)W));
+  CK(cudaMemcpy(M->tpx_peers_dev, M->tpx_peer.data(), sizeof(char *) * (size_t)W, cudaMemcpyHostToDevice));
   return 1;
 }
 
@@ -840,6 +883,7 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   if (M->tp_world > 1 && (!dev_zeros(&M->tp_max, 1) || !dev_zeros(&M->tp_acc, dm) ||
                           !dev_zeros(&M->logits_full, M->vocab_full)))
     return 0;
+  if (M->tp_world > 1 && !tp_map_peers(M)) return 0;
   CK(cudaDeviceSynchronize());
   return 1;
 }
@@ -937,22 +981,27 @@ DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
 }
 
 // A row-parallel product of one decode step (Wo or W2 shard, this rank's rows
-// of K): the activation scale needs the absmax of the whole row, so the ranks
-// max-reduce their local absmax first (quant.c:104-106); each rank then forms
-// its exact int32 partial sums, the ranks add them (integer adds: the result
-// equals the single-GPU sums bit for bit), and the residual update applies the
-// scales (quant.c:117, llama.c:578 / 589).
-int row_parallel(DevModel *M, const Mat &w, const GemvPlan &p, const float *in, cudaStream_t st) {
-  CK(launch_pdl(k_row_absmax, dim3(1), dim3(kThreads), 0, st, in, w.K, M->tp_max));
-  NK(g_nccl.AllReduce(M->tp_max, M->tp_max, 1, ncclFloat32, ncclMax, g_tp.comm, st));
+// of K), as two kernels over NVLink peer memory: k_tp_absmax forms the group's
+// absmax of the input (the reference quantises with the whole row's absmax,
+// quant.c:104-106); the GEMV then forms this rank's exact int32 partial sums
+// and, per slab, exchanges them with the other ranks and applies
+// as * ws * sum + residual itself (quant.c:117, llama.c:578 / 589).  Integer
+// sums: bit-identical to one GPU.  pidx numbers the step's products.
+int row_parallel(DevModel *M, const Mat &w, const GemvPlan &p, const float *in, int pidx, cudaStream_t st) {
+  TpExchange t{};
+  t.peers = M->tpx_peers_dev;
+  t.seq = M->tp_seq;
+  t.rank = M->tp_rank;
+  t.world = M->tp_world;
+  t.dm = M->cfg.d_model;
+  t.pidx = pidx;
+  CK(launch_pdl(k_tp_absmax, dim3(1), dim3(kThreads), 0, st, in, w.K, M->tp_max, t, M->err));
   GemvArgs a = base_args(w, p, M->acc, M->cnt, M->err);
   a.in = in;
   a.absmax_in = M->tp_max;
-  a.out = reinterpret_cast<float *>(M->tp_acc);
-  CK((launch_gemv<PRO_ABSMAX, EPI_ACC, 1>(a, p, st, true)));
-  NK(g_nccl.AllReduce(M->tp_acc, M->tp_acc, (size_t)w.N, ncclInt32, ncclSum, g_tp.comm, st));
-  CK(launch_pdl(k_tp_resid, dim3((w.N + 255) / 256), dim3(256), 0, st, M->x, static_cast<const int *>(M->tp_acc),
-                static_cast<const float *>(M->tp_max), w.ws, w.N));
+  a.out = M->x;
+  a.tp = t;
+  CK((launch_gemv<PRO_ABSMAX, EPI_TP_RESID, 1>(a, p, st, true)));
   return 1;
 }
 
@@ -1023,7 +1072,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       PROF_MARK();
     }
     if (M->tp_world > 1) {
-      if (!row_parallel(M, M->wo[l], M->p_wo, M->o, st)) return 0;
+      if (!row_parallel(M, M->wo[l], M->p_wo, M->o, 2 * l, st)) return 0;
     } else {
       GemvArgs a = base_args(M->wo[l], M->p_wo, M->acc, M->cnt, M->err);
       a.in = M->o;
@@ -1041,7 +1090,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       PROF_MARK();
     }
     if (M->tp_world > 1) {
-      if (!row_parallel(M, M->w2[l], M->p_w2, M->h, st)) return 0;
+      if (!row_parallel(M, M->w2[l], M->p_w2, M->h, 2 * l + 1, st)) return 0;
     } else {
       GemvArgs a = base_args(M->w2[l], M->p_w2, M->acc, M->cnt, M->err);
       a.in = M->h;
@@ -1065,7 +1114,8 @@ int record_step(DevModel *M, DevKV *K, int mode) {
     NK(g_nccl.AllReduce(M->argmax, M->argmax, 1, ncclUint64, ncclMax, g_tp.comm, st));
     if (mode == 2) NK(g_nccl.AllGather(M->logits, M->logits_full, (size_t)cfg.vocab, ncclFloat32, g_tp.comm, st));
   }
-  CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st));
+  CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st,
+                   M->tp_world > 1 ? M->tp_seq : nullptr, 2u * (unsigned)cfg.n_layers));
       PROF_MARK();
   if (mode > 0) CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
   if (mode == 2)
@@ -1755,7 +1805,7 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
 LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   const DevModel *M = find_model(m);
-  return (M && M->tp_world > 1 ? 10 : 6) * m->n_layers + 2;  // + absmax and residual kernels per row-parallel product
+  return (M && M->tp_world > 1 ? 8 : 6) * m->n_layers + 2;  // + the absmax exchange per row-parallel product
 }
 
 // ------------------------------------------------- tensor-parallel group API

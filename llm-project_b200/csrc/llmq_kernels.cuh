@@ -145,8 +145,56 @@ enum Epilogue : int {
   EPI_RESID = 2,   // out[j] += as*ws*acc                           (Wo, W2)
   EPI_SWIGLU = 3,  // out[j] = SiLU(gate) * up                      (W1|W3)
   EPI_LOGITS = 4,  // logits + device argmax                        (lm-head)
-  EPI_ACC = 5      // ((int *)out)[j] = acc: this rank's partial sum (row-parallel shard)
+  EPI_TP_RESID = 5 // row-parallel shard: exchange the slab's partial sums with the peers over
+                   // NVLink peer memory, add them, then out[j] += as*ws*sum (tp_exchange.h)
 };
+
+// ------------------------------------------- tensor-parallel peer exchange
+// Every rank of a tensor-parallel group holds one exchange region, mapped into
+// the other ranks' address spaces (CUDA IPC).  Layout, for world W, d_model dm
+// and ns slabs of 256 columns:
+//   int      data[2][W][dm]   partial sums of a row-parallel product, by the
+//                             product's parity and the source rank
+//   float    amax[2][W]       the source rank's absmax of the product's input
+//   unsigned flag_slab[ns][W] epoch of the last slab partials received from W
+//   unsigned flag_amax[W]     epoch of the last absmax received
+// (ns = ceil(dm / 256)).  A rank stores into every region (its own
+// included), fences system-wide, then raises its flag in every region;
+// readers wait for the flags of all ranks to reach the product's epoch.
+// Epochs increase by one per product and never repeat; a rank is at most one
+// product ahead of another (its next push needs the others' pushes of the
+// current product), so two data buffers suffice.
+struct TpExchange {
+  char *const *peers;      // [W] region base of every rank, this rank's own included
+  const unsigned *seq;     // products completed before this step
+  int rank, world, dm, pidx;  // pidx: the product's index within the step (epoch = *seq + pidx + 1)
+};
+__host__ __device__ inline size_t tpx_data_off() { return 0; }
+__host__ __device__ inline size_t tpx_amax_off(int W, int dm) { return (size_t)2 * W * dm * 4; }
+__host__ __device__ inline size_t tpx_fslab_off(int W, int dm) {
+  return (tpx_amax_off(W, dm) + (size_t)2 * W * 4 + 15) & ~size_t(15);
+}
+__host__ __device__ inline size_t tpx_famax_off(int W, int dm) {
+  return tpx_fslab_off(W, dm) + (size_t)((dm + 255) / 256) * W * 4;
+}
+__host__ __device__ inline size_t tpx_bytes(int W, int dm) { return tpx_famax_off(W, dm) + (size_t)W * 4; }
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Bounded wait until *p >= epoch; false after ~2^24 polls (about a second).
+__device__ __forceinline__ bool wait_flag(const unsigned *p, unsigned epoch) {
+  for (uint32_t it = 0; it < (1u << 24); ++it) {
+    if (ld_acquire_u32(p) >= epoch) return true;
+    __nanosleep(32);
+  }
+  return false;
+}
 
 // Tile geometry: a tile is KT rows of k by kNT columns, stored as
 // [KT/16][kNT][16 bytes] so that one column's 16 consecutive k values form one
@@ -186,6 +234,7 @@ struct GemvArgs {
   unsigned long long *argmax;
   int idx_offset;      // EPI_LOGITS: global index of column 0 (vocab shard)
   const float *absmax_in;  // PRO_ABSMAX: if set, the row's absmax over all shards (else computed here)
+  TpExchange tp;           // EPI_TP_RESID
 };
 
 // Owner CTA of tile t under the contiguous split [c*T/G, (c+1)*T/G).
@@ -386,13 +435,42 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     __threadfence();
     // ---- fused epilogue for columns [slab*kNT, slab*kNT + kNT)
     const int p0 = static_cast<int>(slab) * kNT;
-    if (EPI == EPI_ACC) {
-      for (int r = 0; r < a.rows && r < MR; ++r)
+    if (EPI == EPI_TP_RESID) {
+      // This slab's partial sums go to every rank; once every rank's have
+      // arrived, their (exact, integer) sum feeds the residual update.
+      const TpExchange &x = a.tp;
+      const unsigned epoch = *x.seq + x.pidx + 1;
+      const int par = epoch & 1u;
+      const size_t fs = tpx_fslab_off(x.world, x.dm);
+      for (int c = tid; c < kNT; c += kThreads) {
+        const int j = p0 + c;
+        const int v = atomicExch(a.acc + j, 0);
+        if (j < a.N)
+          for (int q = 0; q < x.world; ++q)
+            reinterpret_cast<int *>(x.peers[q] + tpx_data_off())[((size_t)par * x.world + x.rank) * x.dm + j] = v;
+      }
+      __threadfence_system();
+      __syncthreads();
+      if (tid < x.world) {
+        st_release_u32(reinterpret_cast<unsigned *>(x.peers[tid] + fs) + (size_t)slab * x.world + x.rank, epoch);
+        const unsigned *own = reinterpret_cast<const unsigned *>(x.peers[x.rank] + fs) + (size_t)slab * x.world + tid;
+        if (!wait_flag(own, epoch)) {
+          atomicOr(a.err, ERR_TIMEOUT);
+          s_abort = 1;
+        }
+      }
+      __syncthreads();
+      if (!s_abort) {
+        const int *data = reinterpret_cast<const int *>(x.peers[x.rank] + tpx_data_off());
+        const float as = s_as[0];
         for (int c = tid; c < kNT; c += kThreads) {
           const int j = p0 + c;
-          const int v = atomicExch(a.acc + (size_t)r * a.Npad + j, 0);
-          if (j < a.N) reinterpret_cast<int *>(a.out)[(size_t)r * a.N + j] = v;
+          if (j >= a.N) continue;
+          int sum = 0;
+          for (int q = 0; q < x.world; ++q) sum += __ldcv(data + ((size_t)par * x.world + q) * x.dm + j);
+          a.out[j] = __fadd_rn(a.out[j], dequant(as, a.ws[j], sum));  // llama.c:578 / 589
         }
+      }
     } else if (EPI == EPI_PLAIN || EPI == EPI_RESID) {
       for (int r = 0; r < a.rows && r < MR; ++r) {
         const float as = s_as[r];
@@ -753,8 +831,9 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
 // device-side token and position (used when steps are chained on the device),
 // record the generated id, and reset the argmax cell and error word.
 __global__ void k_step_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
-                              int max_seq) {
+                              int max_seq, unsigned *tp_seq, unsigned tp_products) {
   pdl_wait();
+  if (tp_seq) *tp_seq += tp_products;  // the step's row-parallel products are done on this rank
   const unsigned long long key = *argmax;
   const int idx = static_cast<int>(0xffffffffu - static_cast<uint32_t>(key & 0xffffffffull));
   const int pos = step->pos;
@@ -857,29 +936,40 @@ __global__ void k_repack_plain(const int8_t *src, int K, int N, int Kpad, int Np
 }
 
 // ---------------------------------------------------- tensor parallelism
-// Absmax of one row (quant.c:104-106), the local part of a row-parallel
-// product's activation scale; the ranks then max-reduce it.
-__global__ void __launch_bounds__(kThreads) k_row_absmax(const float *x, int n, float *out) {
+// Absmax of a row-parallel product's input over the whole group: this rank's
+// absmax (quant.c:104-106) goes to every rank's region, the group maximum of
+// all ranks' values to *out.  One CTA.
+__global__ void __launch_bounds__(kThreads) k_tp_absmax(const float *x, int n, float *out, TpExchange t, int *err) {
   __shared__ float s_red[32];
+  __shared__ int s_bad;
   pdl_launch_dependents();
   pdl_wait();
   float m = 0.0f;
   for (int k = threadIdx.x; k < n; k += kThreads) m = fmaxf(m, fabsf(x[k]));
   m = block_max<kThreads>(m, s_red);
-  if (threadIdx.x == 0) *out = m;
-}
-
-// Residual update after the ranks' partial sums are added (exact in int32):
-// x[j] += (as * ws[j]) * acc[j] with as from the reduced absmax (quant.c:106,
-// 117; llama.c:578, 589).
-__global__ void k_tp_resid(float *x, const int *acc, const float *absmax, const float *ws, int n) {
-  pdl_launch_dependents();
-  pdl_wait();
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= n) return;
-  const float m = *absmax;
-  const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
-  x[j] = __fadd_rn(x[j], dequant(as, ws[j], acc[j]));
+  const unsigned epoch = *t.seq + t.pidx + 1;
+  const int par = epoch & 1u;
+  const size_t ao = tpx_amax_off(t.world, t.dm), fo = tpx_famax_off(t.world, t.dm);
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  if (threadIdx.x < t.world) {
+    char *peer = t.peers[threadIdx.x];
+    reinterpret_cast<float *>(peer + ao)[par * t.world + t.rank] = m;
+    __threadfence_system();
+    st_release_u32(reinterpret_cast<unsigned *>(peer + fo) + t.rank, epoch);
+    if (!wait_flag(reinterpret_cast<const unsigned *>(t.peers[t.rank] + fo) + threadIdx.x, epoch)) s_bad = 1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (s_bad) {
+      atomicOr(err, ERR_TIMEOUT);
+      return;
+    }
+    const float *am = reinterpret_cast<const float *>(t.peers[t.rank] + ao) + par * t.world;
+    float g = 0.0f;
+    for (int q = 0; q < t.world; ++q) g = fmaxf(g, __ldcv(am + q));
+    *out = g;
+  }
 }
 
 // expf of a batch (tests compare this against the host libm over all inputs).
