@@ -224,6 +224,17 @@ def run_ours(args, rank, world):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_value = world * K / float(t.item())
 
+    # ---- the same K positions with the CLI's sampler settings (main.c:643-645),
+    # drawn on the device inside each step's graph
+    kv.len = start_len
+    rng = lib.rng_create(1234)
+    if lib.q_llama_generate_sample(C.byref(m), C.byref(kv), start_tok, K, 0.8, 40, 0.95, C.byref(rng), ids) != 0:
+        llmq.check(lib)
+    s_ms = float(lib.q_llama_last_step_ms())
+    sampled = {"value": round(world * K / (s_ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(s_ms / K, 4),
+               "api": "q_llama_generate_sample (temperature 0.8, top-k 40, top-p 0.95, seed 1234)",
+               "sampler_ms_per_step": round((s_ms - ms) / K, 4)}
+
     # ---- one step replayed kernel by kernel (no graph, no overlap): where the time goes
     nk = int(lib.llmq_kernels_per_step(C.byref(m)))
     prof = np.zeros(nk, np.float32)
@@ -287,6 +298,7 @@ def run_ours(args, rank, world):
                 "same_tokens_as_value_run": e2e_ids == gen_ids},
         "roofline": roofline,
         "cpu_baseline": cpu,
+        "sampled_decode": sampled,
         "step_profile": step_profile,
         "gemv_sweep": gemv_sweep(lib, [1, 64], hbm_peak) if args.workload == "8b" else None,
         "gpu_launches": K * int(lib.llmq_kernels_per_step(C.byref(m))),

@@ -104,6 +104,14 @@ typedef struct {
 } QLlamaModel;
 #endif
 
+#ifndef SAMPLER_H
+#define SAMPLER_H
+/* xorshift64 stream (sampler.h:13-15). */
+typedef struct {
+  unsigned long long state;
+} Rng;
+#endif
+
 /* ========================================================================= */
 /* quant.h entry points                                                       */
 /* ========================================================================= */
@@ -165,6 +173,27 @@ void llama_kv_free(LlamaKV *kv);
 void q_llama_decode_step(const QLlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
 
 /* ========================================================================= */
+/* sampler.h entry points (sampler.c, the generation loop's token choice)     */
+/* ========================================================================= */
+
+/* Replace sampler.c:26-30 and sampler.c:41-44 (host arithmetic, same stream). */
+Rng rng_create(unsigned long long seed);
+float rng_uniform(Rng *r);
+
+/* Replaces sampler.c:8-21 (sampler.h:10): the first index of the largest
+ * logit of row `row`, computed on the GPU. */
+int sample_argmax(const Tensor *logits, int row);
+
+/* Replaces sampler.c:60-115 (sampler.h:25-26): temperature, top-k and top-p
+ * sampling of row `row` on the GPU, advancing *rng by one draw (none when
+ * temperature <= 0).  The returned id equals the reference's for every input,
+ * ties included (glibc's stable qsort order: p descending, then index).  The
+ * GPU keeps up to 1024 candidates: top_k must be in 1..1024 unless vocab <=
+ * 1024; otherwise -1 is returned with q_llama_last_error() set and *rng
+ * unchanged. */
+int sample_token(const Tensor *logits, int row, float temperature, int top_k, float top_p, Rng *rng);
+
+/* ========================================================================= */
 /* Additions (no counterpart in the reference headers)                        */
 /* ========================================================================= */
 
@@ -189,6 +218,21 @@ void q_llama_clear_error(void);
  * `logits` may be NULL, in which case no logits are copied to the host (4 bytes
  * cross PCIe per token).  Returns -1 on error. */
 int q_llama_decode_step_argmax(const QLlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
+
+/* q_llama_decode_step followed by sample_token on its logits row
+ * (main.c:663-668), with the sampler run on the GPU inside the same graph:
+ * returns the drawn next token (-1 on error) and advances kv->len and *rng.
+ * `logits` may be NULL.  temperature <= 0 takes the greedy id and draws
+ * nothing; top_k follows sample_token's limit.  Additive extension. */
+int q_llama_decode_step_sample(const QLlamaModel *m, LlamaKV *kv, int token, float temperature, int top_k,
+                               float top_p, Rng *rng, Tensor *logits);
+
+/* Sampled generation chained on the GPU: as q_llama_generate, with each next
+ * token drawn by the sampler (the reference's loop of q_llama_decode_step and
+ * sample_token, main.c:663-668).  ids[i] is the token drawn after step i;
+ * kv->len advances by n and *rng by n draws.  Returns 0 or an error code. */
+int q_llama_generate_sample(const QLlamaModel *m, LlamaKV *kv, int token, int n, float temperature, int top_k,
+                            float top_p, Rng *rng, int *ids);
 
 /* Batched decode: one token for each of B sequences at once.  Sequence b feeds
  * tokens[b] at position kvs[b]->len of its own cache; row b of `logits`

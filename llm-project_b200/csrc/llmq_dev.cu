@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <functional>
@@ -18,6 +19,7 @@
 #include "llmq_kernels.cuh"
 #include "llmq_tc_gemm.cuh"
 #include "llmq_rows.cuh"
+#include "llmq_sample.cuh"
 
 using namespace llmq;
 
@@ -80,6 +82,9 @@ struct DevCtx {
   float *tc_as = nullptr;
   int *tc_acc = nullptr;
   size_t tc_codes_n = 0, tc_as_n = 0, tc_acc_n = 0;
+  // standalone sampler: state, id, row and scratch
+  char *sample_buf = nullptr;
+  size_t sample_n = 0;
 };
 
 DevCtx g_ctx[kMaxDevices];
@@ -569,7 +574,8 @@ struct DevKV {
   DevModel *model = nullptr;
   int max_seq = 0;
   float *k = nullptr, *v = nullptr;  // [n_layers][max_seq][kvd]
-  cudaGraphExec_t graph[3] = {nullptr, nullptr, nullptr};  // device-chained, host io, host io + logits
+  // greedy: device-chained, host io, host io + logits; sampled: the same three
+  cudaGraphExec_t graph[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
 };
 
 struct DevModel {
@@ -589,8 +595,11 @@ struct DevModel {
   int *acc = nullptr, *cnt = nullptr, *err = nullptr, *result = nullptr, *tokens = nullptr;
   unsigned long long *argmax = nullptr;
   StepState *step = nullptr;
+  SampleState *sample = nullptr;  // sampler settings and xorshift64 state
+  float *sample_p = nullptr;      // [vocab_full] sampler scratch
   // pinned host staging
   StepState *h_step = nullptr;
+  SampleState *h_sample = nullptr;
   int *h_result = nullptr;
   int *h_tokens = nullptr;
   float *h_logits = nullptr;
@@ -660,7 +669,8 @@ void release_model(DevModel *M) {
   void *tp_ptrs[] = {M->tp_max, M->tp_acc, M->logits_full, M->tpx, M->tpx_peers_dev, M->tp_seq};
   for (void *p : tp_ptrs) cudaFree(p);
   void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o, M->scores,
-                      M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step};
+                      M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step,
+                      M->sample, M->sample_p};
   for (void *p : dev_ptrs) cudaFree(p);
   {
     auto &R = M->rows;
@@ -671,6 +681,7 @@ void release_model(DevModel *M) {
     cudaFreeHost(R.h_err);
   }
   cudaFreeHost(M->h_step);
+  cudaFreeHost(M->h_sample);
   cudaFreeHost(M->h_result);
   cudaFreeHost(M->h_tokens);
   cudaFreeHost(M->h_logits);
@@ -874,9 +885,11 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   if (!dev_zeros(&M->x, dm) || !dev_zeros(&M->q, (size_t)qd + kvd) || !dev_zeros(&M->o, qd) || !dev_zeros(&M->h, dff) ||
       !dev_zeros(&M->logits, std::max(cfg.vocab, max_npad)) || !dev_zeros(&M->acc, max_npad) ||
       !dev_zeros(&M->cnt, max_slabs) || !dev_zeros(&M->err, 4) || !dev_zeros(&M->result, 4) ||
-      !dev_zeros(&M->tokens, cfg.max_seq) || !dev_zeros(&M->argmax, 1) || !dev_zeros(&M->step, 1))
+      !dev_zeros(&M->tokens, cfg.max_seq) || !dev_zeros(&M->argmax, 1) || !dev_zeros(&M->step, 1) ||
+      !dev_zeros(&M->sample, 1) || !dev_zeros(&M->sample_p, M->vocab_full))
     return 0;
   CK(cudaMallocHost(&M->h_step, sizeof(StepState)));
+  CK(cudaMallocHost(&M->h_sample, sizeof(SampleState)));
   CK(cudaMallocHost(&M->h_result, 4 * sizeof(int)));
   CK(cudaMallocHost(&M->h_tokens, (size_t)cfg.max_seq * sizeof(int)));
   CK(cudaMallocHost(&M->h_logits, (size_t)M->vocab_full * sizeof(float)));
@@ -1007,7 +1020,9 @@ int row_parallel(DevModel *M, const Mat &w, const GemvPlan &p, const float *in, 
 
 // Records one decode step into the model stream.  mode 0: token/pos come from
 // the device state (chained steps); 1: copied from h_step, result copied back;
-// 2: as 1, plus the logits.
+// 2: as 1, plus the logits.  Modes 3-5 are modes 0-2 with the next token drawn
+// by k_sample (sampler.c:60-115) instead of the greedy argmax; in modes 4 and 5
+// the sampler settings and stream are copied in from h_sample and back out.
 int record_step(DevModel *M, DevKV *K, int mode) {
   if (M->tp_world > 1 && (!g_tp.comm || g_tp.world != M->tp_world)) {
     llmq_set_error(LLMQ_ERR_STATE, "libllmq_cuda: the tensor-parallel group of this shard is gone");
@@ -1024,7 +1039,10 @@ int record_step(DevModel *M, DevKV *K, int mode) {
   cudaStream_t st = M->stream;
   const LlmqConfig &cfg = M->cfg;
   const size_t per_layer = (size_t)K->max_seq * M->kvd;
-  if (mode > 0) CK(cudaMemcpyAsync(M->step, M->h_step, sizeof(StepState), cudaMemcpyHostToDevice, st));
+  const bool sampled = mode >= 3, host_io = mode % 3 != 0, want_logits = mode % 3 == 2;
+  if (host_io) CK(cudaMemcpyAsync(M->step, M->h_step, sizeof(StepState), cudaMemcpyHostToDevice, st));
+  if (host_io && sampled)
+    CK(cudaMemcpyAsync(M->sample, M->h_sample, sizeof(SampleState), cudaMemcpyHostToDevice, st));
   for (int l = 0; l < cfg.n_layers; ++l) {
     {
       GemvArgs a = base_args(M->qkv[l], M->p_qkv, M->acc, M->cnt, M->err);
@@ -1111,14 +1129,27 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       PROF_MARK();
   }
   if (M->tp_world > 1) {  // the first maximum over every shard's vocab slice (sampler.c:8-21)
-    NK(g_nccl.AllReduce(M->argmax, M->argmax, 1, ncclUint64, ncclMax, g_tp.comm, st));
-    if (mode == 2) NK(g_nccl.AllGather(M->logits, M->logits_full, (size_t)cfg.vocab, ncclFloat32, g_tp.comm, st));
+    if (!sampled) NK(g_nccl.AllReduce(M->argmax, M->argmax, 1, ncclUint64, ncclMax, g_tp.comm, st));
+    if (want_logits || sampled)
+      NK(g_nccl.AllGather(M->logits, M->logits_full, (size_t)cfg.vocab, ncclFloat32, g_tp.comm, st));
+  }
+  if (sampled) {  // every rank draws from the same whole row with the same stream
+    SampleArgs a{};
+    a.logits = M->tp_world > 1 ? M->logits_full : M->logits;
+    a.V = M->vocab_full;
+    a.st = M->sample;
+    a.p = M->sample_p;
+    a.argmax = M->argmax;
+    CK(launch_pdl(k_sample, dim3(1), dim3(kSampleThreads), 0, st, a));
+    PROF_MARK();
   }
   CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st,
                    M->tp_world > 1 ? M->tp_seq : nullptr, 2u * (unsigned)cfg.n_layers));
       PROF_MARK();
-  if (mode > 0) CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
-  if (mode == 2)
+  if (host_io) CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (host_io && sampled)
+    CK(cudaMemcpyAsync(M->h_sample, M->sample, sizeof(SampleState), cudaMemcpyDeviceToHost, st));
+  if (want_logits)
     CK(cudaMemcpyAsync(M->h_logits, M->tp_world > 1 ? M->logits_full : M->logits,
                        (size_t)M->vocab_full * sizeof(float), cudaMemcpyDeviceToHost, st));
 #undef PROF_MARK
@@ -1555,17 +1586,33 @@ void llmqd_kv_release(const LlamaKV *kv) {
   if (cur >= 0) cudaSetDevice(cur);
 }
 
-int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next) {
+static_assert(sizeof(SampleState) == sizeof(LlmqSample) && offsetof(SampleState, rng) == offsetof(LlmqSample, rng),
+              "LlmqSample mirrors SampleState");
+
+int check_sample(const LlmqSample *s, int V) {
+  if (!(s->temperature <= 0.0f) && (s->k < 1 || s->k > kSampleMaxK || s->k > V)) {
+    llmq_set_error(LLMQ_ERR_ARG,
+                   "libllmq_cuda: device sampling keeps 1..%d candidates; top-k resolves to %d of vocab %d "
+                   "(sample on the host from the logits instead)",
+                   kSampleMaxK, s->k, V);
+    return 0;
+  }
+  return 1;
+}
+
+int decode_one(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next, LlmqSample *smp) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   DevModel *M = get_model(m);
   if (!M) return 0;
   DevKV *K = get_kv(M, kv);
   if (!K || !check_step_inputs(M, kv, token, 1)) return 0;
-  const int mode = logits ? 2 : 1;
+  if (smp && !check_sample(smp, M->vocab_full)) return 0;
+  const int mode = (logits ? 2 : 1) + (smp ? 3 : 0);
   cudaGraphExec_t g = nullptr;
   if (!get_graph(M, K, mode, &g)) return 0;
   M->h_step->token = token;
   M->h_step->pos = kv->len;
+  if (smp) std::memcpy(M->h_sample, smp, sizeof(SampleState));
   CK(cudaEventRecord(M->ev0, M->stream));
   CK(cudaGraphLaunch(g, M->stream));
   CK(cudaEventRecord(M->ev1, M->stream));
@@ -1574,32 +1621,99 @@ int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token, float *logi
   if (M->h_result[1]) return reset_after_device_error(M, M->h_result[1]);
   if (logits) std::memcpy(logits, M->h_logits, (size_t)M->vocab_full * sizeof(float));
   if (next) *next = M->h_result[0];
+  if (smp) smp->rng = M->h_sample->rng;
   return 1;
 }
 
-int llmqd_generate(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids) {
+int generate_n(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids, LlmqSample *smp) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   DevModel *M = get_model(m);
   if (!M) return 0;
   DevKV *K = get_kv(M, kv);
   if (!K || n < 0 || !check_step_inputs(M, kv, token, n)) return 0;
+  if (smp && !check_sample(smp, M->vocab_full)) return 0;
   if (n == 0) return 1;
   cudaGraphExec_t g = nullptr;
-  if (!get_graph(M, K, 0, &g)) return 0;
+  if (!get_graph(M, K, smp ? 3 : 0, &g)) return 0;
   M->h_step->token = token;
   M->h_step->pos = kv->len;
   cudaStream_t st = M->stream;
   CK(cudaMemcpyAsync(M->step, M->h_step, sizeof(StepState), cudaMemcpyHostToDevice, st));
   CK(cudaMemsetAsync(M->result, 0, 4 * sizeof(int), st));
+  if (smp) {
+    std::memcpy(M->h_sample, smp, sizeof(SampleState));
+    CK(cudaMemcpyAsync(M->sample, M->h_sample, sizeof(SampleState), cudaMemcpyHostToDevice, st));
+  }
   CK(cudaEventRecord(M->ev0, st));
   for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(g, st));
   CK(cudaEventRecord(M->ev1, st));
   CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
   CK(cudaMemcpyAsync(M->h_tokens, M->tokens + kv->len, (size_t)n * sizeof(int), cudaMemcpyDeviceToHost, st));
+  if (smp) CK(cudaMemcpyAsync(M->h_sample, M->sample, sizeof(SampleState), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
   cudaEventElapsedTime(&g_last_ms, M->ev0, M->ev1);
   if (M->h_result[3]) return reset_after_device_error(M, M->h_result[3]);
   std::memcpy(ids, M->h_tokens, (size_t)n * sizeof(int));
+  if (smp) smp->rng = M->h_sample->rng;
+  return 1;
+}
+
+int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next) {
+  return decode_one(m, kv, token, logits, next, nullptr);
+}
+
+int llmqd_decode_sample(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next,
+                        LlmqSample *smp) {
+  return decode_one(m, kv, token, logits, next, smp);
+}
+
+int llmqd_generate(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids) {
+  return generate_n(m, kv, token, n, ids, nullptr);
+}
+
+int llmqd_generate_sample(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids, LlmqSample *smp) {
+  return generate_n(m, kv, token, n, ids, smp);
+}
+
+// One logits row in host memory, sampled on the current device (the
+// standalone sample_token / sample_argmax).
+int llmqd_sample_row(const float *row, int V, LlmqSample *smp, int *id) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!row || V <= 0 || !smp || !id) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: bad sampler arguments");
+    return 0;
+  }
+  if (!check_sample(smp, V)) return 0;
+  DevCtx *c = get_ctx();
+  if (!c) return 0;
+  cudaStream_t st = c->stream;
+  // [V] logits, [V] scratch, the state, the id
+  const size_t need = 2 * (size_t)V * sizeof(float) + sizeof(SampleState) + 16;
+  if (c->sample_n < need) {
+    cudaFree(c->sample_buf);
+    c->sample_buf = nullptr;
+    c->sample_n = 0;
+    CK(cudaMalloc(&c->sample_buf, need));
+    c->sample_n = need;
+  }
+  SampleState *d_st = reinterpret_cast<SampleState *>(c->sample_buf);
+  int *d_id = reinterpret_cast<int *>(c->sample_buf + sizeof(SampleState));
+  float *d_row = reinterpret_cast<float *>(c->sample_buf + sizeof(SampleState) + 16);
+  SampleArgs a{};
+  a.logits = d_row;
+  a.V = V;
+  a.st = d_st;
+  a.p = d_row + V;
+  a.out = d_id;
+  CK(cudaMemcpyAsync(d_st, smp, sizeof(SampleState), cudaMemcpyHostToDevice, st));
+  CK(cudaMemcpyAsync(d_row, row, (size_t)V * sizeof(float), cudaMemcpyHostToDevice, st));
+  k_sample<<<1, kSampleThreads, 0, st>>>(a);
+  CK(cudaGetLastError());
+  LlmqSample back{};
+  CK(cudaMemcpyAsync(&back, d_st, sizeof(SampleState), cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(id, d_id, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  smp->rng = back.rng;
   return 1;
 }
 

@@ -406,6 +406,111 @@ LLMQ_API int q_llama_generate(const QLlamaModel *m, LlamaKV *kv, int token, int 
   return LLMQ_OK;
 }
 
+/* ---- sampler.h (sampler.c): the stream on the host, the draw on the GPU ---- */
+
+/* xorshift64 with the reference's shifts and non-zero default seed
+ * (sampler.c:26-39): the stream must be the same number for number. */
+LLMQ_API Rng rng_create(unsigned long long seed) {
+  Rng r;
+  r.state = seed ? seed : 0x9E3779B97F4A7C15ULL;
+  return r;
+}
+
+static unsigned long long rng_next(unsigned long long *s) {
+  unsigned long long x = *s;
+  x ^= x << 13;
+  x ^= x >> 7;
+  x ^= x << 17;
+  *s = x;
+  return x;
+}
+
+LLMQ_API float rng_uniform(Rng *r) {
+  /* top 53 bits times 2^-53, exact in double, then rounded to float (sampler.c:41-44) */
+  return (float)((double)(rng_next(&r->state) >> 11) * (1.0 / 9007199254740992.0));
+}
+
+/* The device form of one sampler call: top_k resolved to the number of
+ * candidates it keeps (sampler.c:87-88). */
+static LlmqSample sample_settings(int vocab, float temperature, int top_k, float top_p, const Rng *rng) {
+  LlmqSample s;
+  s.temperature = temperature;
+  s.k = (top_k > 0 && top_k < vocab) ? top_k : vocab;
+  s.top_p = top_p;
+  s.pad = 0;
+  s.rng = rng ? rng->state : 0;
+  return s;
+}
+
+static const float *logits_row(const Tensor *logits, int row, const char *who) {
+  if (!logits || !logits->data || !logits->shape || logits->ndim < 2 || logits->shape[1] <= 0 || row < 0 ||
+      (size_t)(row + 1) * (size_t)logits->shape[1] > logits->size) {
+    llmq_set_error(LLMQ_ERR_ARG, "%s: logits row %d out of range", who, row);
+    return NULL;
+  }
+  return logits->data + (size_t)row * (size_t)logits->shape[1];
+}
+
+LLMQ_API int sample_argmax(const Tensor *logits, int row) {
+  const float *r = logits_row(logits, row, "sample_argmax");
+  if (!r) return -1;
+  LlmqSample s = sample_settings(logits->shape[1], 0.0f, 0, 1.0f, NULL);
+  int id = -1;
+  if (!llmqd_sample_row(r, logits->shape[1], &s, &id)) return -1;
+  return id;
+}
+
+LLMQ_API int sample_token(const Tensor *logits, int row, float temperature, int top_k, float top_p, Rng *rng) {
+  const float *r = logits_row(logits, row, "sample_token");
+  if (!r) return -1;
+  if (!rng) {
+    llmq_set_error(LLMQ_ERR_ARG, "sample_token: rng is NULL");
+    return -1;
+  }
+  LlmqSample s = sample_settings(logits->shape[1], temperature, top_k, top_p, rng);
+  int id = -1;
+  if (!llmqd_sample_row(r, logits->shape[1], &s, &id)) return -1;
+  rng->state = s.rng;
+  return id;
+}
+
+LLMQ_API int q_llama_decode_step_sample(const QLlamaModel *m, LlamaKV *kv, int token, float temperature, int top_k,
+                                        float top_p, Rng *rng, Tensor *logits) {
+  if (!rng || (logits && (!logits->data || logits->size < (size_t)m->vocab))) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_decode_step_sample: bad rng or logits tensor (needs %d floats)",
+                   m->vocab);
+    return -1;
+  }
+  int next = -1;
+  float *out = logits ? logits->data : NULL;
+  if (temperature <= 0.0f) { /* greedy (sampler.c:65-67): the fused argmax, no draw */
+    if (!llmqd_decode(m, kv, token, out, &next)) return -1;
+  } else {
+    LlmqSample s = sample_settings(m->vocab, temperature, top_k, top_p, rng);
+    if (!llmqd_decode_sample(m, kv, token, out, &next, &s)) return -1;
+    rng->state = s.rng;
+  }
+  kv->len = kv->len + 1;
+  return next;
+}
+
+LLMQ_API int q_llama_generate_sample(const QLlamaModel *m, LlamaKV *kv, int token, int n, float temperature,
+                                     int top_k, float top_p, Rng *rng, int *ids) {
+  if (n < 0 || (n > 0 && !ids) || !rng) {
+    llmq_set_error(LLMQ_ERR_ARG, "q_llama_generate_sample: bad arguments");
+    return LLMQ_ERR_ARG;
+  }
+  if (temperature <= 0.0f) {
+    if (!llmqd_generate(m, kv, token, n, ids)) return q_llama_last_error();
+  } else {
+    LlmqSample s = sample_settings(m->vocab, temperature, top_k, top_p, rng);
+    if (!llmqd_generate_sample(m, kv, token, n, ids, &s)) return q_llama_last_error();
+    rng->state = s.rng;
+  }
+  kv->len = kv->len + n;
+  return LLMQ_OK;
+}
+
 LLMQ_API void q_llama_decode_batch(const QLlamaModel *m, LlamaKV **kvs, const int *tokens, int B, Tensor *logits) {
   if (!logits || !logits->data || B <= 0 || logits->size < (size_t)B * (size_t)m->vocab) {
     llmq_set_error(LLMQ_ERR_ARG, "q_llama_decode_batch: logits tensor must hold B x %d floats", m->vocab);

@@ -46,6 +46,25 @@ LLMQ_HIDDEN int llmqd_decode_rows(const QLlamaModel *m, LlamaKV *const *kvs, con
 LLMQ_HIDDEN int llmqd_prefill(const QLlamaModel *m, const LlamaKV *kv, const int *ids, int n, float *logits,
                               int *next);
 LLMQ_HIDDEN float llmqd_last_ms(void);
+
+/* Sampler settings (sampler.c:60-115) as the device keeps them: k is the
+ * number of candidates top-k keeps (top_k when 0 < top_k < vocab, else vocab,
+ * sampler.c:87-88); rng is Rng.state (sampler.h). */
+typedef struct {
+  float temperature;
+  int k;
+  float top_p;
+  int pad;
+  unsigned long long rng;
+} LlmqSample;
+/* As llmqd_decode, with the next token drawn by the sampler; smp->rng advances. */
+LLMQ_HIDDEN int llmqd_decode_sample(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next,
+                                    LlmqSample *smp);
+/* As llmqd_generate, each next token drawn by the sampler. */
+LLMQ_HIDDEN int llmqd_generate_sample(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids,
+                                      LlmqSample *smp);
+/* One host logits row of V floats sampled on the current device. */
+LLMQ_HIDDEN int llmqd_sample_row(const float *row, int V, LlmqSample *smp, int *id);
 /* Size of this process's tensor-parallel group (1 if none). */
 LLMQ_HIDDEN int llmqd_tp_world(void);
 

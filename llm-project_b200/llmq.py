@@ -25,6 +25,10 @@ class Tensor(C.Structure):  # tensor.h:10-16
                 ("size", C.c_size_t)]
 
 
+class Rng(C.Structure):  # sampler.h:13-15
+    _fields_ = [("state", C.c_ulonglong)]
+
+
 class QTensor(C.Structure):  # quant.h:22-26
     _fields_ = [("rows", C.c_int), ("cols", C.c_int), ("q", c_byte_p), ("scale", c_float_p)]
 
@@ -101,6 +105,14 @@ SIGNATURES = {
     "q_llama_model_shard": (C.c_int, [C.POINTER(QLlamaModel), C.c_int, C.c_int, C.POINTER(QLlamaModel)]),
     "q_llama_model_upload": (C.c_int, [C.POINTER(QLlamaModel)]),
     "q_llama_generate": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_int, c_int_p]),
+    "rng_create": (Rng, [C.c_ulonglong]),
+    "rng_uniform": (C.c_float, [C.POINTER(Rng)]),
+    "sample_argmax": (C.c_int, [C.POINTER(Tensor), C.c_int]),
+    "sample_token": (C.c_int, [C.POINTER(Tensor), C.c_int, C.c_float, C.c_int, C.c_float, C.POINTER(Rng)]),
+    "q_llama_decode_step_sample": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_float,
+                                             C.c_int, C.c_float, C.POINTER(Rng), C.POINTER(Tensor)]),
+    "q_llama_generate_sample": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_int,
+                                          C.c_float, C.c_int, C.c_float, C.POINTER(Rng), c_int_p]),
     "q_llama_last_step_ms": (C.c_float, []),
     "llmq_expf_device": (C.c_int, [c_float_p, c_float_p, C.c_longlong]),
     "llmq_bench_gemv": (C.c_int, [C.POINTER(QLlamaModel), C.c_int, C.c_int, C.c_int, c_float_p,
@@ -143,6 +155,10 @@ def load(path: str | None = None) -> C.CDLL:
     if path is None:
         _lib = lib
     return lib
+
+
+# error codes (llmq_cuda.h)
+LLMQ_OK, LLMQ_ERR_ARG, LLMQ_ERR_CUDA, LLMQ_ERR_NO_DEVICE, LLMQ_ERR_IO, LLMQ_ERR_OOM, LLMQ_ERR_STATE = range(7)
 
 
 class LlmqError(RuntimeError):

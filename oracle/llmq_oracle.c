@@ -118,6 +118,73 @@ int orc_argmax(const float *r, int n) {
   return best;
 }
 
+/* sampler.c:32-39 */
+unsigned long long orc_xorshift64(unsigned long long *state) {
+  unsigned long long x = *state;
+  x ^= x << 13;
+  x ^= x >> 7;
+  x ^= x << 17;
+  *state = x;
+  return x;
+}
+
+typedef struct {
+  float p;
+  int idx;
+} OrcCand;
+
+/* p descending, then index ascending: the order glibc's stable qsort leaves
+ * the reference's (p, index) array in (sampler.c:54-58, 84), as a total order. */
+static int orc_cand_order(const void *a, const void *b) {
+  const OrcCand *x = (const OrcCand *)a, *y = (const OrcCand *)b;
+  if (x->p > y->p) return -1;
+  if (x->p < y->p) return 1;
+  return (x->idx > y->idx) - (x->idx < y->idx);
+}
+
+int orc_sample_token(const float *l, int V, float temperature, int top_k, float top_p,
+                     unsigned long long *state) {
+  if (temperature <= 0.0f) return orc_argmax(l, V); /* sampler.c:65-67 */
+  float mx = l[0];                                  /* sampler.c:70-71 */
+  for (int j = 1; j < V; j++)
+    if (l[j] > mx) mx = l[j];
+  OrcCand *c = (OrcCand *)malloc((size_t)V * sizeof(OrcCand));
+  float sum = 0.0f; /* sampler.c:74-81 */
+  for (int j = 0; j < V; j++) {
+    const float e = expf((l[j] - mx) / temperature);
+    c[j].p = e;
+    c[j].idx = j;
+    sum += e;
+  }
+  for (int j = 0; j < V; j++) c[j].p /= sum;
+  qsort(c, (size_t)V, sizeof(OrcCand), orc_cand_order);
+  int keep = (top_k > 0 && top_k < V) ? top_k : V; /* sampler.c:87-99 */
+  if (top_p > 0.0f && top_p < 1.0f) {
+    float cum = 0.0f;
+    int n = 0;
+    while (n < keep) {
+      cum += c[n++].p;
+      if (cum >= top_p) break;
+    }
+    keep = n;
+  }
+  if (keep < 1) keep = 1;
+  float z = 0.0f; /* sampler.c:102-111 */
+  for (int i = 0; i < keep; i++) z += c[i].p;
+  const float u = (float)((double)(orc_xorshift64(state) >> 11) * (1.0 / 9007199254740992.0)) * z;
+  int chosen = c[keep - 1].idx;
+  float run = 0.0f;
+  for (int i = 0; i < keep; i++) {
+    run += c[i].p;
+    if (u <= run) {
+      chosen = c[i].idx;
+      break;
+    }
+  }
+  free(c);
+  return chosen;
+}
+
 LlamaKV orc_kv_create(const QLlamaModel *m) {
   /* llama.c:513-526 */
   LlamaKV kv;

@@ -2,7 +2,7 @@
  *
  * A plain-C restatement of the reference's int8 decode path
  * (marjoncajocon/llm-project quant.c, matrix.c qacc_*, rmsnorm.c, rope.c,
- * llama.c q_* section, sampler.c argmax).  Every function names the reference
+ * llama.c q_* section, sampler.c).  Every function names the reference
  * lines it follows and performs the same fp32 operations in the same order,
  * so its results are bit-identical to the reference's (checked against the
  * reference sources compiled into oracle/_ref/ and against tests/golden/).
@@ -37,6 +37,11 @@ void orc_rmsnorm_row(const float *x, const float *gamma, int n, float eps, float
 void orc_rope_heads_pos_row(float *x, int n_heads, int head_dim, float base, int pos);
 /* sampler.c:8-21 */
 int orc_argmax(const float *r, int n);
+/* sampler.c:32-39: one xorshift64 step. */
+unsigned long long orc_xorshift64(unsigned long long *state);
+/* sampler.c:60-115 on one row of V logits; *state is Rng.state. */
+int orc_sample_token(const float *l, int V, float temperature, int top_k, float top_p,
+                     unsigned long long *state);
 
 /* llama.c:513-526 / 290-294 */
 LlamaKV orc_kv_create(const QLlamaModel *m);

@@ -20,7 +20,7 @@ ROOT = os.path.dirname(HERE)
 sys.path.insert(0, os.path.join(ROOT, "llm-project_b200"))
 
 import llmq  # noqa: E402
-from llmq import (LlamaKV, LlamaModel, QLlamaModel, QTensor, Tensor, c_byte_p,  # noqa: E402
+from llmq import (LlamaKV, LlamaModel, QLlamaModel, QTensor, Rng, Tensor, c_byte_p,  # noqa: E402
                   c_float_p, c_int_p)
 
 ORACLE_PATH = os.path.join(HERE, "_build", "liboracle.so")
@@ -59,6 +59,8 @@ _ORC_SIGS = {
     "orc_rmsnorm_row": (None, [c_float_p, c_float_p, C.c_int, C.c_float, c_float_p]),
     "orc_rope_heads_pos_row": (None, [c_float_p, C.c_int, C.c_int, C.c_float, C.c_int]),
     "orc_argmax": (C.c_int, [c_float_p, C.c_int]),
+    "orc_xorshift64": (C.c_ulonglong, [C.POINTER(C.c_ulonglong)]),
+    "orc_sample_token": (C.c_int, [c_float_p, C.c_int, C.c_float, C.c_int, C.c_float, C.POINTER(C.c_ulonglong)]),
     "orc_kv_create": (LlamaKV, [C.POINTER(QLlamaModel)]),
     "orc_kv_free": (None, [C.POINTER(LlamaKV)]),
     "orc_decode_step": (None, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, c_float_p]),
@@ -85,6 +87,9 @@ _REF_SIGS = {
     "llama_model_forward": (None, [C.POINTER(LlamaModel), c_int_p, C.c_int, C.POINTER(Tensor)]),
     "llama_model_free": (None, [C.POINTER(LlamaModel)]),
     "sample_argmax": (C.c_int, [C.POINTER(Tensor), C.c_int]),
+    "rng_create": (Rng, [C.c_ulonglong]),
+    "rng_uniform": (C.c_float, [C.POINTER(Rng)]),
+    "sample_token": (C.c_int, [C.POINTER(Tensor), C.c_int, C.c_float, C.c_int, C.c_float, C.POINTER(Rng)]),
     "rmsnorm": (None, [C.POINTER(Tensor), C.POINTER(Tensor), C.POINTER(Tensor), C.c_float]),
     "rope_heads_pos": (None, [C.POINTER(Tensor), C.c_int, C.c_float, C.c_int]),
 }

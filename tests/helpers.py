@@ -144,3 +144,63 @@ def bits_equal(a: np.ndarray, b: np.ndarray) -> bool:
 
 TINY = dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768, max_seq=256,
             rope_base=10000.0, eps=1e-5)
+
+
+# ------------------------------------------------------------------ sampler
+def sampler_rows(seed=2024) -> dict:
+    """Logits rows for the sampler tests: smooth, peaked, tied, flat, with NaN
+    and infinities, tiny and 8B-vocabulary sized."""
+    g = np.random.default_rng(seed)
+    f32 = np.float32
+    rows = {
+        "normal32k": g.normal(0, 2, 32000).astype(f32),
+        "normal128k": g.normal(0, 3, 128256).astype(f32),
+        "ties": (np.round(g.normal(0, 2, 32000) * 2) / 2).astype(f32),
+        "flat": np.zeros(5000, f32),
+        "wide": g.normal(0, 60, 20000).astype(f32),  # most probabilities underflow to 0
+        "small": g.normal(0, 1, 7).astype(f32),
+        "v1024": g.normal(0, 1, 1024).astype(f32),
+    }
+    peaked = g.normal(0, 1, 128256).astype(f32)
+    peaked[g.integers(0, 128256, 30)] += 9.0
+    rows["peaked128k"] = peaked
+    nan0 = g.normal(0, 1, 1000).astype(f32)
+    nan0[0] = np.nan
+    rows["nan_first"] = nan0
+    nanm = g.normal(0, 1, 1000).astype(f32)
+    nanm[500] = np.nan
+    rows["nan_middle"] = nanm
+    ninf = g.normal(0, 1, 2000).astype(f32)
+    ninf[g.integers(0, 2000, 300)] = -np.inf
+    rows["neg_inf"] = ninf
+    pinf = g.normal(0, 1, 2000).astype(f32)
+    pinf[77] = np.inf
+    rows["pos_inf"] = pinf
+    return rows
+
+
+# (temperature, top_k, top_p): the CLI's settings (main.c:643-645, 771-772),
+# the selftest's (selftest.c:329-337), and the edges of each knob
+SAMPLER_SETTINGS = [
+    (0.8, 40, 0.95), (0.9, 40, 0.95), (1.0, 1, 1.0), (0.8, 8, 0.95), (1.0, 1024, 1.0), (1.5, 1024, 0.5),
+    (0.3, 40, 1.0), (1.0, 40, 0.0), (1.0, 50, 1e-9), (2.0, 700, 0.999), (0.0, 40, 0.95), (-1.0, 0, 1.0),
+    (1.0, 0, 1.0), (1.0, 0, 0.9), (float("nan"), 40, 0.95),
+]
+
+
+def sampler_k(V: int, top_k: int) -> int:
+    """Candidates the reference keeps after top-k (sampler.c:87-88)."""
+    return top_k if 0 < top_k < V else V
+
+
+def ref_sample(ref, row: np.ndarray, T, top_k, top_p, state: int) -> tuple[int, int]:
+    t = llmq.host_tensor(row.reshape(1, -1))
+    r = llmq.Rng(state)
+    tok = ref.sample_token(C.byref(t), 0, T, top_k, top_p, C.byref(r))
+    return tok, r.state
+
+
+def orc_sample(orc, row: np.ndarray, T, top_k, top_p, state: int) -> tuple[int, int]:
+    st = C.c_ulonglong(state)
+    tok = orc.orc_sample_token(fp(row), row.size, T, top_k, top_p, C.byref(st))
+    return tok, st.value

@@ -2,9 +2,10 @@
 (launched with torch.distributed.run, one process per GPU).
 
 Every rank decodes its shard of the same synthetic model; rank 0 compares the
-whole logits rows (gathered by the library on every rank) and the greedy ids
-of q_llama_generate with the oracle's single-sequence decode of the whole
-model, bit for bit, and writes the verdicts to <out_dir>/tp.json."""
+whole logits rows (gathered by the library on every rank), the greedy ids of
+q_llama_generate and the sampled ids of q_llama_generate_sample with the
+oracle's single-sequence decode of the whole model, bit for bit, and writes the
+verdicts to <out_dir>/tp.json."""
 from __future__ import annotations
 
 import ctypes as C
@@ -22,7 +23,7 @@ import torch.distributed as dist  # noqa: E402
 
 import llmq  # noqa: E402
 import oracle  # noqa: E402
-from helpers import TINY, bits_equal, orc_decode, synth  # noqa: E402
+from helpers import TINY, bits_equal, fp, orc_decode, orc_sample, synth  # noqa: E402
 
 CASES = [
     ("tiny_bias", TINY, True, [5, 77, 31999, 0, 1234, 42, 9, 17, 256, 3000]),
@@ -55,6 +56,14 @@ def main():
         gen = (C.c_int * n_gen)()
         if lib.q_llama_generate(C.byref(sh), C.byref(kv), int(np.argmax(got[-1])), n_gen, gen) != 0:
             llmq.check(lib)
+        # then sampled steps (temperature 0.8, top-k 40, top-p 0.95, seed 1234),
+        # every rank drawing from the gathered row with the same stream
+        n_smp = 8
+        smp = (C.c_int * n_smp)()
+        r = lib.rng_create(1234)
+        if lib.q_llama_generate_sample(C.byref(sh), C.byref(kv), gen[n_gen - 1], n_smp, 0.8, 40, 0.95, C.byref(r),
+                                       smp) != 0:
+            llmq.check(lib)
         if rank == 0:
             orc = oracle.load_oracle()
             full = synth(lib, cfg, seed=1234, with_bias=bias)
@@ -64,6 +73,17 @@ def main():
             want, _ = orc_decode(orc, full, ids)
             verdicts[name + ".logits"] = bits_equal(got, want)
             verdicts[name + ".generate"] = list(gen) == greedy[1:]
+            kvo = orc.orc_kv_create(C.byref(full))
+            row_o = np.zeros(cfg["vocab"], np.float32)
+            for tok in ids + greedy[:-1]:
+                orc.orc_decode_step(C.byref(full), C.byref(kvo), int(tok), fp(row_o))
+            st, tok, want_s = lib.rng_create(1234).state, greedy[-1], []
+            for _ in range(n_smp):
+                orc.orc_decode_step(C.byref(full), C.byref(kvo), int(tok), fp(row_o))
+                tok, st = orc_sample(orc, row_o, 0.8, 40, 0.95, st)
+                want_s.append(tok)
+            orc.orc_kv_free(C.byref(kvo))
+            verdicts[name + ".generate_sample"] = list(smp) == want_s and r.state == st
             lib.q_llama_model_free(C.byref(full))
         dist.barrier()
         lib.llama_kv_free(C.byref(kv))
