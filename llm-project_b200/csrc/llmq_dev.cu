@@ -258,6 +258,9 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_pv, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_finish, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_step_finish, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_sample_exp, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_sample_max, 0);
+  ea = ea != cudaSuccess ? ea : set_attr(k_sample, static_cast<int>(kSampleSmem));
   if (ea != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
     return nullptr;
@@ -596,7 +599,8 @@ struct DevModel {
   unsigned long long *argmax = nullptr;
   StepState *step = nullptr;
   SampleState *sample = nullptr;  // sampler settings and xorshift64 state
-  float *sample_p = nullptr;      // [vocab_full] sampler scratch
+  float *sample_e = nullptr;      // [vocab_full] sampler scratch
+  unsigned *sample_hist = nullptr;  // [kSampleBins + 1], zero between draws
   // pinned host staging
   StepState *h_step = nullptr;
   SampleState *h_sample = nullptr;
@@ -670,7 +674,7 @@ void release_model(DevModel *M) {
   for (void *p : tp_ptrs) cudaFree(p);
   void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o, M->scores,
                       M->h, M->logits, M->acc, M->cnt, M->err, M->result, M->tokens, M->argmax, M->step,
-                      M->sample, M->sample_p};
+                      M->sample, M->sample_e, M->sample_hist};
   for (void *p : dev_ptrs) cudaFree(p);
   {
     auto &R = M->rows;
@@ -886,7 +890,8 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
       !dev_zeros(&M->logits, std::max(cfg.vocab, max_npad)) || !dev_zeros(&M->acc, max_npad) ||
       !dev_zeros(&M->cnt, max_slabs) || !dev_zeros(&M->err, 4) || !dev_zeros(&M->result, 4) ||
       !dev_zeros(&M->tokens, cfg.max_seq) || !dev_zeros(&M->argmax, 1) || !dev_zeros(&M->step, 1) ||
-      !dev_zeros(&M->sample, 1) || !dev_zeros(&M->sample_p, M->vocab_full))
+      !dev_zeros(&M->sample, 1) || !dev_zeros(&M->sample_e, M->vocab_full) ||
+      !dev_zeros(&M->sample_hist, kSampleBins + 1))
     return 0;
   CK(cudaMallocHost(&M->h_step, sizeof(StepState)));
   CK(cudaMallocHost(&M->h_sample, sizeof(SampleState)));
@@ -1129,7 +1134,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       PROF_MARK();
   }
   if (M->tp_world > 1) {  // the first maximum over every shard's vocab slice (sampler.c:8-21)
-    if (!sampled) NK(g_nccl.AllReduce(M->argmax, M->argmax, 1, ncclUint64, ncclMax, g_tp.comm, st));
+    NK(g_nccl.AllReduce(M->argmax, M->argmax, 1, ncclUint64, ncclMax, g_tp.comm, st));
     if (want_logits || sampled)
       NK(g_nccl.AllGather(M->logits, M->logits_full, (size_t)cfg.vocab, ncclFloat32, g_tp.comm, st));
   }
@@ -1138,9 +1143,13 @@ int record_step(DevModel *M, DevKV *K, int mode) {
     a.logits = M->tp_world > 1 ? M->logits_full : M->logits;
     a.V = M->vocab_full;
     a.st = M->sample;
-    a.p = M->sample_p;
-    a.argmax = M->argmax;
-    CK(launch_pdl(k_sample, dim3(1), dim3(kSampleThreads), 0, st, a));
+    a.e = M->sample_e;
+    a.hist = M->sample_hist;
+    a.maxkey = M->argmax;  // the row's max comes with its argmax key
+    a.argmax = M->argmax;  // and the drawn id replaces it
+    CK(launch_pdl(k_sample_exp, dim3(sample_exp_grid(a.V)), dim3(kSampleExpThreads), 0, st, a));
+    PROF_MARK();
+    CK(launch_pdl(k_sample, dim3(1), dim3(kSampleThreads), kSampleSmem, st, a));
     PROF_MARK();
   }
   CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st,
@@ -1687,27 +1696,38 @@ int llmqd_sample_row(const float *row, int V, LlmqSample *smp, int *id) {
   DevCtx *c = get_ctx();
   if (!c) return 0;
   cudaStream_t st = c->stream;
-  // [V] logits, [V] scratch, the state, the id
-  const size_t need = 2 * (size_t)V * sizeof(float) + sizeof(SampleState) + 16;
+  // the state (32 B), the id and the argmax key (32 B), the histogram, then
+  // [V] logits and [V] scratch
+  const size_t hist_bytes = roundup((kSampleBins + 1) * 4, 256);
+  const size_t head = 64 + hist_bytes;
+  const size_t need = head + 2 * (size_t)roundup(V, 64) * sizeof(float);
   if (c->sample_n < need) {
     cudaFree(c->sample_buf);
     c->sample_buf = nullptr;
     c->sample_n = 0;
     CK(cudaMalloc(&c->sample_buf, need));
+    CK(cudaMemset(c->sample_buf, 0, head));
     c->sample_n = need;
   }
   SampleState *d_st = reinterpret_cast<SampleState *>(c->sample_buf);
-  int *d_id = reinterpret_cast<int *>(c->sample_buf + sizeof(SampleState));
-  float *d_row = reinterpret_cast<float *>(c->sample_buf + sizeof(SampleState) + 16);
+  int *d_id = reinterpret_cast<int *>(c->sample_buf + 32);
+  unsigned long long *d_key = reinterpret_cast<unsigned long long *>(c->sample_buf + 48);
+  unsigned *d_hist = reinterpret_cast<unsigned *>(c->sample_buf + 64);
+  float *d_row = reinterpret_cast<float *>(c->sample_buf + head);
   SampleArgs a{};
   a.logits = d_row;
   a.V = V;
   a.st = d_st;
-  a.p = d_row + V;
+  a.e = d_row + roundup(V, 64);
+  a.hist = d_hist;
+  a.maxkey = d_key;
   a.out = d_id;
   CK(cudaMemcpyAsync(d_st, smp, sizeof(SampleState), cudaMemcpyHostToDevice, st));
   CK(cudaMemcpyAsync(d_row, row, (size_t)V * sizeof(float), cudaMemcpyHostToDevice, st));
-  k_sample<<<1, kSampleThreads, 0, st>>>(a);
+  CK(cudaMemsetAsync(d_key, 0, sizeof(unsigned long long), st));
+  k_sample_max<<<std::min(c->num_sms, (V + 255) / 256), 256, 0, st>>>(d_row, V, d_key);
+  k_sample_exp<<<sample_exp_grid(V), kSampleExpThreads, 0, st>>>(a);
+  k_sample<<<1, kSampleThreads, kSampleSmem, st>>>(a);
   CK(cudaGetLastError());
   LlmqSample back{};
   CK(cudaMemcpyAsync(&back, d_st, sizeof(SampleState), cudaMemcpyDeviceToHost, st));
