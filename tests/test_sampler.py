@@ -47,6 +47,20 @@ def test_oracle_sampler_matches_reference(orc, ref):
                 assert (to, so) == (tr, sr), (name, T, k, p, d)
 
 
+def test_windowed_chain_sum_matches_sequential_loop(tmp_path):
+    """The GPU sampler's windowed evaluation of the softmax denominator
+    (llmq_sample.cuh), restated on the CPU in tests/sampler_chain_check.c,
+    equals the sequential float loop bit for bit on random rows of eight
+    kinds (ties, subnormals, dyadic values, wide ranges)."""
+    import os
+    import subprocess
+    src = os.path.join(os.path.dirname(os.path.abspath(__file__)), "sampler_chain_check.c")
+    exe = str(tmp_path / "chain_check")
+    subprocess.run(["gcc", "-O2", "-std=c11", "-ffp-contract=off", "-o", exe, src, "-lm"], check=True)
+    r = subprocess.run([exe, "600", "20000000"], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 def test_reference_sort_is_stable_on_ties(ref):
     """The premise of the tie rule: with all logits equal, the reference's
     top-k keeps the k lowest indices and top-p the lowest-index prefix
