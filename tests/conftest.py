@@ -39,7 +39,8 @@ def _ensure_built():
     orc = os.path.join(ROOT, "oracle", "_build", "liboracle.so")
     if not os.path.exists(orc):
         subprocess.run(["make", "-C", os.path.join(ROOT, "oracle")], check=True, capture_output=True)
-    if not os.path.exists(llmq.LIB_PATH):
+    cli = os.path.join(ROOT, "llm-project_b200", "bin", "llmq_run")
+    if not os.path.exists(llmq.LIB_PATH) or not os.path.exists(cli):
         subprocess.run(["make", "-C", os.path.join(ROOT, "llm-project_b200", "csrc")], check=True,
                        capture_output=True)
 
