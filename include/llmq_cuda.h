@@ -173,6 +173,48 @@ void llama_kv_free(LlamaKV *kv);
 void q_llama_decode_step(const QLlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
 
 /* ========================================================================= */
+/* llama.h fp32 (LLMA) decode entry points                                   */
+/* ========================================================================= */
+
+/* Replaces llama.c:275-288 (llama.h:101): the KV cache of an fp32 model, on
+ * the GPU (head-major as for the int8 model) plus the reference-shaped host
+ * arrays.  The model's GPU copy is made on first use. */
+LlamaKV llama_kv_create(const LlamaModel *m);
+
+/* Replaces llama.c:296-362 (llama.h:106): one decode step of an fp32 model on
+ * the GPU, bit-identical to the reference's.  Every product is fp32 with the
+ * reference's accumulation order (matrix.c:178-199: one sequential chain per
+ * output column, each product and sum rounded on its own); norms, RoPE,
+ * attention and SwiGLU are the int8 path's kernels.  The model is
+ * snapshotted at its first use: release the GPU copy with
+ * llmq_llama_model_release (or llmq_llama_model_free) before editing it. */
+void llama_decode_step(const LlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
+
+/* As llama_decode_step; returns the greedy next id (-1 on error); logits may
+ * be NULL.  Additive extension. */
+int llama_decode_step_argmax(const LlamaModel *m, LlamaKV *kv, int token, Tensor *logits);
+/* As q_llama_decode_step_sample, for an fp32 model. */
+int llama_decode_step_sample(const LlamaModel *m, LlamaKV *kv, int token, float temperature, int top_k,
+                             float top_p, Rng *rng, Tensor *logits);
+/* As q_llama_generate / q_llama_generate_sample, for an fp32 model. */
+int llama_generate(const LlamaModel *m, LlamaKV *kv, int token, int n, int *ids);
+int llama_generate_sample(const LlamaModel *m, LlamaKV *kv, int token, int n, float temperature, int top_k,
+                          float top_p, Rng *rng, int *ids);
+
+/* llama.c:390-440 under a name of this library: reads an LLMA (f32) or LLMQ
+ * (int8, dequantised on load as quant.c:29-33) checkpoint into an fp32 model
+ * in host memory (the GPU copy is made on first use).  Same messages and 0/1
+ * return as llama_model_load.  Free with llmq_llama_model_free. */
+int llmq_llama_model_load(const char *path, LlamaModel *out);
+/* Frees a model made by llmq_llama_model_load / llmq_synth_model_f32 and its
+ * GPU copy. */
+void llmq_llama_model_free(LlamaModel *m);
+/* Uploads / releases the GPU copy of an fp32 model (both otherwise implicit).
+ * Returns 0 or an error code. */
+int llmq_llama_model_upload(const LlamaModel *m);
+void llmq_llama_model_release(const LlamaModel *m);
+
+/* ========================================================================= */
 /* sampler.h entry points (sampler.c, the generation loop's token choice)     */
 /* ========================================================================= */
 
@@ -305,6 +347,12 @@ typedef struct {
  * Returns 0 or an error code. */
 int llmq_synth_model(const LlmqConfig *cfg, uint64_t seed, float stddev, int with_bias,
                      QLlamaModel *out);
+
+/* The fp32 model an LLMQ checkpoint of llmq_synth_model(cfg, seed, stddev,
+ * with_bias) loads as with llama_model_load (llama.c:419-427: every 2-D
+ * tensor dequantised).  Free with llmq_llama_model_free.  Returns 0 or an
+ * error code. */
+int llmq_synth_model_f32(const LlmqConfig *cfg, uint64_t seed, float stddev, int with_bias, LlamaModel *out);
 
 /* Tensor-parallel shard `rank` of `world` of the same synthetic model (no
  * reference counterpart): Wq/Wk/Wv and b_q/b_k/b_v keep the columns of this

@@ -13,6 +13,7 @@
 #include <functional>
 #include <mutex>
 #include <unordered_map>
+#include <thread>
 #include <vector>
 
 #include "llmq_internal.h"
@@ -20,6 +21,7 @@
 #include "llmq_tc_gemm.cuh"
 #include "llmq_rows.cuh"
 #include "llmq_sample.cuh"
+#include "llmq_f32.cuh"
 
 using namespace llmq;
 
@@ -103,6 +105,23 @@ void free_mat(Mat &m) {
   cudaFree(m.w);
   cudaFree(m.ws);
   m = Mat{};
+}
+
+// An fp32 matrix of the LLMA path, stored as one region per CTA (see
+// llmq_f32.cuh) for a grid of `grid` CTAs.
+struct MatF {
+  float *w = nullptr;
+  long long *cta_off = nullptr;
+  int *cta_u0 = nullptr;
+  int K = 0, N = 0, grid = 0, threads = 0, KC = 0, stages = 0, stage_floats = 0;
+  size_t smem = 0;
+};
+
+void free_matf(MatF &m) {
+  cudaFree(m.w);
+  cudaFree(m.cta_off);
+  cudaFree(m.cta_u0);
+  m = MatF{};
 }
 
 // Every kernel asks for the largest shared-memory carveout, so consecutive
@@ -261,6 +280,12 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_attr(k_sample_exp, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_sample_max, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_sample, static_cast<int>(kSampleSmem));
+  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_PLAIN, F32_EPI_RESID>, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_SWIGLU, F32_EPI_RESID>, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_RMSNORM, F32_EPI_QKV>, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_EMBED_RMSNORM, F32_EPI_QKV>, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_RMSNORM, F32_EPI_PLAIN>, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_RMSNORM, F32_EPI_LOGITS>, sm);
   if (ea != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
     return nullptr;
@@ -588,6 +613,12 @@ struct DevModel {
   int qd = 0, kvd = 0;
   std::vector<Mat> qkv, wo, w13, w2;
   Mat lm;
+  // fp32 (LLMA) model: the same step with fp32 products
+  bool f32 = false;
+  std::vector<MatF> fqkv, fwo, fw13, fw2;
+  MatF flm;
+  float *wte_f = nullptr;  // [vocab][d_model]
+  float *gu = nullptr;     // [2 * d_ff]: gate then up of the current step
   std::vector<float *> attn_norm, ffn_norm, bias_qkv;
   float *final_norm = nullptr;
   int8_t *wte_q = nullptr;
@@ -666,6 +697,11 @@ void release_model(DevModel *M) {
   for (auto *v : {&M->qkv, &M->wo, &M->w13, &M->w2})
     for (Mat &m : *v) free_mat(m);
   free_mat(M->lm);
+  for (auto *v : {&M->fqkv, &M->fwo, &M->fw13, &M->fw2})
+    for (MatF &m : *v) free_matf(m);
+  free_matf(M->flm);
+  cudaFree(M->wte_f);
+  cudaFree(M->gu);
   for (auto *v : {&M->attn_norm, &M->ffn_norm, &M->bias_qkv})
     for (float *p : *v) cudaFree(p);
   for (int q = 0; q < (int)M->tpx_peer.size(); ++q)
@@ -906,6 +942,255 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   return 1;
 }
 
+// ------------------------------------------------------------ fp32 models
+// Lays out the columns of up to three row-major [K][n_i] matrices, side by
+// side, as one region per CTA of a `grid`-CTA launch, and plans the launch.
+int build_matf(DevCtx &c, MatF &out, int K, const float *const src[3], const int ns[3], int grid) {
+  int N = 0;
+  for (int i = 0; i < 3; ++i) N += src[i] ? ns[i] : 0;
+  const int U = (N + kF32Unit - 1) / kF32Unit;
+  std::vector<int> u0(grid + 1);
+  std::vector<long long> off(grid + 1);
+  int nu_max = 0;
+  for (int g = 0; g <= grid; ++g) {
+    u0[g] = static_cast<int>((long long)g * U / grid);
+    off[g] = (long long)K * kF32Unit * u0[g];
+    if (g > 0) nu_max = std::max(nu_max, u0[g] - u0[g - 1]);
+  }
+  const int threads = std::max(32, roundup(nu_max * kF32Unit, 32));
+  if (threads > kF32MaxThreads) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 product with %d columns is wider than this build handles", N);
+    return 0;
+  }
+  std::vector<float> buf((size_t)K * U * kF32Unit, 0.0f);
+  auto fill = [&](int g0, int g1) {
+    for (int g = g0; g < g1; ++g) {
+      const int c0 = u0[g] * kF32Unit, nc = (u0[g + 1] - u0[g]) * kF32Unit;
+      for (int k = 0; k < K; ++k) {
+        float *dst = buf.data() + off[g] + (size_t)k * nc;
+        int base = 0;
+        for (int i = 0; i < 3; ++i) {
+          if (!src[i]) continue;
+          const int lo = std::max(c0, base), hi = std::min(c0 + nc, base + ns[i]);
+          if (lo < hi) std::memcpy(dst + (lo - c0), src[i] + (size_t)k * ns[i] + (lo - base), (size_t)(hi - lo) * 4);
+          base += ns[i];
+        }
+      }
+    }
+  };
+  {
+    const int nt = std::max(1, std::min(32, static_cast<int>(std::thread::hardware_concurrency())));
+    std::vector<std::thread> pool;
+    for (int t = 0; t < nt; ++t) pool.emplace_back(fill, t * grid / nt, (t + 1) * grid / nt);
+    for (auto &th : pool) th.join();
+  }
+  if (!dev_upload(&out.w, buf.data(), buf.size()) || !dev_upload(&out.cta_off, off.data(), off.size()) ||
+      !dev_upload(&out.cta_u0, u0.data(), u0.size()))
+    return 0;
+  out.K = K;
+  out.N = N;
+  out.grid = grid;
+  out.threads = threads;
+  // ring slots of about 24 KB, as many as fit beside the input row (and its squares)
+  const size_t xs_bytes = (2 * (size_t)roundup(K, 4) + 8) * sizeof(float);
+  int KC = std::max(4, std::min(256, 24576 / (nu_max * kF32Unit * 4))) & ~3;
+  for (;;) {
+    const size_t slot = (size_t)KC * nu_max * kF32Unit * 4;
+    const long long room = (long long)c.max_smem - 1024 - (long long)xs_bytes;
+    const int S = room > 0 ? static_cast<int>(std::min<long long>(kF32MaxStages, room / (long long)slot)) : 0;
+    if (S >= 2 || KC == 4) {
+      if (S < 2) {
+        llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 product (K %d) does not fit in shared memory", K);
+        return 0;
+      }
+      out.KC = KC;
+      out.stages = S;
+      out.stage_floats = KC * nu_max * kF32Unit;
+      out.smem = (size_t)S * slot + xs_bytes;
+      return 1;
+    }
+    KC = std::max(4, (KC / 2) & ~3);
+  }
+}
+
+template <int PRO, int EPI>
+cudaError_t launch_f32(const MatF &m, F32Args a, cudaStream_t st, bool pdl = true) {
+  a.w = m.w;
+  a.cta_off = m.cta_off;
+  a.cta_u0 = m.cta_u0;
+  a.K = m.K;
+  a.N = m.N;
+  a.KC = m.KC;
+  a.stages = m.stages;
+  a.stage_floats = m.stage_floats;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(m.grid);
+  cfg.blockDim = dim3(m.threads);
+  cfg.dynamicSmemBytes = m.smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+  ++g_launches;
+  return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI>, a);
+}
+
+int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
+  if (g_tp.world > 1) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 models decode on one GPU (no tensor-parallel group)");
+    return 0;
+  }
+  LlmqConfig &cfg = M->cfg;
+  cfg.vocab = m->vocab;
+  cfg.d_model = m->d_model;
+  cfg.n_layers = m->n_layers;
+  cfg.n_heads = m->n_heads;
+  cfg.n_kv = m->n_kv;
+  cfg.head_dim = m->head_dim;
+  cfg.d_ff = m->d_ff;
+  cfg.max_seq = m->max_seq;
+  cfg.rope_base = m->rope_base;
+  cfg.eps = m->eps;
+  M->f32 = true;
+  M->vocab_full = m->vocab;
+  M->kvd_full = m->n_kv * m->head_dim;
+  const int dm = cfg.d_model, hd = cfg.head_dim, dff = cfg.d_ff, L = cfg.n_layers;
+  M->qd = cfg.n_heads * hd;
+  M->kvd = cfg.n_kv * hd;
+  const int qd = M->qd, kvd = M->kvd;
+  if (hd % 2 != 0 || hd > 256) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: head_dim %d unsupported (even, <= 256)", hd);
+    return 0;
+  }
+  auto shape_ok = [](const Tensor &t, int r, int cc) {
+    return t.data && t.ndim == 2 && t.shape && t.shape[0] == r && t.shape[1] == cc;
+  };
+  M->device = c.device;
+  CK(cudaStreamCreateWithFlags(&M->stream, cudaStreamNonBlocking));
+  CK(cudaEventCreate(&M->ev0));
+  CK(cudaEventCreate(&M->ev1));
+  const int grid = c.num_sms;
+  for (int l = 0; l < L; ++l) {
+    const LlamaBlock &b = m->blocks[l];
+    if (!shape_ok(b.Wq, dm, qd) || !shape_ok(b.Wk, dm, kvd) || !shape_ok(b.Wv, dm, kvd) || !shape_ok(b.Wo, qd, dm) ||
+        !shape_ok(b.Wgate, dm, dff) || !shape_ok(b.Wup, dm, dff) || !shape_ok(b.Wdown, dff, dm)) {
+      llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: layer %d weights do not match the model config", l);
+      return 0;
+    }
+    {
+      const float *src[3] = {b.Wq.data, b.Wk.data, b.Wv.data};
+      const int ns[3] = {qd, kvd, kvd};
+      M->fqkv.emplace_back();
+      if (!build_matf(c, M->fqkv.back(), dm, src, ns, grid)) return 0;
+      std::vector<float> bias((size_t)qd + 2 * kvd, 0.0f);  // llama.c:316-318 (absent biases are zero)
+      if (b.b_q.data) std::memcpy(bias.data(), b.b_q.data, qd * sizeof(float));
+      if (b.b_k.data) std::memcpy(bias.data() + qd, b.b_k.data, kvd * sizeof(float));
+      if (b.b_v.data) std::memcpy(bias.data() + qd + kvd, b.b_v.data, kvd * sizeof(float));
+      float *db = nullptr;
+      if (!dev_upload(&db, bias.data(), bias.size())) return 0;
+      M->bias_qkv.push_back(db);
+    }
+    {
+      const float *src[3] = {b.Wo.data, nullptr, nullptr};
+      const int ns[3] = {dm, 0, 0};
+      M->fwo.emplace_back();
+      if (!build_matf(c, M->fwo.back(), qd, src, ns, grid)) return 0;
+    }
+    {
+      const float *src[3] = {b.Wgate.data, b.Wup.data, nullptr};
+      const int ns[3] = {dff, dff, 0};
+      M->fw13.emplace_back();
+      if (!build_matf(c, M->fw13.back(), dm, src, ns, grid)) return 0;
+    }
+    {
+      const float *src[3] = {b.Wdown.data, nullptr, nullptr};
+      const int ns[3] = {dm, 0, 0};
+      M->fw2.emplace_back();
+      if (!build_matf(c, M->fw2.back(), dff, src, ns, grid)) return 0;
+    }
+    float *an = nullptr, *fn = nullptr;
+    if (!dev_upload(&an, b.attn_norm.data, dm) || !dev_upload(&fn, b.ffn_norm.data, dm)) return 0;
+    M->attn_norm.push_back(an);
+    M->ffn_norm.push_back(fn);
+  }
+  if (!shape_ok(m->lm_head, dm, cfg.vocab) || !shape_ok(m->wte, cfg.vocab, dm) || !m->final_norm.data) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: embedding / lm-head shapes do not match the model config");
+    return 0;
+  }
+  {
+    const float *src[3] = {m->lm_head.data, nullptr, nullptr};
+    const int ns[3] = {cfg.vocab, 0, 0};
+    if (!build_matf(c, M->flm, dm, src, ns, grid)) return 0;
+  }
+  if (!dev_upload(&M->final_norm, m->final_norm.data, dm)) return 0;
+  if (!dev_upload(&M->wte_f, m->wte.data, (size_t)cfg.vocab * dm)) return 0;
+  {
+    const size_t n = (size_t)cfg.max_seq * (hd / 2);
+    std::vector<float> cs(n), sn(n);
+    llmq_rope_tables(cfg.rope_base, hd, cfg.max_seq, cs.data(), sn.data());
+    if (!dev_upload(&M->rope_cos, cs.data(), n) || !dev_upload(&M->rope_sin, sn.data(), n)) return 0;
+  }
+  {
+    AttnArgs probe{};
+    probe.n_heads = cfg.n_heads;
+    probe.n_kv = cfg.n_kv;
+    probe.hd = hd;
+    probe.max_seq = cfg.max_seq;
+    probe.pv_whole = pv_whole_bytes(cfg.max_seq) <= kPVWholeLimit;
+    M->attn_smem = std::max(scores_smem(probe), pv_smem(probe));
+  }
+  if (M->attn_smem > (size_t)c.max_smem) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: max_seq %d too long for the attention kernel", cfg.max_seq);
+    return 0;
+  }
+  if (!dev_zeros(&M->scores, (size_t)cfg.n_heads * cfg.max_seq) || !dev_zeros(&M->x, dm) ||
+      !dev_zeros(&M->q, (size_t)qd + kvd) || !dev_zeros(&M->o, qd) || !dev_zeros(&M->gu, 2 * (size_t)dff) ||
+      !dev_zeros(&M->logits, cfg.vocab) || !dev_zeros(&M->err, 4) || !dev_zeros(&M->result, 4) ||
+      !dev_zeros(&M->tokens, cfg.max_seq) || !dev_zeros(&M->argmax, 1) || !dev_zeros(&M->step, 1) ||
+      !dev_zeros(&M->sample, 1) || !dev_zeros(&M->sample_e, M->vocab_full) ||
+      !dev_zeros(&M->sample_hist, kSampleBins + 1))
+    return 0;
+  CK(cudaMallocHost(&M->h_step, sizeof(StepState)));
+  CK(cudaMallocHost(&M->h_sample, sizeof(SampleState)));
+  CK(cudaMallocHost(&M->h_result, 4 * sizeof(int)));
+  CK(cudaMallocHost(&M->h_tokens, (size_t)cfg.max_seq * sizeof(int)));
+  CK(cudaMallocHost(&M->h_logits, (size_t)M->vocab_full * sizeof(float)));
+  CK(cudaDeviceSynchronize());
+  return 1;
+}
+
+DevModel *get_model_f32(const LlamaModel *m) {
+  if (!m || !m->blocks) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: null model");
+    return nullptr;
+  }
+  auto it = g_models.find(m->blocks);
+  if (it != g_models.end()) {
+    DevModel *M = it->second;
+    if (!M->f32) {
+      llmq_set_error(LLMQ_ERR_STATE, "libllmq_cuda: these blocks belong to an int8 model");
+      return nullptr;
+    }
+    if (cudaSetDevice(M->device) != cudaSuccess) {
+      llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cannot select device %d", M->device);
+      return nullptr;
+    }
+    return M;
+  }
+  DevCtx *c = get_ctx();
+  if (!c) return nullptr;
+  DevModel *M = new DevModel();
+  M->key = m->blocks;
+  if (!upload_model_f32(*c, m, M)) {
+    release_model(M);
+    return nullptr;
+  }
+  g_models[M->key] = M;
+  return M;
+}
+
 DevModel *find_model(const QLlamaModel *m) {
   auto it = g_models.find(m->blocks);
   return it == g_models.end() ? nullptr : it->second;
@@ -917,6 +1202,10 @@ DevModel *get_model(const QLlamaModel *m) {
     return nullptr;
   }
   if (DevModel *M = find_model(m)) {
+    if (M->f32) {
+      llmq_set_error(LLMQ_ERR_STATE, "libllmq_cuda: these blocks belong to an fp32 model");
+      return nullptr;
+    }
     if (cudaSetDevice(M->device) != cudaSuccess) {
       llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cannot select device %d", M->device);
       return nullptr;
@@ -1048,8 +1337,35 @@ int record_step(DevModel *M, DevKV *K, int mode) {
   if (host_io) CK(cudaMemcpyAsync(M->step, M->h_step, sizeof(StepState), cudaMemcpyHostToDevice, st));
   if (host_io && sampled)
     CK(cudaMemcpyAsync(M->sample, M->h_sample, sizeof(SampleState), cudaMemcpyHostToDevice, st));
+  auto f32_args = [&]() {
+    F32Args a{};
+    a.err = M->err;
+    a.eps = cfg.eps;
+    a.step = M->step;
+    return a;
+  };
   for (int l = 0; l < cfg.n_layers; ++l) {
-    {
+    if (M->f32) {
+      F32Args a = f32_args();
+      a.in = M->x;
+      a.gamma = M->attn_norm[l];
+      a.out = M->q;
+      a.bias = M->bias_qkv[l];
+      a.qd = M->qd;
+      a.kvd = M->kvd;
+      a.hd = cfg.head_dim;
+      a.max_seq = K->max_seq;
+      a.vcache = K->v + l * per_layer;
+      if (l == 0) {
+        a.wte = M->wte_f;
+        a.vocab = M->vocab_full;
+        a.x_out = M->x;
+        CK((launch_f32<F32_PRO_EMBED_RMSNORM, F32_EPI_QKV>(M->fqkv[l], a, st, false)));
+      } else {
+        CK((launch_f32<F32_PRO_RMSNORM, F32_EPI_QKV>(M->fqkv[l], a, st)));
+      }
+      PROF_MARK();
+    } else {
       GemvArgs a = base_args(M->qkv[l], M->p_qkv, M->acc, M->cnt, M->err);
       a.in = M->x;
       a.gamma = M->attn_norm[l];
@@ -1094,7 +1410,13 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       CK(launch_attention(a, st, true, 1));
       PROF_MARK();
     }
-    if (M->tp_world > 1) {
+    if (M->f32) {
+      F32Args a = f32_args();
+      a.in = M->o;
+      a.out = M->x;
+      CK((launch_f32<F32_PRO_PLAIN, F32_EPI_RESID>(M->fwo[l], a, st)));
+      PROF_MARK();
+    } else if (M->tp_world > 1) {
       if (!row_parallel(M, M->wo[l], M->p_wo, M->o, 2 * l, st)) return 0;
     } else {
       GemvArgs a = base_args(M->wo[l], M->p_wo, M->acc, M->cnt, M->err);
@@ -1103,7 +1425,14 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       CK((launch_gemv<PRO_ABSMAX, EPI_RESID, 1>(a, M->p_wo, st, true)));
       PROF_MARK();
     }
-    {
+    if (M->f32) {
+      F32Args a = f32_args();
+      a.in = M->x;
+      a.gamma = M->ffn_norm[l];
+      a.out = M->gu;
+      CK((launch_f32<F32_PRO_RMSNORM, F32_EPI_PLAIN>(M->fw13[l], a, st)));
+      PROF_MARK();
+    } else {
       GemvArgs a = base_args(M->w13[l], M->p_w13, M->acc, M->cnt, M->err);
       a.in = M->x;
       a.gamma = M->ffn_norm[l];
@@ -1112,7 +1441,14 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       CK((launch_gemv<PRO_RMSNORM, EPI_SWIGLU, 1>(a, M->p_w13, st, true)));
       PROF_MARK();
     }
-    if (M->tp_world > 1) {
+    if (M->f32) {
+      F32Args a = f32_args();
+      a.in = M->gu;
+      a.dff = cfg.d_ff;
+      a.out = M->x;
+      CK((launch_f32<F32_PRO_SWIGLU, F32_EPI_RESID>(M->fw2[l], a, st)));
+      PROF_MARK();
+    } else if (M->tp_world > 1) {
       if (!row_parallel(M, M->w2[l], M->p_w2, M->h, 2 * l + 1, st)) return 0;
     } else {
       GemvArgs a = base_args(M->w2[l], M->p_w2, M->acc, M->cnt, M->err);
@@ -1122,7 +1458,15 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       PROF_MARK();
     }
   }
-  {
+  if (M->f32) {
+    F32Args a = f32_args();
+    a.in = M->x;
+    a.gamma = M->final_norm;
+    a.out = M->logits;
+    a.argmax = M->argmax;
+    CK((launch_f32<F32_PRO_RMSNORM, F32_EPI_LOGITS>(M->flm, a, st)));
+    PROF_MARK();
+  } else {
     GemvArgs a = base_args(M->lm, M->p_lm, M->acc, M->cnt, M->err);
     a.in = M->x;
     a.gamma = M->final_norm;
@@ -1609,9 +1953,8 @@ int check_sample(const LlmqSample *s, int V) {
   return 1;
 }
 
-int decode_one(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next, LlmqSample *smp) {
-  std::lock_guard<std::recursive_mutex> lk(g_mu);
-  DevModel *M = get_model(m);
+// One step of model M (the caller holds g_mu).
+int decode_one(DevModel *M, const LlamaKV *kv, int token, float *logits, int *next, LlmqSample *smp) {
   if (!M) return 0;
   DevKV *K = get_kv(M, kv);
   if (!K || !check_step_inputs(M, kv, token, 1)) return 0;
@@ -1634,9 +1977,8 @@ int decode_one(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits
   return 1;
 }
 
-int generate_n(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids, LlmqSample *smp) {
-  std::lock_guard<std::recursive_mutex> lk(g_mu);
-  DevModel *M = get_model(m);
+// n device-chained steps of model M (the caller holds g_mu).
+int generate_n(DevModel *M, const LlamaKV *kv, int token, int n, int *ids, LlmqSample *smp) {
   if (!M) return 0;
   DevKV *K = get_kv(M, kv);
   if (!K || n < 0 || !check_step_inputs(M, kv, token, n)) return 0;
@@ -1668,20 +2010,56 @@ int generate_n(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *i
 }
 
 int llmqd_decode(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next) {
-  return decode_one(m, kv, token, logits, next, nullptr);
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return decode_one(get_model(m), kv, token, logits, next, nullptr);
 }
 
 int llmqd_decode_sample(const QLlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next,
                         LlmqSample *smp) {
-  return decode_one(m, kv, token, logits, next, smp);
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return decode_one(get_model(m), kv, token, logits, next, smp);
 }
 
 int llmqd_generate(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids) {
-  return generate_n(m, kv, token, n, ids, nullptr);
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return generate_n(get_model(m), kv, token, n, ids, nullptr);
 }
 
 int llmqd_generate_sample(const QLlamaModel *m, const LlamaKV *kv, int token, int n, int *ids, LlmqSample *smp) {
-  return generate_n(m, kv, token, n, ids, smp);
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return generate_n(get_model(m), kv, token, n, ids, smp);
+}
+
+// ---- the fp32 (LLMA) model: the same steps with fp32 products
+int llmqd_model_upload_f32(const LlamaModel *m) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return get_model_f32(m) != nullptr;
+}
+
+void llmqd_model_release_f32(const LlamaModel *m) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!m || !m->blocks) return;
+  auto it = g_models.find(m->blocks);
+  if (it == g_models.end() || !it->second->f32) return;
+  DevModel *M = it->second;
+  g_models.erase(it);
+  release_model(M);
+}
+
+int llmqd_kv_register_f32(const LlamaModel *m, const LlamaKV *kv) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevModel *M = get_model_f32(m);
+  return M && get_kv(M, kv) != nullptr;
+}
+
+int llmqd_decode_f32(const LlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next, LlmqSample *smp) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return decode_one(get_model_f32(m), kv, token, logits, next, smp);
+}
+
+int llmqd_generate_f32(const LlamaModel *m, const LlamaKV *kv, int token, int n, int *ids, LlmqSample *smp) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  return generate_n(get_model_f32(m), kv, token, n, ids, smp);
 }
 
 // One logits row in host memory, sampled on the current device (the

@@ -189,7 +189,7 @@ LLMQ_API void q_llama_model_free(QLlamaModel *m) {
 
 /* Header sanity (llama.c:371-386): positive bounded dims, GQA groups that divide,
  * and 2-D element counts that fit an int. */
-static int config_valid(const int32_t *c) {
+int llmq_config_valid(const int32_t *c) {
   const int32_t maxd = 1000000;
   for (int i = 0; i < 8; i++)
     if (c[i] <= 0 || c[i] > maxd) return 0;
@@ -227,7 +227,7 @@ LLMQ_API int q_llama_model_load(const char *path, QLlamaModel *out) {
     fclose(f);
     return 1;
   }
-  if (!config_valid(cfg)) {
+  if (!llmq_config_valid(cfg)) {
     fprintf(stderr, "Error: '%s' has an invalid/unsupported config\n", path);
     fclose(f);
     return 1;
@@ -432,7 +432,7 @@ LLMQ_API float rng_uniform(Rng *r) {
 
 /* The device form of one sampler call: top_k resolved to the number of
  * candidates it keeps (sampler.c:87-88). */
-static LlmqSample sample_settings(int vocab, float temperature, int top_k, float top_p, const Rng *rng) {
+LlmqSample llmq_sample_settings(int vocab, float temperature, int top_k, float top_p, const Rng *rng) {
   LlmqSample s;
   s.temperature = temperature;
   s.k = (top_k > 0 && top_k < vocab) ? top_k : vocab;
@@ -454,7 +454,7 @@ static const float *logits_row(const Tensor *logits, int row, const char *who) {
 LLMQ_API int sample_argmax(const Tensor *logits, int row) {
   const float *r = logits_row(logits, row, "sample_argmax");
   if (!r) return -1;
-  LlmqSample s = sample_settings(logits->shape[1], 0.0f, 0, 1.0f, NULL);
+  LlmqSample s = llmq_sample_settings(logits->shape[1], 0.0f, 0, 1.0f, NULL);
   int id = -1;
   if (!llmqd_sample_row(r, logits->shape[1], &s, &id)) return -1;
   return id;
@@ -467,7 +467,7 @@ LLMQ_API int sample_token(const Tensor *logits, int row, float temperature, int 
     llmq_set_error(LLMQ_ERR_ARG, "sample_token: rng is NULL");
     return -1;
   }
-  LlmqSample s = sample_settings(logits->shape[1], temperature, top_k, top_p, rng);
+  LlmqSample s = llmq_sample_settings(logits->shape[1], temperature, top_k, top_p, rng);
   int id = -1;
   if (!llmqd_sample_row(r, logits->shape[1], &s, &id)) return -1;
   rng->state = s.rng;
@@ -486,7 +486,7 @@ LLMQ_API int q_llama_decode_step_sample(const QLlamaModel *m, LlamaKV *kv, int t
   if (temperature <= 0.0f) { /* greedy (sampler.c:65-67): the fused argmax, no draw */
     if (!llmqd_decode(m, kv, token, out, &next)) return -1;
   } else {
-    LlmqSample s = sample_settings(m->vocab, temperature, top_k, top_p, rng);
+    LlmqSample s = llmq_sample_settings(m->vocab, temperature, top_k, top_p, rng);
     if (!llmqd_decode_sample(m, kv, token, out, &next, &s)) return -1;
     rng->state = s.rng;
   }
@@ -503,7 +503,7 @@ LLMQ_API int q_llama_generate_sample(const QLlamaModel *m, LlamaKV *kv, int toke
   if (temperature <= 0.0f) {
     if (!llmqd_generate(m, kv, token, n, ids)) return q_llama_last_error();
   } else {
-    LlmqSample s = sample_settings(m->vocab, temperature, top_k, top_p, rng);
+    LlmqSample s = llmq_sample_settings(m->vocab, temperature, top_k, top_p, rng);
     if (!llmqd_generate_sample(m, kv, token, n, ids, &s)) return q_llama_last_error();
     rng->state = s.rng;
   }

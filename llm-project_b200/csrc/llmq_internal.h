@@ -65,6 +65,22 @@ LLMQ_HIDDEN int llmqd_generate_sample(const QLlamaModel *m, const LlamaKV *kv, i
                                       LlmqSample *smp);
 /* One host logits row of V floats sampled on the current device. */
 LLMQ_HIDDEN int llmqd_sample_row(const float *row, int V, LlmqSample *smp, int *id);
+/* The device form of one sampler call: top_k resolved to the number of
+ * candidates it keeps (sampler.c:87-88). */
+LLMQ_HIDDEN LlmqSample llmq_sample_settings(int vocab, float temperature, int top_k, float top_p, const Rng *rng);
+/* LLMA / LLMQ header check (llama.c:371-386). */
+LLMQ_HIDDEN int llmq_config_valid(const int32_t *cfg);
+
+/* ---- fp32 (LLMA) models: the same decode step with fp32 products */
+LLMQ_HIDDEN int llmqd_model_upload_f32(const LlamaModel *m);
+LLMQ_HIDDEN void llmqd_model_release_f32(const LlamaModel *m);
+LLMQ_HIDDEN int llmqd_kv_register_f32(const LlamaModel *m, const LlamaKV *kv);
+/* One step; logits / next / smp may be NULL (smp: draw the next token). */
+LLMQ_HIDDEN int llmqd_decode_f32(const LlamaModel *m, const LlamaKV *kv, int token, float *logits, int *next,
+                                 LlmqSample *smp);
+/* n device-chained steps (greedy, or drawn when smp is set). */
+LLMQ_HIDDEN int llmqd_generate_f32(const LlamaModel *m, const LlamaKV *kv, int token, int n, int *ids,
+                                   LlmqSample *smp);
 /* Size of this process's tensor-parallel group (1 if none). */
 LLMQ_HIDDEN int llmqd_tp_world(void);
 

@@ -41,6 +41,7 @@
 // (sampler.c:65-67 -> sampler.c:8-21) and draws nothing.
 #pragma once
 
+#include "llmq_chain.cuh"
 #include "llmq_kernels.cuh"
 
 namespace llmq {
@@ -54,7 +55,6 @@ constexpr int kSumWindow = kSampleThreads * kSumPer;
 constexpr int kSumHead = 1024;           // leading elements added one by one (from shared memory)
 constexpr int kSumTieCap = 512;          // half-way cases resolved per window
 constexpr int kSampleExpThreads = 512;
-constexpr uint32_t kSat = 1u << 30;      // step counts saturate here (>= 2^24 ends the binade)
 // dynamic shared memory of k_sample: the candidates, then the histogram
 constexpr size_t kSampleSmem = ((size_t)kSampleCandCap * 2 + kSampleBins) * 4;
 
@@ -100,57 +100,6 @@ __device__ __forceinline__ void sample_hist_add(unsigned *hist, uint32_t bin, bo
     const unsigned peers = __match_any_sync(act, bin);
     if ((threadIdx.x & 31) == static_cast<unsigned>(__ffs(peers) - 1)) atomicAdd(&hist[bin], __popc(peers));
   }
-}
-
-// Grid steps of e >= 0 on the grid of spacing 2^uexp: n = floor(e / u),
-// r = e / u rounded to nearest, tie when e / u ends in exactly one half (then
-// r = n).  Counts saturate at kSat.
-struct ChainStep {
-  uint32_t n, r;
-  bool tie;
-};
-__device__ __forceinline__ ChainStep chain_step(uint32_t eb, int uexp) {
-  const uint32_t ef = eb >> 23;
-  const uint32_t me = ef ? ((eb & 0x7fffffu) | 0x800000u) : eb;
-  const int d = (ef ? static_cast<int>(ef) - 150 : -149) - uexp;
-  ChainStep c{0u, 0u, false};
-  if (d >= 0) {
-    const unsigned long long n = d >= 40 ? kSat : (static_cast<unsigned long long>(me) << d);
-    c.n = c.r = n >= kSat ? kSat : static_cast<uint32_t>(n);
-  } else if (d > -32) {
-    const int sh = -d;
-    const uint32_t rem = me & ((1u << sh) - 1u), half = 1u << (sh - 1);
-    c.n = me >> sh;
-    c.r = c.n + (rem > half ? 1u : 0u);
-    c.tie = rem == half;
-  }
-  return c;
-}
-
-// The same from e and 1/u in float, for grids with 2^-100 <= u <= 1: e / u is
-// then exact (a power-of-two scaling) and so are its floor and fraction.
-__device__ __forceinline__ ChainStep chain_step_f(uint32_t eb, float inv_u) {
-  const float t = __fmul_rn(__uint_as_float(eb), inv_u);
-  const float n = floorf(t);
-  const float fr = __fsub_rn(t, n);
-  ChainStep c;
-  c.n = static_cast<uint32_t>(fminf(n, 1073741824.0f));  // kSat
-  c.r = min(c.n + (fr > 0.5f ? 1u : 0u), kSat);
-  c.tie = fr == 0.5f;
-  return c;
-}
-
-__device__ __forceinline__ uint32_t sat_add(uint32_t a, uint32_t b) { return min(a + b, kSat); }
-
-// 2^x as a float, x in [-149, 127]
-__device__ __forceinline__ float pow2f(int x) {
-  return x >= -126 ? __uint_as_float(static_cast<uint32_t>(x + 127) << 23) : __uint_as_float(1u << (x + 149));
-}
-
-__device__ __forceinline__ int warp_min(int v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
 }
 
 // ---------------------------------------------------------------- exp pass
@@ -380,7 +329,7 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(const SampleArgs a) {
     const uint32_t woff = __shfl_sync(0xffffffffu, wr, (warp + 31) & 31);
     const int toff = __shfl_sync(0xffffffffu, wt, (warp + 31) & 31);
     // exclusive prefix of this thread: the previous lane's inclusive one (a
-    // saturated prefix is exact below kSat, and nothing past the first flagged
+    // saturated prefix is exact below kChainSat, and nothing past the first flagged
     // element is used)
     uint32_t ex = __shfl_up_sync(0xffffffffu, ri, 1);
     if (lane == 0) ex = 0u;

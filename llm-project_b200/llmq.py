@@ -105,6 +105,19 @@ SIGNATURES = {
     "q_llama_model_shard": (C.c_int, [C.POINTER(QLlamaModel), C.c_int, C.c_int, C.POINTER(QLlamaModel)]),
     "q_llama_model_upload": (C.c_int, [C.POINTER(QLlamaModel)]),
     "q_llama_generate": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_int, c_int_p]),
+    "llama_kv_create": (LlamaKV, [C.POINTER(LlamaModel)]),
+    "llama_decode_step": (None, [C.POINTER(LlamaModel), C.POINTER(LlamaKV), C.c_int, C.POINTER(Tensor)]),
+    "llama_decode_step_argmax": (C.c_int, [C.POINTER(LlamaModel), C.POINTER(LlamaKV), C.c_int, C.POINTER(Tensor)]),
+    "llama_decode_step_sample": (C.c_int, [C.POINTER(LlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_float, C.c_int,
+                                           C.c_float, C.POINTER(Rng), C.POINTER(Tensor)]),
+    "llama_generate": (C.c_int, [C.POINTER(LlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_int, c_int_p]),
+    "llama_generate_sample": (C.c_int, [C.POINTER(LlamaModel), C.POINTER(LlamaKV), C.c_int, C.c_int, C.c_float,
+                                        C.c_int, C.c_float, C.POINTER(Rng), c_int_p]),
+    "llmq_llama_model_load": (C.c_int, [C.c_char_p, C.POINTER(LlamaModel)]),
+    "llmq_llama_model_free": (None, [C.POINTER(LlamaModel)]),
+    "llmq_llama_model_upload": (C.c_int, [C.POINTER(LlamaModel)]),
+    "llmq_llama_model_release": (None, [C.POINTER(LlamaModel)]),
+    "llmq_synth_model_f32": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_float, C.c_int, C.POINTER(LlamaModel)]),
     "rng_create": (Rng, [C.c_ulonglong]),
     "rng_uniform": (C.c_float, [C.POINTER(Rng)]),
     "sample_argmax": (C.c_int, [C.POINTER(Tensor), C.c_int]),

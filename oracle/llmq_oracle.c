@@ -212,12 +212,47 @@ static void qlinear(const float *x, int K, const QTensor *W, float *out) {
   orc_qmatmul(x, 1, K, W->q, W->scale, W->cols, out);
 }
 
+/* llama.c:554-576 (and llama.c:326-341, the same code in the fp32 step): per
+ * query head, scores over 0..pos, softmax, weighted values; kc / vc hold one
+ * layer's cache rows [pos][n_kv * hd]. */
+static void orc_attend(const float *q, const float *kc, const float *vc, int n_heads, int n_kv, int hd, int pos,
+                       float *sc, float *o) {
+  const int kvd = n_kv * hd, group = n_heads / n_kv;
+  const float att_scale = 1.0f / sqrtf((float)hd);
+  for (int h = 0; h < n_heads; h++) {
+    const int kh = h / group;
+    const float *qh = q + (size_t)h * hd;
+    float mx = -INFINITY;
+    for (int p = 0; p <= pos; p++) {
+      const float *kp = kc + (size_t)p * kvd + (size_t)kh * hd;
+      float dot = 0.0f;
+      for (int d = 0; d < hd; d++) dot += qh[d] * kp[d];
+      const float s = dot * att_scale;
+      sc[p] = s;
+      if (s > mx) mx = s;
+    }
+    float sum = 0.0f;
+    for (int p = 0; p <= pos; p++) {
+      const float e = expf(sc[p] - mx);
+      sc[p] = e;
+      sum += e;
+    }
+    const float inv = 1.0f / sum;
+    float *oh = o + (size_t)h * hd;
+    for (int d = 0; d < hd; d++) oh[d] = 0.0f;
+    for (int p = 0; p <= pos; p++) {
+      const float w = sc[p] * inv;
+      const float *vp = vc + (size_t)p * kvd + (size_t)kh * hd;
+      for (int d = 0; d < hd; d++) oh[d] += w * vp[d];
+    }
+  }
+}
+
 void orc_decode_step(const QLlamaModel *m, LlamaKV *kv, int token, float *logits) {
   /* llama.c:528-600, one token at position kv->len. */
   const int dm = m->d_model, hd = m->head_dim, dff = m->d_ff;
   const int qd = m->n_heads * hd, kvd = m->n_kv * hd;
-  const int pos = kv->len, group = m->n_heads / m->n_kv;
-  const float att_scale = 1.0f / sqrtf((float)hd);
+  const int pos = kv->len;
 
   float *x = (float *)calloc((size_t)dm, sizeof(float));
   float *xn = (float *)calloc((size_t)dm, sizeof(float));
@@ -248,34 +283,7 @@ void orc_decode_step(const QLlamaModel *m, LlamaKV *kv, int token, float *logits
     memcpy(kv->k[l] + (size_t)pos * kvd, k, (size_t)kvd * sizeof(float));
     memcpy(kv->v[l] + (size_t)pos * kvd, v, (size_t)kvd * sizeof(float));
 
-    /* llama.c:554-576: per query head, scores over 0..pos, softmax, weighted V */
-    for (int h = 0; h < m->n_heads; h++) {
-      const int kh = h / group;
-      const float *qh = q + (size_t)h * hd;
-      float mx = -INFINITY;
-      for (int p = 0; p <= pos; p++) {
-        const float *kp = kv->k[l] + (size_t)p * kvd + (size_t)kh * hd;
-        float dot = 0.0f;
-        for (int d = 0; d < hd; d++) dot += qh[d] * kp[d];
-        const float s = dot * att_scale;
-        sc[p] = s;
-        if (s > mx) mx = s;
-      }
-      float sum = 0.0f;
-      for (int p = 0; p <= pos; p++) {
-        const float e = expf(sc[p] - mx);
-        sc[p] = e;
-        sum += e;
-      }
-      const float inv = 1.0f / sum;
-      float *oh = o + (size_t)h * hd;
-      for (int d = 0; d < hd; d++) oh[d] = 0.0f;
-      for (int p = 0; p <= pos; p++) {
-        const float w = sc[p] * inv;
-        const float *vp = kv->v[l] + (size_t)p * kvd + (size_t)kh * hd;
-        for (int d = 0; d < hd; d++) oh[d] += w * vp[d];
-      }
-    }
+    orc_attend(q, kv->k[l], kv->v[l], m->n_heads, m->n_kv, hd, pos, sc, o);  /* llama.c:554-576 */
     /* llama.c:577-578 */
     qlinear(o, qd, &b->Wo, t);
     for (int j = 0; j < dm; j++) x[j] += t[j];
@@ -294,6 +302,92 @@ void orc_decode_step(const QLlamaModel *m, LlamaKV *kv, int token, float *logits
   /* llama.c:592-594 */
   orc_rmsnorm_row(x, m->final_norm.data, dm, m->eps, xn);
   qlinear(xn, dm, &m->lm_head, logits);
+  kv->len = pos + 1;
+
+  free(x); free(xn); free(q); free(k); free(v); free(o); free(t); free(g); free(u); free(sc);
+}
+
+/* ------------------------------------------------------- fp32 (LLMA) step */
+
+/* matrix.c:178-191 for one row: c[j] = 0, then c[j] += a[k] * W[k][j] for
+ * k in order (one rounded product and one rounded sum per term). */
+static void flinear(const float *a, int K, const Tensor *W, float *c) {
+  const int N = W->shape[1];
+  for (int j = 0; j < N; j++) c[j] = 0.0f;
+  for (int k = 0; k < K; k++) {
+    const float ak = a[k];
+    const float *wk = W->data + (size_t)k * N;
+    for (int j = 0; j < N; j++) c[j] += ak * wk[j];
+  }
+}
+
+LlamaKV orc_f32_kv_create(const LlamaModel *m) {
+  /* llama.c:275-288 */
+  LlamaKV kv;
+  kv.n_layers = m->n_layers;
+  kv.max_seq = m->max_seq;
+  kv.kv_dim = m->n_kv * m->head_dim;
+  kv.len = 0;
+  kv.k = (float **)malloc((size_t)m->n_layers * sizeof(float *));
+  kv.v = (float **)malloc((size_t)m->n_layers * sizeof(float *));
+  for (int l = 0; l < m->n_layers; l++) {
+    kv.k[l] = (float *)calloc((size_t)m->max_seq * kv.kv_dim, sizeof(float));
+    kv.v[l] = (float *)calloc((size_t)m->max_seq * kv.kv_dim, sizeof(float));
+  }
+  return kv;
+}
+
+void orc_f32_decode_step(const LlamaModel *m, LlamaKV *kv, int token, float *logits) {
+  /* llama.c:296-362, one token at position kv->len. */
+  const int dm = m->d_model, hd = m->head_dim, dff = m->d_ff;
+  const int qd = m->n_heads * hd, kvd = m->n_kv * hd;
+  const int pos = kv->len;
+  float *x = (float *)calloc((size_t)dm, sizeof(float));
+  float *xn = (float *)calloc((size_t)dm, sizeof(float));
+  float *q = (float *)calloc((size_t)qd, sizeof(float));
+  float *k = (float *)calloc((size_t)kvd, sizeof(float));
+  float *v = (float *)calloc((size_t)kvd, sizeof(float));
+  float *o = (float *)calloc((size_t)qd, sizeof(float));
+  float *t = (float *)calloc((size_t)dm, sizeof(float));
+  float *g = (float *)calloc((size_t)dff, sizeof(float));
+  float *u = (float *)calloc((size_t)dff, sizeof(float));
+  float *sc = (float *)calloc((size_t)pos + 1, sizeof(float));
+
+  for (int j = 0; j < dm; j++) x[j] = m->wte.data[(size_t)token * dm + j]; /* llama.c:302-303 */
+  for (int l = 0; l < m->n_layers; l++) {
+    const LlamaBlock *b = &m->blocks[l];
+    /* llama.c:312-322 */
+    orc_rmsnorm_row(x, b->attn_norm.data, dm, m->eps, xn);
+    flinear(xn, dm, &b->Wq, q);
+    for (int j = 0; j < qd; j++) q[j] = q[j] + b->b_q.data[j];
+    flinear(xn, dm, &b->Wk, k);
+    for (int j = 0; j < kvd; j++) k[j] = k[j] + b->b_k.data[j];
+    flinear(xn, dm, &b->Wv, v);
+    for (int j = 0; j < kvd; j++) v[j] = v[j] + b->b_v.data[j];
+    orc_rope_heads_pos_row(q, m->n_heads, hd, m->rope_base, pos);
+    orc_rope_heads_pos_row(k, m->n_kv, hd, m->rope_base, pos);
+    memcpy(kv->k[l] + (size_t)pos * kvd, k, (size_t)kvd * sizeof(float));
+    memcpy(kv->v[l] + (size_t)pos * kvd, v, (size_t)kvd * sizeof(float));
+    orc_attend(q, kv->k[l], kv->v[l], m->n_heads, m->n_kv, hd, pos, sc, o); /* llama.c:324-341 */
+    /* llama.c:342-343 */
+    flinear(o, qd, &b->Wo, t);
+    for (int j = 0; j < dm; j++) x[j] += t[j];
+    /* llama.c:346-348 over swiglu.c:33-43 */
+    orc_rmsnorm_row(x, b->ffn_norm.data, dm, m->eps, xn);
+    flinear(xn, dm, &b->Wgate, g);
+    flinear(xn, dm, &b->Wup, u);
+    for (int j = 0; j < dff; j++) {
+      const float z = g[j];
+      const float s = 1.0f / (1.0f + expf(-z)); /* swiglu.c:9-12 */
+      const float a = z * s;
+      g[j] = a * u[j];
+    }
+    flinear(g, dff, &b->Wdown, t);
+    for (int j = 0; j < dm; j++) x[j] += t[j];
+  }
+  /* llama.c:351-353 */
+  orc_rmsnorm_row(x, m->final_norm.data, dm, m->eps, xn);
+  flinear(xn, dm, &m->lm_head, logits);
   kv->len = pos + 1;
 
   free(x); free(xn); free(q); free(k); free(v); free(o); free(t); free(g); free(u); free(sc);

@@ -49,6 +49,10 @@ void orc_kv_free(LlamaKV *kv);
 /* llama.c:528-600: one decode step; logits has m->vocab floats. */
 void orc_decode_step(const QLlamaModel *m, LlamaKV *kv, int token, float *logits);
 
+/* llama.c:275-288 / 296-362: the fp32 (LLMA) model's cache and decode step. */
+LlamaKV orc_f32_kv_create(const LlamaModel *m);
+void orc_f32_decode_step(const LlamaModel *m, LlamaKV *kv, int token, float *logits);
+
 /* llama.c:603-657: LLMQ v2 reader (0 ok, 1 error). */
 int orc_model_load(const char *path, QLlamaModel *out);
 void orc_model_free(QLlamaModel *m);

@@ -64,6 +64,8 @@ _ORC_SIGS = {
     "orc_kv_create": (LlamaKV, [C.POINTER(QLlamaModel)]),
     "orc_kv_free": (None, [C.POINTER(LlamaKV)]),
     "orc_decode_step": (None, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, c_float_p]),
+    "orc_f32_kv_create": (LlamaKV, [C.POINTER(LlamaModel)]),
+    "orc_f32_decode_step": (None, [C.POINTER(LlamaModel), C.POINTER(LlamaKV), C.c_int, c_float_p]),
     "orc_model_load": (C.c_int, [C.c_char_p, C.POINTER(QLlamaModel)]),
     "orc_model_free": (None, [C.POINTER(QLlamaModel)]),
     "orc_model_save": (C.c_int, [C.c_char_p, C.POINTER(QLlamaModel)]),
@@ -86,6 +88,9 @@ _REF_SIGS = {
     "llama_model_randomize": (None, [C.POINTER(LlamaModel)]),
     "llama_model_forward": (None, [C.POINTER(LlamaModel), c_int_p, C.c_int, C.POINTER(Tensor)]),
     "llama_model_free": (None, [C.POINTER(LlamaModel)]),
+    "llama_kv_create": (LlamaKV, [C.POINTER(LlamaModel)]),
+    "llama_decode_step": (None, [C.POINTER(LlamaModel), C.POINTER(LlamaKV), C.c_int, C.POINTER(Tensor)]),
+    "llama_model_load": (C.c_int, [C.c_char_p, C.POINTER(LlamaModel)]),
     "sample_argmax": (C.c_int, [C.POINTER(Tensor), C.c_int]),
     "rng_create": (Rng, [C.c_ulonglong]),
     "rng_uniform": (C.c_float, [C.POINTER(Rng)]),
