@@ -63,6 +63,10 @@ WORKLOADS = {
                      fast=True,
                      name="llama3-70b-shaped int8 W8A8, batch 32, tensor-parallel over all GPUs: 1024-id prompts "
                           "prefilled, then batched greedy decode"),
+    "8b-f32": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=32, n_heads=32, n_kv=8, head_dim=128, d_ff=14336,
+                            rope_base=500000.0, eps=1e-5), prompt=64, gen=128, f32=True,
+                   name="llama3-8b-shaped fp32 (LLMA path: the int8 synthetic model dequantised, as "
+                        "llama_model_load reads an LLMQ file), batch 1: 64-id prompt then greedy decode"),
     "tiny": dict(cfg=dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768,
                           rope_base=10000.0, eps=1e-5), prompt=16, gen=240,
                  name="tiny llama int8 W8A8, batch 1: 16-id prompt then greedy decode"),
@@ -308,6 +312,112 @@ def run_ours(args, rank, world):
     lib.q_llama_model_free(C.byref(m))
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def run_f32(args, rank, world):
+    """The fp32 (LLMA) path: llama_decode_step on a dequantised 8B-shaped model.
+    A step is one token; value from K device-chained steps (llama_generate),
+    e2e through llama_decode_step with the logits row copied to the host."""
+    lib = llmq.load()
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if lib.q_llama_set_device(local) != 0:
+        raise RuntimeError(lib.q_llama_last_error_message().decode())
+    wl = WORKLOADS[args.workload]
+    cfg = wl["cfg"]
+    P, W, K = args.prompt or wl["prompt"], args.warmup, args.steps
+    c = llmq.config(max_seq=P + W + 2 * K + 8, **cfg)
+    m = llmq.LlamaModel()
+    t0 = time.time()
+    if lib.llmq_synth_model_f32(C.byref(c), SEED_WEIGHTS, 0.02, 0, C.byref(m)) != 0:
+        llmq.check(lib)
+    log(f"fp32 synthetic model built in {time.time() - t0:.1f}s")
+    t0 = time.time()
+    if lib.llmq_llama_model_upload(C.byref(m)) != 0:
+        llmq.check(lib)
+    log(f"uploaded in {time.time() - t0:.1f}s")
+    kv = lib.llama_kv_create(C.byref(m))
+    llmq.check(lib)
+    nxt = -1
+    for t in prompt_ids(cfg, P):
+        nxt = lib.llama_decode_step_argmax(C.byref(m), C.byref(kv), int(t), None)
+    llmq.check(lib)
+    ids = (C.c_int * max(W, K))()
+    if lib.llama_generate(C.byref(m), C.byref(kv), nxt, W, ids) != 0:
+        llmq.check(lib)
+    start_len, start_tok = kv.len, ids[W - 1]
+    with ClockSampler(local) as clk:
+        if lib.llama_generate(C.byref(m), C.byref(kv), start_tok, K, ids) != 0:
+            llmq.check(lib)
+        ms = float(lib.q_llama_last_step_ms())
+    gen_ids = [ids[i] for i in range(K)]
+    value = world * K / (ms / 1e3)
+    kv.len = start_len
+    logits = np.zeros((1, cfg["vocab"]), np.float32)
+    lt = llmq.host_tensor(logits)
+    tok, e2e_ids = start_tok, []
+    t0 = time.perf_counter()
+    for _ in range(K):
+        lib.llama_decode_step(C.byref(m), C.byref(kv), tok, C.byref(lt))
+        tok = int(np.argmax(logits[0]))
+        e2e_ids.append(tok)
+    e2e_s = time.perf_counter() - t0
+    llmq.check(lib)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except OSError:
+        pass
+    hbm_peak = float(peaks.get("hbm_gbs", 6650.0))
+    step_bytes = 4 * weight_bytes(cfg)
+    achieved = step_bytes / (ms / K / 1e3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = f32_cpu_baseline(m, cfg)
+    line = {
+        "metric": "fp32-weight decode tok/s (bs1)", "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": wl["name"], "kv_len_start": start_len, "kv_len_end": start_len + K, "prompt": P,
+                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                   "l2": f"inputs larger than L2: {step_bytes / 1e9:.1f} GB of fp32 weights streamed per step"},
+        "e2e": {"value": round(world * K / e2e_s, 2), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                "d2h_bytes_per_step": 16 + 4 * cfg["vocab"], "api": "llama_decode_step (host logits, host argmax)",
+                "same_tokens_as_value_run": e2e_ids == gen_ids},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "traffic": None,
+                     "kernel": "whole step: fp32 weight bytes per step / step time (k_gemv_f32 dominates)",
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s"},
+        "cpu_baseline": cpu,
+        "gpu_launches": K * (6 * cfg["n_layers"] + 2),  # per step: 6 per layer, lm-head, finish
+        "clocks": clk.summary(),
+    }
+    lib.llama_kv_free(C.byref(kv))
+    lib.llmq_llama_model_free(C.byref(m))
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def f32_cpu_baseline(m, cfg):
+    """The reference's own llama_decode_step (oracle/_ref) on the same fp32
+    model, from an empty cache, for about 10 s on the host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    ref = oracle.load_reference()
+    if ref is None:
+        return None
+    kv = ref.llama_kv_create(C.byref(m))
+    row = np.zeros((1, cfg["vocab"]), np.float32)
+    t = llmq.host_tensor(row)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < 10.0 and n < 64:
+        ref.llama_decode_step(C.byref(m), C.byref(kv), int(n * 7 % cfg["vocab"]), C.byref(t))
+        n += 1
+    dt = time.perf_counter() - t0
+    ref.llama_kv_free(C.byref(kv))
+    # matrix.c's matmul threads over output rows (parallel_for(M)); a decode
+    # step has one row, so the reference runs it on one core
+    return {"value": round(n / dt, 4), "unit": "tok/s", "cores": 1, "kind": "reference",
+            "sample": f"{n} fp32 decode steps of the same model at positions 0..{n - 1}"}
 
 
 def run_serve(args, rank, world):
@@ -768,6 +878,8 @@ def main():
             run_serve(args, rank, world)
         elif WORKLOADS[args.workload].get("tp"):
             run_tp(args, rank, world)
+        elif WORKLOADS[args.workload].get("f32"):
+            run_f32(args, rank, world)
         else:
             run_ours(args, rank, world)
     finally:

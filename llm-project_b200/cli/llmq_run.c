@@ -11,11 +11,15 @@
  * "gen: <prompt ids> <sampled ids>" (main.c:569-574).  Tools that spawn the
  * reference binary (tools/llama_stream.py:61-65) read the same lines.
  *
- * The prompt goes through q_llama_prefill in one pass (its logits equal those
- * of the token-by-token loop); the first id is drawn by sample_token from
- * those logits, every later one by q_llama_decode_step_sample inside the step
- * graph.  The ids equal the reference CLI's.  LLMA (f32) checkpoints are not
- * on the device path and are refused. */
+ * LLMQ (int8) checkpoints: the prompt goes through q_llama_prefill in one
+ * pass (its logits equal those of the token-by-token loop); the first id is
+ * drawn by sample_token from those logits, every later one by
+ * q_llama_decode_step_sample inside the step graph.  LLMA (f32) checkpoints
+ * run the fp32 path: the prompt token by token through
+ * llama_decode_step_argmax, the last step's logits sampled, then
+ * llama_decode_step_sample.  The ids equal the reference CLI's.  The LLMA
+ * text mode (a tokenizer as 4th argument, main.c:584-622) needs the
+ * reference's tokenizer and is not provided. */
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -55,10 +59,57 @@ static int fail(const char *what) {
   return 1;
 }
 
+/* The LLMA branch of main.c:675-700 on the fp32 GPU path. */
+static int run_llama_f32(const char *path, int n_new) {
+  const float temperature = 0.8f;
+  const int top_k = 40;
+  const float top_p = 0.95f;
+  Rng rng = rng_create(1234);
+  LlamaModel m;
+  if (llmq_llama_model_load(path, &m) != 0) return 1;
+  fprintf(stderr, "loaded LLMA (f32): vocab %d d_model %d layers %d heads %d kv %d head_dim %d d_ff %d\n", m.vocab,
+          m.d_model, m.n_layers, m.n_heads, m.n_kv, m.head_dim, m.d_ff);
+  LlamaKV kv = llama_kv_create(&m);
+  if (q_llama_last_error()) {
+    llmq_llama_model_free(&m);
+    return fail("llama_kv_create");
+  }
+  float *row = (float *)malloc((size_t)m.vocab * sizeof(float));
+  int shape[2] = {1, m.vocab};
+  Tensor logits = {row, NULL, shape, 2, (size_t)m.vocab};
+  int *seq = (int *)malloc((size_t)m.max_seq * sizeof(int));
+  static char line[8192];
+  int rc = 0;
+  while (rc == 0 && fgets(line, sizeof line, stdin)) {
+    int n = parse_ids(line, seq, m.vocab, m.max_seq);
+    if (n == 0) continue;
+    kv.len = 0;
+    for (int i = 0; i < n && rc == 0; i++)
+      if (llama_decode_step_argmax(&m, &kv, seq[i], i == n - 1 ? &logits : NULL) < 0) rc = fail("llama_decode_step");
+    for (int s = 0; s < n_new && n < m.max_seq && rc == 0; s++) {
+      const int nxt = s == 0 ? sample_token(&logits, 0, temperature, top_k, top_p, &rng)
+                             : llama_decode_step_sample(&m, &kv, seq[n - 1], temperature, top_k, top_p, &rng, NULL);
+      if (nxt < 0) {
+        rc = fail("sampling");
+        break;
+      }
+      seq[n++] = nxt;
+      printf("t %d\n", nxt);
+      fflush(stdout);
+    }
+    if (rc == 0) print_gen(seq, n);
+  }
+  free(seq);
+  free(row);
+  llama_kv_free(&kv);
+  llmq_llama_model_free(&m);
+  return rc;
+}
+
 static int run_llama(int argc, char **argv) {
   if (argc < 3) {
     fprintf(stderr, "usage: llmq_run llama <checkpoint.bin> [n_new=40]\n"
-                    "  LLMQ (int8) checkpoint, decoded on the GPU;\n"
+                    "  LLMA (f32) or LLMQ (int8) checkpoint, decoded on the GPU;\n"
                     "  reads space-separated token IDs per stdin line; prints 't <id>' per\n"
                     "  sampled token, then 'gen: <ids>'\n");
     return 2;
@@ -76,10 +127,16 @@ static int run_llama(int argc, char **argv) {
     return 1;
   }
   fclose(pf);
-  if (magic != LLMQ_MAGIC) {
-    fprintf(stderr, "Error: '%s' is %s; only LLMQ (int8) checkpoints run on the GPU path\n", argv[2],
-            magic == LLMA_MAGIC ? "an LLMA (f32) checkpoint" : "not an LLMQ checkpoint");
+  if (magic != LLMQ_MAGIC && magic != LLMA_MAGIC) {
+    fprintf(stderr, "Error: '%s' is not an LLMA/LLMQ checkpoint\n", argv[2]);
     return 1;
+  }
+  if (magic == LLMA_MAGIC) {
+    if (argc > 4) {
+      fprintf(stderr, "Error: text mode (a tokenizer argument) is not provided; pass token ids\n");
+      return 2;
+    }
+    return run_llama_f32(argv[2], n_new);
   }
 
   const float temperature = 0.8f;

@@ -107,20 +107,18 @@ void free_mat(Mat &m) {
   m = Mat{};
 }
 
-// An fp32 matrix of the LLMA path, stored as one region per CTA (see
-// llmq_f32.cuh) for a grid of `grid` CTAs.
+// An fp32 matrix of the LLMA path: tiles of 32 columns, each a contiguous
+// [K][32] block (llmq_f32.cuh), split over a grid of `grid` CTAs.
 struct MatF {
   float *w = nullptr;
-  long long *cta_off = nullptr;
-  int *cta_u0 = nullptr;
-  int K = 0, N = 0, grid = 0, threads = 0, KC = 0, stages = 0, stage_floats = 0;
+  int *cta_t0 = nullptr;
+  int K = 0, N = 0, grid = 0, threads = 0, rows = 0, slots = 0;
   size_t smem = 0;
 };
 
 void free_matf(MatF &m) {
   cudaFree(m.w);
-  cudaFree(m.cta_off);
-  cudaFree(m.cta_u0);
+  cudaFree(m.cta_t0);
   m = MatF{};
 }
 
@@ -205,6 +203,13 @@ cudaError_t set_gemv_attr(int smem) {
   return set_attr(k_gemv<PRO, EPI, MR, 128>, smem);
 }
 
+template <int PRO, int EPI>
+cudaError_t set_f32_attr(int smem) {
+  cudaError_t e = set_attr(k_gemv_f32<PRO, EPI, 256>, smem);
+  if (e != cudaSuccess) return e;
+  return set_attr(k_gemv_f32<PRO, EPI, kF32MaxThreads>, smem);
+}
+
 int init_expf_table(DevCtx &c) {
   const uint32_t n = llmq_expf_exceptions_count;
   uint32_t cap = 1;
@@ -280,12 +285,11 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_attr(k_sample_exp, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_sample_max, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_sample, static_cast<int>(kSampleSmem));
-  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_PLAIN, F32_EPI_RESID>, sm);
-  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_SWIGLU, F32_EPI_RESID>, sm);
-  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_RMSNORM, F32_EPI_QKV>, sm);
-  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_EMBED_RMSNORM, F32_EPI_QKV>, sm);
-  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_RMSNORM, F32_EPI_PLAIN>, sm);
-  ea = ea != cudaSuccess ? ea : set_attr(k_gemv_f32<F32_PRO_RMSNORM, F32_EPI_LOGITS>, sm);
+  ea = ea != cudaSuccess ? ea : set_f32_attr<F32_PRO_PLAIN, F32_EPI_RESID>(sm);
+  ea = ea != cudaSuccess ? ea : set_f32_attr<F32_PRO_RMSNORM, F32_EPI_QKV>(sm);
+  ea = ea != cudaSuccess ? ea : set_f32_attr<F32_PRO_EMBED_RMSNORM, F32_EPI_QKV>(sm);
+  ea = ea != cudaSuccess ? ea : set_f32_attr<F32_PRO_RMSNORM, F32_EPI_SWIGLU>(sm);
+  ea = ea != cudaSuccess ? ea : set_f32_attr<F32_PRO_RMSNORM, F32_EPI_LOGITS>(sm);
   if (ea != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
     return nullptr;
@@ -618,7 +622,6 @@ struct DevModel {
   std::vector<MatF> fqkv, fwo, fw13, fw2;
   MatF flm;
   float *wte_f = nullptr;  // [vocab][d_model]
-  float *gu = nullptr;     // [2 * d_ff]: gate then up of the current step
   std::vector<float *> attn_norm, ffn_norm, bias_qkv;
   float *final_norm = nullptr;
   int8_t *wte_q = nullptr;
@@ -701,7 +704,6 @@ void release_model(DevModel *M) {
     for (MatF &m : *v) free_matf(m);
   free_matf(M->flm);
   cudaFree(M->wte_f);
-  cudaFree(M->gu);
   for (auto *v : {&M->attn_norm, &M->ffn_norm, &M->bias_qkv})
     for (float *p : *v) cudaFree(p);
   for (int q = 0; q < (int)M->tpx_peer.size(); ++q)
@@ -943,86 +945,102 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
 }
 
 // ------------------------------------------------------------ fp32 models
-// Lays out the columns of up to three row-major [K][n_i] matrices, side by
-// side, as one region per CTA of a `grid`-CTA launch, and plans the launch.
-int build_matf(DevCtx &c, MatF &out, int K, const float *const src[3], const int ns[3], int grid) {
-  int N = 0;
-  for (int i = 0; i < 3; ++i) N += src[i] ? ns[i] : 0;
-  const int U = (N + kF32Unit - 1) / kF32Unit;
-  std::vector<int> u0(grid + 1);
-  std::vector<long long> off(grid + 1);
-  int nu_max = 0;
+// Lays out the N columns of a fused matrix as 32-column tiles, each a
+// contiguous [K][32] block; fused column p is column colsrc[p] & 0xffffff of
+// source colsrc[p] >> 24 (row-major [K][ns[src]]), or zero when colsrc[p] < 0.
+// Splits the tiles over `grid` CTAs and plans the per-warp rings.
+int build_matf(DevCtx &c, MatF &out, int K, const std::vector<int> &colsrc, const float *const src[3],
+               const int ns[3], int grid) {
+  const int N = static_cast<int>(colsrc.size());
+  const int T = (N + kF32Tile - 1) / kF32Tile;
+  std::vector<int> t0(grid + 1);
+  int per_cta = 0;
   for (int g = 0; g <= grid; ++g) {
-    u0[g] = static_cast<int>((long long)g * U / grid);
-    off[g] = (long long)K * kF32Unit * u0[g];
-    if (g > 0) nu_max = std::max(nu_max, u0[g] - u0[g - 1]);
+    t0[g] = static_cast<int>((long long)g * T / grid);
+    if (g > 0) per_cta = std::max(per_cta, t0[g] - t0[g - 1]);
   }
-  const int threads = std::max(32, roundup(nu_max * kF32Unit, 32));
+  const int threads = std::max(1, per_cta) * kF32Tile;
   if (threads > kF32MaxThreads) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 product with %d columns is wider than this build handles", N);
     return 0;
   }
-  std::vector<float> buf((size_t)K * U * kF32Unit, 0.0f);
-  auto fill = [&](int g0, int g1) {
-    for (int g = g0; g < g1; ++g) {
-      const int c0 = u0[g] * kF32Unit, nc = (u0[g + 1] - u0[g]) * kF32Unit;
-      for (int k = 0; k < K; ++k) {
-        float *dst = buf.data() + off[g] + (size_t)k * nc;
-        int base = 0;
-        for (int i = 0; i < 3; ++i) {
-          if (!src[i]) continue;
-          const int lo = std::max(c0, base), hi = std::min(c0 + nc, base + ns[i]);
-          if (lo < hi) std::memcpy(dst + (lo - c0), src[i] + (size_t)k * ns[i] + (lo - base), (size_t)(hi - lo) * 4);
-          base += ns[i];
-        }
+  std::vector<float> buf((size_t)T * K * kF32Tile, 0.0f);
+  auto fill = [&](int ta, int tb) {
+    for (int t = ta; t < tb; ++t) {
+      float *blk = buf.data() + (size_t)t * K * kF32Tile;
+      // a tile whose 32 columns are consecutive columns of one source is copied row by row
+      const int p0 = t * kF32Tile;
+      bool run = p0 + kF32Tile <= N && colsrc[p0] >= 0;
+      for (int q = 1; run && q < kF32Tile; ++q) run = colsrc[p0 + q] == colsrc[p0] + q;
+      if (run) {
+        const int sidx = colsrc[p0] >> 24, col = colsrc[p0] & 0xffffff;
+        for (int k = 0; k < K; ++k)
+          std::memcpy(blk + (size_t)k * kF32Tile, src[sidx] + (size_t)k * ns[sidx] + col, kF32Tile * sizeof(float));
+        continue;
+      }
+      for (int q = 0; q < kF32Tile && p0 + q < N; ++q) {
+        const int cs = colsrc[p0 + q];
+        if (cs < 0) continue;
+        const float *sp = src[cs >> 24] + (cs & 0xffffff);
+        const int ld = ns[cs >> 24];
+        for (int k = 0; k < K; ++k) blk[(size_t)k * kF32Tile + q] = sp[(size_t)k * ld];
       }
     }
   };
   {
     const int nt = std::max(1, std::min(32, static_cast<int>(std::thread::hardware_concurrency())));
     std::vector<std::thread> pool;
-    for (int t = 0; t < nt; ++t) pool.emplace_back(fill, t * grid / nt, (t + 1) * grid / nt);
+    for (int t = 0; t < nt; ++t) pool.emplace_back(fill, (int)((long long)t * T / nt), (int)((long long)(t + 1) * T / nt));
     for (auto &th : pool) th.join();
   }
-  if (!dev_upload(&out.w, buf.data(), buf.size()) || !dev_upload(&out.cta_off, off.data(), off.size()) ||
-      !dev_upload(&out.cta_u0, u0.data(), u0.size()))
-    return 0;
+  if (!dev_upload(&out.w, buf.data(), buf.size()) || !dev_upload(&out.cta_t0, t0.data(), t0.size())) return 0;
   out.K = K;
   out.N = N;
   out.grid = grid;
   out.threads = threads;
-  // ring slots of about 24 KB, as many as fit beside the input row (and its squares)
-  const size_t xs_bytes = (2 * (size_t)roundup(K, 4) + 8) * sizeof(float);
-  int KC = std::max(4, std::min(256, 24576 / (nu_max * kF32Unit * 4))) & ~3;
-  for (;;) {
-    const size_t slot = (size_t)KC * nu_max * kF32Unit * 4;
-    const long long room = (long long)c.max_smem - 1024 - (long long)xs_bytes;
-    const int S = room > 0 ? static_cast<int>(std::min<long long>(kF32MaxStages, room / (long long)slot)) : 0;
-    if (S >= 2 || KC == 4) {
-      if (S < 2) {
-        llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 product (K %d) does not fit in shared memory", K);
-        return 0;
-      }
-      out.KC = KC;
-      out.stages = S;
-      out.stage_floats = KC * nu_max * kF32Unit;
-      out.smem = (size_t)S * slot + xs_bytes;
-      return 1;
-    }
-    KC = std::max(4, (KC / 2) & ~3);
+  // each warp's share of shared memory beside the input row (and its squares):
+  // slots of up to 16 KB (128 rows), as many as fit, at most 8
+  const int nw = threads / kF32Tile;
+  const long long xs_bytes = (2LL * roundup(K, 4) + 8) * 4;
+  const long long per_warp = ((long long)c.max_smem - 1024 - xs_bytes) / nw - 2 * kF32MaxSlots * 8;
+  int rows = static_cast<int>(std::min<long long>(128, per_warp / 4 / (kF32Tile * 4))) & ~7;
+  if (rows < 8) rows = 8;
+  const int slots = static_cast<int>(std::min<long long>(kF32MaxSlots, per_warp / ((long long)rows * kF32Tile * 4)));
+  if (slots < 2) {
+    llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 product (K %d, %d columns) does not fit in shared memory", K, N);
+    return 0;
   }
+  out.rows = rows;
+  out.slots = slots;
+  out.smem = (size_t)nw * slots * rows * kF32Tile * 4 + (((size_t)nw * slots + 1) & ~size_t(1)) * 8 + (size_t)xs_bytes;
+  return 1;
+}
+
+// Column maps: sources side by side, or gate / up interleaved in fours.
+std::vector<int> cols_concat(const int ns[3]) {
+  std::vector<int> cs;
+  for (int i = 0; i < 3; ++i)
+    for (int j = 0; j < ns[i]; ++j) cs.push_back((i << 24) | j);
+  return cs;
+}
+std::vector<int> cols_interleave4(int n) {
+  std::vector<int> cs((size_t)8 * ((n + 3) / 4), -1);
+  for (size_t p = 0; p < cs.size(); ++p) {
+    const int g = static_cast<int>(p / 8), w = static_cast<int>(p % 8);
+    const int j = g * 4 + (w & 3);
+    if (j < n) cs[p] = ((w < 4 ? 0 : 1) << 24) | j;
+  }
+  return cs;
 }
 
 template <int PRO, int EPI>
 cudaError_t launch_f32(const MatF &m, F32Args a, cudaStream_t st, bool pdl = true) {
   a.w = m.w;
-  a.cta_off = m.cta_off;
-  a.cta_u0 = m.cta_u0;
+  a.cta_t0 = m.cta_t0;
   a.K = m.K;
   a.N = m.N;
-  a.KC = m.KC;
-  a.stages = m.stages;
-  a.stage_floats = m.stage_floats;
+  a.rows = m.rows;
+  a.slots = m.slots;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(m.grid);
   cfg.blockDim = dim3(m.threads);
@@ -1034,7 +1052,8 @@ cudaError_t launch_f32(const MatF &m, F32Args a, cudaStream_t st, bool pdl = tru
   cfg.attrs = attr;
   cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
   ++g_launches;
-  return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI>, a);
+  if (m.threads <= 256) return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI, 256>, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI, kF32MaxThreads>, a);
 }
 
 int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
@@ -1083,7 +1102,7 @@ int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
       const float *src[3] = {b.Wq.data, b.Wk.data, b.Wv.data};
       const int ns[3] = {qd, kvd, kvd};
       M->fqkv.emplace_back();
-      if (!build_matf(c, M->fqkv.back(), dm, src, ns, grid)) return 0;
+      if (!build_matf(c, M->fqkv.back(), dm, cols_concat(ns), src, ns, grid)) return 0;
       std::vector<float> bias((size_t)qd + 2 * kvd, 0.0f);  // llama.c:316-318 (absent biases are zero)
       if (b.b_q.data) std::memcpy(bias.data(), b.b_q.data, qd * sizeof(float));
       if (b.b_k.data) std::memcpy(bias.data() + qd, b.b_k.data, kvd * sizeof(float));
@@ -1096,19 +1115,19 @@ int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
       const float *src[3] = {b.Wo.data, nullptr, nullptr};
       const int ns[3] = {dm, 0, 0};
       M->fwo.emplace_back();
-      if (!build_matf(c, M->fwo.back(), qd, src, ns, grid)) return 0;
+      if (!build_matf(c, M->fwo.back(), qd, cols_concat(ns), src, ns, grid)) return 0;
     }
     {
       const float *src[3] = {b.Wgate.data, b.Wup.data, nullptr};
       const int ns[3] = {dff, dff, 0};
       M->fw13.emplace_back();
-      if (!build_matf(c, M->fw13.back(), dm, src, ns, grid)) return 0;
+      if (!build_matf(c, M->fw13.back(), dm, cols_interleave4(dff), src, ns, grid)) return 0;
     }
     {
       const float *src[3] = {b.Wdown.data, nullptr, nullptr};
       const int ns[3] = {dm, 0, 0};
       M->fw2.emplace_back();
-      if (!build_matf(c, M->fw2.back(), dff, src, ns, grid)) return 0;
+      if (!build_matf(c, M->fw2.back(), dff, cols_concat(ns), src, ns, grid)) return 0;
     }
     float *an = nullptr, *fn = nullptr;
     if (!dev_upload(&an, b.attn_norm.data, dm) || !dev_upload(&fn, b.ffn_norm.data, dm)) return 0;
@@ -1122,7 +1141,7 @@ int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
   {
     const float *src[3] = {m->lm_head.data, nullptr, nullptr};
     const int ns[3] = {cfg.vocab, 0, 0};
-    if (!build_matf(c, M->flm, dm, src, ns, grid)) return 0;
+    if (!build_matf(c, M->flm, dm, cols_concat(ns), src, ns, grid)) return 0;
   }
   if (!dev_upload(&M->final_norm, m->final_norm.data, dm)) return 0;
   if (!dev_upload(&M->wte_f, m->wte.data, (size_t)cfg.vocab * dm)) return 0;
@@ -1146,7 +1165,7 @@ int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
     return 0;
   }
   if (!dev_zeros(&M->scores, (size_t)cfg.n_heads * cfg.max_seq) || !dev_zeros(&M->x, dm) ||
-      !dev_zeros(&M->q, (size_t)qd + kvd) || !dev_zeros(&M->o, qd) || !dev_zeros(&M->gu, 2 * (size_t)dff) ||
+      !dev_zeros(&M->q, (size_t)qd + kvd) || !dev_zeros(&M->o, qd) || !dev_zeros(&M->h, dff) ||
       !dev_zeros(&M->logits, cfg.vocab) || !dev_zeros(&M->err, 4) || !dev_zeros(&M->result, 4) ||
       !dev_zeros(&M->tokens, cfg.max_seq) || !dev_zeros(&M->argmax, 1) || !dev_zeros(&M->step, 1) ||
       !dev_zeros(&M->sample, 1) || !dev_zeros(&M->sample_e, M->vocab_full) ||
@@ -1429,8 +1448,9 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       F32Args a = f32_args();
       a.in = M->x;
       a.gamma = M->ffn_norm[l];
-      a.out = M->gu;
-      CK((launch_f32<F32_PRO_RMSNORM, F32_EPI_PLAIN>(M->fw13[l], a, st)));
+      a.out = M->h;
+      a.n_out = cfg.d_ff;
+      CK((launch_f32<F32_PRO_RMSNORM, F32_EPI_SWIGLU>(M->fw13[l], a, st)));
       PROF_MARK();
     } else {
       GemvArgs a = base_args(M->w13[l], M->p_w13, M->acc, M->cnt, M->err);
@@ -1443,10 +1463,9 @@ int record_step(DevModel *M, DevKV *K, int mode) {
     }
     if (M->f32) {
       F32Args a = f32_args();
-      a.in = M->gu;
-      a.dff = cfg.d_ff;
+      a.in = M->h;
       a.out = M->x;
-      CK((launch_f32<F32_PRO_SWIGLU, F32_EPI_RESID>(M->fw2[l], a, st)));
+      CK((launch_f32<F32_PRO_PLAIN, F32_EPI_RESID>(M->fw2[l], a, st)));
       PROF_MARK();
     } else if (M->tp_world > 1) {
       if (!row_parallel(M, M->w2[l], M->p_w2, M->h, 2 * l + 1, st)) return 0;

@@ -19,11 +19,17 @@ CLI = os.path.join(ROOT, "llm-project_b200", "bin", "llmq_run")
 MODEL = os.path.join(GOLDEN, "mini.llmq")
 
 
-def reference_protocol(orc, lines, n_new):
-    """main.c:650-671 over the oracle: returns the stdout lines."""
+def reference_protocol(orc, lines, n_new, f32_model=None):
+    """main.c:650-671 (or, for an fp32 model, main.c:685-697) over the
+    oracle: returns the stdout lines."""
     import llmq
-    m = llmq.QLlamaModel()
-    assert orc.orc_model_load(MODEL.encode(), C.byref(m)) == 0
+    if f32_model is None:
+        m = llmq.QLlamaModel()
+        assert orc.orc_model_load(MODEL.encode(), C.byref(m)) == 0
+        kv_create, step = orc.orc_kv_create, orc.orc_decode_step
+    else:
+        m = f32_model
+        kv_create, step = orc.orc_f32_kv_create, orc.orc_f32_decode_step
     state = 0x4D2  # rng_create(1234)
     out = []
     row = np.zeros(m.vocab, np.float32)
@@ -38,9 +44,9 @@ def reference_protocol(orc, lines, n_new):
                 seq.append(int(t))
         if not seq:
             continue
-        kv = orc.orc_kv_create(C.byref(m))
+        kv = kv_create(C.byref(m))
         for t in seq:
-            orc.orc_decode_step(C.byref(m), C.byref(kv), t, fp(row))
+            step(C.byref(m), C.byref(kv), t, fp(row))
         n = len(seq)
         for _ in range(n_new):
             if n >= m.max_seq:
@@ -49,10 +55,11 @@ def reference_protocol(orc, lines, n_new):
             seq.append(nxt)
             n += 1
             out.append(f"t {nxt}")
-            orc.orc_decode_step(C.byref(m), C.byref(kv), nxt, fp(row))
+            step(C.byref(m), C.byref(kv), nxt, fp(row))
         out.append("gen: " + " ".join(str(i) for i in seq))
         orc.orc_kv_free(C.byref(kv))
-    orc.orc_model_free(C.byref(m))
+    if f32_model is None:
+        orc.orc_model_free(C.byref(m))
     return out
 
 
@@ -65,10 +72,14 @@ def test_cli_usage_and_bad_checkpoint(tmp_path):
     assert r.returncode == 2 and "usage" in r.stderr
     r = subprocess.run([CLI, "llama"], capture_output=True, text=True)
     assert r.returncode == 2
-    bad = tmp_path / "f32.bin"
-    bad.write_bytes(b"LLMA" + b"\0" * 60)
+    bad = tmp_path / "bad.bin"
+    bad.write_bytes(b"XXXX" + b"\0" * 60)
     r = subprocess.run([CLI, "llama", str(bad)], capture_output=True, text=True, input="1 2\n")
-    assert r.returncode == 1 and "LLMA (f32)" in r.stderr
+    assert r.returncode == 1 and "not an LLMA/LLMQ checkpoint" in r.stderr
+    trunc = tmp_path / "trunc.bin"
+    trunc.write_bytes(b"LLMA" + b"\0" * 60)
+    r = subprocess.run([CLI, "llama", str(trunc)], capture_output=True, text=True, input="1 2\n")
+    assert r.returncode == 1
 
 
 @pytest.mark.gpu
@@ -85,3 +96,24 @@ def test_cli_matches_reference_loop(orc):
     assert r.stdout.splitlines() == want
     assert "skip out-of-range id 600 (vocab 512)" in r.stderr
     assert "loaded LLMQ (int8, in-memory): vocab 512" in r.stderr
+
+
+@pytest.mark.gpu
+def test_cli_llma_checkpoint_matches_reference_loop(orc, ref, tmp_path):
+    """An LLMA (f32) checkpoint, written by the reference's llama_model_save,
+    through the fp32 GPU path."""
+    import llmq
+    ref.llama_model_save.restype = C.c_int
+    ref.llama_model_save.argtypes = [C.c_char_p, C.POINTER(llmq.LlamaModel)]
+    m = ref.llama_model_create(512, 64, 2, 4, 2, 16, 160, 48, 10000.0, 1e-5)
+    ref.llama_model_randomize(C.byref(m))
+    path = tmp_path / "model_f32.bin"
+    assert ref.llama_model_save(str(path).encode(), C.byref(m)) == 0
+    lines = ["3 141 59 26 5", "42 7", "1 2 3 4 5 6 7 8 9 10 11 12 13 14 15 16 17 18 19 20 21 22 23 24 25 26 27 28 29 30"]
+    want = reference_protocol(orc, lines, 16, f32_model=m)
+    r = subprocess.run([CLI, "llama", str(path), "16"], input="".join(l + "\n" for l in lines),
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.splitlines() == want
+    assert "loaded LLMA (f32): vocab 512" in r.stderr
+    ref.llama_model_free(C.byref(m))
