@@ -67,6 +67,9 @@ WORKLOADS = {
                             rope_base=500000.0, eps=1e-5), prompt=64, gen=128, f32=True,
                    name="llama3-8b-shaped fp32 (LLMA path: the int8 synthetic model dequantised, as "
                         "llama_model_load reads an LLMQ file), batch 1: 64-id prompt then greedy decode"),
+    "8b2-f32": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128,
+                             d_ff=14336, rope_base=500000.0, eps=1e-5), prompt=16, gen=64, f32=True,
+                    name="llama3-8b layer shapes in fp32, 2 layers (profiling case), batch 1"),
     "tiny": dict(cfg=dict(vocab=32000, d_model=288, n_layers=6, n_heads=6, n_kv=2, head_dim=48, d_ff=768,
                           rope_base=10000.0, eps=1e-5), prompt=16, gen=240,
                  name="tiny llama int8 W8A8, batch 1: 16-id prompt then greedy decode"),
