@@ -113,6 +113,7 @@ struct MatF {
   float *w = nullptr;
   int *cta_t0 = nullptr;
   int K = 0, N = 0, grid = 0, threads = 0, rows = 0, slots = 0;
+  int tw = 32;  // tile width: output columns per warp
   size_t smem = 0;
 };
 
@@ -205,9 +206,11 @@ cudaError_t set_gemv_attr(int smem) {
 
 template <int PRO, int EPI>
 cudaError_t set_f32_attr(int smem) {
-  cudaError_t e = set_attr(k_gemv_f32<PRO, EPI, 256>, smem);
+  cudaError_t e = set_attr(k_gemv_f32<PRO, EPI, 256, 0>, smem);
+  if constexpr (f32_cpl(EPI) == 1)
+    if (e == cudaSuccess) e = set_attr(k_gemv_f32<PRO, EPI, 256, kF32RowsFull>, smem);
   if (e != cudaSuccess) return e;
-  return set_attr(k_gemv_f32<PRO, EPI, kF32MaxThreads>, smem);
+  return set_attr(k_gemv_f32<PRO, EPI, kF32MaxThreads, 0>, smem);
 }
 
 int init_expf_table(DevCtx &c) {
@@ -945,12 +948,17 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
 }
 
 // ------------------------------------------------------------ fp32 models
-// Lays out the N columns of a fused matrix as 32-column tiles, each a
-// contiguous [K][32] block; fused column p is column colsrc[p] & 0xffffff of
-// source colsrc[p] >> 24 (row-major [K][ns[src]]), or zero when colsrc[p] < 0.
-// Splits the tiles over `grid` CTAs and plans the per-warp rings.
+// Lays out the N columns of a fused matrix as tiles of kF32Tile (32 or 64, the
+// width the consuming epilogue's kernel reads: 32 * f32_cpl(epi)) columns,
+// each a contiguous block of f32_tile_rows(K) rows in the order the kernel
+// reads them ([K][64], or [K/4][32][4]); fused column p is column
+// colsrc[p] & 0xffffff of source colsrc[p] >> 24 (row-major [K][ns[src]]), or
+// zero when colsrc[p] < 0.  Splits the tiles over `grid` CTAs (one consumer
+// warp per tile, plus the producer warp for 32-column tiles) and plans the
+// per-warp rings.
 int build_matf(DevCtx &c, MatF &out, int K, const std::vector<int> &colsrc, const float *const src[3],
-               const int ns[3], int grid) {
+               const int ns[3], int grid, int pro, int epi) {
+  const int kF32Tile = 32 * f32_cpl(epi);
   const int N = static_cast<int>(colsrc.size());
   const int T = (N + kF32Tile - 1) / kF32Tile;
   std::vector<int> t0(grid + 1);
@@ -959,23 +967,35 @@ int build_matf(DevCtx &c, MatF &out, int K, const std::vector<int> &colsrc, cons
     t0[g] = static_cast<int>((long long)g * T / grid);
     if (g > 0) per_cta = std::max(per_cta, t0[g] - t0[g - 1]);
   }
-  const int threads = std::max(1, per_cta) * kF32Tile;
+  const int nc = std::max(1, per_cta);  // consumer warps, one per tile
+  const int threads = (nc + (f32_producer(epi) ? 1 : 0)) * 32;
   if (threads > kF32MaxThreads) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 product with %d columns is wider than this build handles", N);
     return 0;
   }
-  std::vector<float> buf((size_t)T * K * kF32Tile, 0.0f);
+  const int Kp = f32_tile_rows(K, f32_cpl(epi));
+  // position of (row k, column q) inside a tile
+  auto at = [kF32Tile](int k, int q) -> size_t {
+    return kF32Tile == 64 ? (size_t)k * 64 + q : ((size_t)(k >> 2) * 32 + q) * 4 + (k & 3);
+  };
+  std::vector<float> buf((size_t)T * Kp * kF32Tile, 0.0f);
   auto fill = [&](int ta, int tb) {
     for (int t = ta; t < tb; ++t) {
-      float *blk = buf.data() + (size_t)t * K * kF32Tile;
-      // a tile whose 32 columns are consecutive columns of one source is copied row by row
+      float *blk = buf.data() + (size_t)t * Kp * kF32Tile;
+      // a tile whose columns are consecutive columns of one source is copied row by row
       const int p0 = t * kF32Tile;
       bool run = p0 + kF32Tile <= N && colsrc[p0] >= 0;
       for (int q = 1; run && q < kF32Tile; ++q) run = colsrc[p0 + q] == colsrc[p0] + q;
       if (run) {
         const int sidx = colsrc[p0] >> 24, col = colsrc[p0] & 0xffffff;
-        for (int k = 0; k < K; ++k)
-          std::memcpy(blk + (size_t)k * kF32Tile, src[sidx] + (size_t)k * ns[sidx] + col, kF32Tile * sizeof(float));
+        for (int k = 0; k < K; ++k) {
+          const float *rowp = src[sidx] + (size_t)k * ns[sidx] + col;
+          if (kF32Tile == 64) {
+            std::memcpy(blk + (size_t)k * 64, rowp, 64 * sizeof(float));
+          } else {
+            for (int q = 0; q < 32; ++q) blk[at(k, q)] = rowp[q];
+          }
+        }
         continue;
       }
       for (int q = 0; q < kF32Tile && p0 + q < N; ++q) {
@@ -983,7 +1003,7 @@ int build_matf(DevCtx &c, MatF &out, int K, const std::vector<int> &colsrc, cons
         if (cs < 0) continue;
         const float *sp = src[cs >> 24] + (cs & 0xffffff);
         const int ld = ns[cs >> 24];
-        for (int k = 0; k < K; ++k) blk[(size_t)k * kF32Tile + q] = sp[(size_t)k * ld];
+        for (int k = 0; k < K; ++k) blk[at(k, q)] = sp[(size_t)k * ld];
       }
     }
   };
@@ -998,21 +1018,29 @@ int build_matf(DevCtx &c, MatF &out, int K, const std::vector<int> &colsrc, cons
   out.N = N;
   out.grid = grid;
   out.threads = threads;
-  // each warp's share of shared memory beside the input row (and its squares):
-  // slots of up to 16 KB (128 rows), as many as fit, at most 8
-  const int nw = threads / kF32Tile;
-  const long long xs_bytes = (2LL * roundup(K, 4) + 8) * 4;
-  const long long per_warp = ((long long)c.max_smem - 1024 - xs_bytes) / nw - 2 * kF32MaxSlots * 8;
-  int rows = static_cast<int>(std::min<long long>(128, per_warp / 4 / (kF32Tile * 4))) & ~7;
-  if (rows < 8) rows = 8;
-  const int slots = static_cast<int>(std::min<long long>(kF32MaxSlots, per_warp / ((long long)rows * kF32Tile * 4)));
+  out.tw = kF32Tile;
+  // each consumer warp's share of shared memory beside the input row (and, for
+  // RMSNorm, its squares).  32-column tiles: slots of 256 rows (the kernel's
+  // unrolled full-slot path) when two or more fit; otherwise, and for 64-column
+  // tiles, slots of up to 128 rows (16 or 32 KB), as many as fit, at most 8.
+  const long long xs_bytes = ((pro == F32_PRO_PLAIN ? 1LL : 2LL) * roundup(K, 4) + 8) * 4;
+  const long long per_warp = ((long long)c.max_smem - 1024 - xs_bytes) / nc - 2LL * 2 * kF32MaxSlots * 8;
+  int rows = 0, slots = 0;
+  if (kF32Tile == 32 && per_warp / (kF32RowsFull * 128LL) >= 2) {
+    rows = kF32RowsFull;
+    slots = static_cast<int>(std::min<long long>(kF32MaxSlots, per_warp / (kF32RowsFull * 128LL)));
+  } else {
+    rows = static_cast<int>(std::min<long long>(128, per_warp / 4 / (kF32Tile * 4))) & ~7;
+    if (rows < 8) rows = 8;
+    slots = static_cast<int>(std::min<long long>(kF32MaxSlots, per_warp / ((long long)rows * kF32Tile * 4)));
+  }
   if (slots < 2) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: fp32 product (K %d, %d columns) does not fit in shared memory", K, N);
     return 0;
   }
   out.rows = rows;
   out.slots = slots;
-  out.smem = (size_t)nw * slots * rows * kF32Tile * 4 + (((size_t)nw * slots + 1) & ~size_t(1)) * 8 + (size_t)xs_bytes;
+  out.smem = f32_ring_floats(nc, slots, rows, kF32Tile) * 4 + f32_bars(nc, slots) * 8 + (size_t)xs_bytes;
   return 1;
 }
 
@@ -1035,6 +1063,7 @@ std::vector<int> cols_interleave4(int n) {
 
 template <int PRO, int EPI>
 cudaError_t launch_f32(const MatF &m, F32Args a, cudaStream_t st, bool pdl = true) {
+  if (m.tw != 32 * f32_cpl(EPI)) return cudaErrorInvalidValue;  // laid out for another epilogue
   a.w = m.w;
   a.cta_t0 = m.cta_t0;
   a.K = m.K;
@@ -1052,8 +1081,12 @@ cudaError_t launch_f32(const MatF &m, F32Args a, cudaStream_t st, bool pdl = tru
   cfg.attrs = attr;
   cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
   ++g_launches;
-  if (m.threads <= 256) return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI, 256>, a);
-  return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI, kF32MaxThreads>, a);
+  if constexpr (f32_cpl(EPI) == 1) {
+    if (m.rows == kF32RowsFull && m.threads <= 256)
+      return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI, 256, kF32RowsFull>, a);
+  }
+  if (m.threads <= 256) return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI, 256, 0>, a);
+  return cudaLaunchKernelEx(&cfg, k_gemv_f32<PRO, EPI, kF32MaxThreads, 0>, a);
 }
 
 int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
@@ -1102,7 +1135,7 @@ int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
       const float *src[3] = {b.Wq.data, b.Wk.data, b.Wv.data};
       const int ns[3] = {qd, kvd, kvd};
       M->fqkv.emplace_back();
-      if (!build_matf(c, M->fqkv.back(), dm, cols_concat(ns), src, ns, grid)) return 0;
+      if (!build_matf(c, M->fqkv.back(), dm, cols_concat(ns), src, ns, grid, F32_PRO_RMSNORM, F32_EPI_QKV)) return 0;
       std::vector<float> bias((size_t)qd + 2 * kvd, 0.0f);  // llama.c:316-318 (absent biases are zero)
       if (b.b_q.data) std::memcpy(bias.data(), b.b_q.data, qd * sizeof(float));
       if (b.b_k.data) std::memcpy(bias.data() + qd, b.b_k.data, kvd * sizeof(float));
@@ -1115,19 +1148,19 @@ int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
       const float *src[3] = {b.Wo.data, nullptr, nullptr};
       const int ns[3] = {dm, 0, 0};
       M->fwo.emplace_back();
-      if (!build_matf(c, M->fwo.back(), qd, cols_concat(ns), src, ns, grid)) return 0;
+      if (!build_matf(c, M->fwo.back(), qd, cols_concat(ns), src, ns, grid, F32_PRO_PLAIN, F32_EPI_RESID)) return 0;
     }
     {
       const float *src[3] = {b.Wgate.data, b.Wup.data, nullptr};
       const int ns[3] = {dff, dff, 0};
       M->fw13.emplace_back();
-      if (!build_matf(c, M->fw13.back(), dm, cols_interleave4(dff), src, ns, grid)) return 0;
+      if (!build_matf(c, M->fw13.back(), dm, cols_interleave4(dff), src, ns, grid, F32_PRO_RMSNORM, F32_EPI_SWIGLU)) return 0;
     }
     {
       const float *src[3] = {b.Wdown.data, nullptr, nullptr};
       const int ns[3] = {dm, 0, 0};
       M->fw2.emplace_back();
-      if (!build_matf(c, M->fw2.back(), dff, cols_concat(ns), src, ns, grid)) return 0;
+      if (!build_matf(c, M->fw2.back(), dff, cols_concat(ns), src, ns, grid, F32_PRO_PLAIN, F32_EPI_RESID)) return 0;
     }
     float *an = nullptr, *fn = nullptr;
     if (!dev_upload(&an, b.attn_norm.data, dm) || !dev_upload(&fn, b.ffn_norm.data, dm)) return 0;
@@ -1141,7 +1174,7 @@ int upload_model_f32(DevCtx &c, const LlamaModel *m, DevModel *M) {
   {
     const float *src[3] = {m->lm_head.data, nullptr, nullptr};
     const int ns[3] = {cfg.vocab, 0, 0};
-    if (!build_matf(c, M->flm, dm, cols_concat(ns), src, ns, grid)) return 0;
+    if (!build_matf(c, M->flm, dm, cols_concat(ns), src, ns, grid, F32_PRO_RMSNORM, F32_EPI_LOGITS)) return 0;
   }
   if (!dev_upload(&M->final_norm, m->final_norm.data, dm)) return 0;
   if (!dev_upload(&M->wte_f, m->wte.data, (size_t)cfg.vocab * dm)) return 0;

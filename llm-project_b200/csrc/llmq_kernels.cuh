@@ -74,6 +74,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
       : "memory");
   return ok != 0;
 }
+// Non-blocking test of an mbarrier phase (for a lane that polls several).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait on an mbarrier phase: gives up after 2^32 SM cycles (about 2 s
 // at boost clock; the SM-local counter is cheap to read, unlike %globaltimer)
 // or 2^26 polls, so a lost copy can never hang the GPU.

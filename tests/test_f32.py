@@ -138,6 +138,18 @@ def test_f32_decode_tiny_matches_oracle(lib, orc):
 
 
 @pytest.mark.gpu
+def test_f32_decode_odd_shapes_matches_oracle(lib, orc):
+    """Chain lengths that are not multiples of 4 or 8 (d_model 50, q width
+    50, d_ff 71): the short tails of the tile rows and of the input rows."""
+    cfg = dict(vocab=1001, d_model=50, n_layers=2, n_heads=5, n_kv=1, head_dim=10, d_ff=71, max_seq=16,
+               rope_base=10000.0, eps=1e-5)
+    m = synth_f32(lib, cfg, seed=77)
+    ids = [0, 1000, 5, 77, 3, 999]
+    assert bits_equal(gpu_f32_decode(lib, m, ids), orc_f32_decode(orc, m, ids))
+    lib.llmq_llama_model_free(C.byref(m))
+
+
+@pytest.mark.gpu
 def test_f32_decode_8b_shapes_two_layers(lib, orc):
     """LLaMA-3-8B layer shapes in fp32 (dm 4096, dff 14336: the down
     projection's chains are 14336 long; vocab 128256: 109 units per CTA)."""
