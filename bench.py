@@ -248,7 +248,8 @@ def run_ours(args, rank, world):
     kv.len = start_len
     if lib.llmq_step_profile(C.byref(m), C.byref(kv), start_tok, prof.ctypes.data_as(llmq.c_float_p), nk) != 0:
         llmq.check(lib)
-    names = ["qkv", "attn_scores", "attn_pv", "wo", "w13", "w2"]
+    per_layer = (nk - 2) // cfg["n_layers"]
+    names = ["qkv", "attn", "wo", "w13", "w2"] if per_layer == 5 else ["qkv", "attn_scores", "attn_pv", "wo", "w13", "w2"]
     step_profile = {n: round(float(prof[i:nk - 2:len(names)].sum()), 4) for i, n in enumerate(names)}
     step_profile.update(lm_head=round(float(prof[nk - 2]), 4), finish=round(float(prof[nk - 1]), 4),
                         total=round(float(prof.sum()), 4), unit="ms per step, kernels serialised")
@@ -391,7 +392,9 @@ def run_f32(args, rank, world):
                      "kernel": "whole step: fp32 weight bytes per step / step time (k_gemv_f32 dominates)",
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (measured)" if peaks else "fallback 6650 GB/s"},
         "cpu_baseline": cpu,
-        "gpu_launches": K * (6 * cfg["n_layers"] + 2),  # per step: 6 per layer, lm-head, finish
+        # per step: QKV, attention (1 or 2), Wo, W1|W3, W2 per layer; lm-head, finish
+        "gpu_launches": K * ((4 + int(lib.llmq_attention_launches(cfg["n_heads"], cfg["n_kv"], cfg["head_dim"],
+                                                                  int(c.max_seq)))) * cfg["n_layers"] + 2),
         "clocks": clk.summary(),
     }
     lib.llama_kv_free(C.byref(kv))

@@ -417,8 +417,16 @@ int llmq_expf_device(const float *x, float *y, long long n);
 int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int iters, float *ms_per_launch,
                     double *bytes_per_launch);
 
-/* Kernels launched by one decode step (6 per layer + 2). */
+/* Kernels launched by one decode step: per layer QKV, attention (one fused
+ * launch, or two), Wo, W1|W3, W2 (+ 2 absmax exchanges under tensor
+ * parallelism); then lm-head and the step's bookkeeping. */
 int llmq_kernels_per_step(const QLlamaModel *m);
+
+/* Attention launches per layer of a batch-1 step with these dimensions: 1 (the
+ * fused cluster kernel) or 2 (scores, then softmax and values; chosen when the
+ * fused kernel's shared memory would not fit, or LLMQ_ATTN_TWO_KERNELS=1);
+ * -1 without a suitable GPU. */
+int llmq_attention_launches(int n_heads, int n_kv, int head_dim, int max_seq);
 
 /* Times `iters` device-resident products C(M, N) = A(M, K) x W on the path
  * qmatmul uses (int8 GEMV for M <= 8, tcgen05 tensor cores for larger M), with

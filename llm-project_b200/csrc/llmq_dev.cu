@@ -274,6 +274,7 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_gemv_attr<PRO_RMSNORM, EPI_LOGITS, 1>(sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_attn_scores, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_attn_pv, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_attn_fused, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<64>, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_tc_gemm<128>, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_act_codes, 0);
@@ -547,8 +548,50 @@ size_t pv_smem(const AttnArgs &a) {
   return ((((size_t)a.max_seq + 3) & ~size_t(3)) + (size_t)kPVRing * kPVChunk * kPVSlice) * sizeof(float);
 }
 
-// The two attention kernels of one layer: scores (part 0), then softmax and
-// values (part 1).
+// Shared memory of k_attn_fused with key chunks of kc rows: q and the rotated
+// k, the weights, the value slice, the key chunk slots (one when a part of the
+// positions always fits in one chunk, else two).
+size_t fused_smem(const AttnArgs &a, int kc) {
+  const int hd4 = (a.hd + 3) & ~3, stride = (a.hd & 3) == 0 ? a.hd + 4 : a.hd + 1;
+  const int nsl = (a.hd + kPVSlice - 1) / kPVSlice;
+  const int part = (a.max_seq + nsl - 1) / nsl;
+  const int slots = kc >= part ? 1 : 2;
+  return (2 * (size_t)hd4 + (((size_t)a.max_seq + 3) & ~size_t(3)) + (size_t)a.max_seq * kPVSlice +
+          (size_t)slots * kc * stride) *
+         sizeof(float);
+}
+// Key chunk for the fused attention: a whole part of the positions when it
+// fits in shared memory, else the largest multiple of 32 rows (at least 32)
+// that does; 0 (the two-kernel path) when not even that fits or a head spans
+// more than 8 slices (the portable cluster size).
+int fused_chunk_rows(const AttnArgs &a, size_t max_smem) {
+  const int nsl = (a.hd + kPVSlice - 1) / kPVSlice;
+  if (nsl > 8) return 0;
+  const int part = (a.max_seq + nsl - 1) / nsl;
+  if (fused_smem(a, part) <= max_smem) return part;
+  for (int kc = ((part - 1) / 32) * 32; kc >= 32; kc -= 32)
+    if (fused_smem(a, kc) <= max_smem) return kc;
+  return 0;
+}
+
+// LLMQ_ATTN_TWO_KERNELS=1 selects the two-kernel attention everywhere (the
+// same arithmetic; for comparisons).
+bool attn_two_kernels_forced() {
+  static const bool on = [] {
+    const char *e = getenv("LLMQ_ATTN_TWO_KERNELS");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+// The batch-1 attention arguments' choice between the two paths.
+void choose_attention(AttnArgs &a) {
+  a.pv_whole = pv_whole_bytes(a.max_seq) <= kPVWholeLimit;
+  a.fused_chunk = attn_two_kernels_forced() ? 0 : fused_chunk_rows(a, (size_t)g_smem_optin - 256);
+}
+
+// The attention of one layer: k_attn_fused when a.fused_chunk > 0 (part 0;
+// part 1 launches nothing), else the scores (part 0), then softmax and values
+// (part 1).
 cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl, int part) {
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -557,6 +600,23 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl, int p
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+  if (a.fused_chunk > 0) {
+    if (part != 0) return cudaSuccess;
+    const int nsl = (a.hd + kPVSlice - 1) / kPVSlice;
+    cudaLaunchAttribute fat[2];
+    fat[0] = attr[0];
+    fat[1].id = cudaLaunchAttributeClusterDimension;
+    fat[1].val.clusterDim.x = nsl;
+    fat[1].val.clusterDim.y = 1;
+    fat[1].val.clusterDim.z = 1;
+    cfg.attrs = fat;
+    cfg.numAttrs = (pdl && pdl_enabled()) ? 2 : 1;
+    if (cfg.numAttrs == 1) fat[0] = fat[1];
+    cfg.gridDim = dim3(nsl, a.n_heads);
+    cfg.blockDim = dim3(kFusedThreads);
+    cfg.dynamicSmemBytes = fused_smem(a, a.fused_chunk);
+    return cudaLaunchKernelEx(&cfg, k_attn_fused, a);
+  }
   if (part == 0) {
     cfg.gridDim = dim3((a.max_seq + kScoreChunk - 1) / kScoreChunk, a.n_kv);
     cfg.blockDim = dim3(kScoreThreads);
@@ -1456,11 +1516,13 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       a.n_kv = cfg.n_kv;
       a.hd = cfg.head_dim;
       a.max_seq = K->max_seq;
-      a.pv_whole = pv_whole_bytes(K->max_seq) <= kPVWholeLimit;
+      choose_attention(a);
       CK(launch_attention(a, st, true, 0));
       PROF_MARK();
-      CK(launch_attention(a, st, true, 1));
-      PROF_MARK();
+      if (a.fused_chunk == 0) {
+        CK(launch_attention(a, st, true, 1));
+        PROF_MARK();
+      }
     }
     if (M->f32) {
       F32Args a = f32_args();
@@ -2319,7 +2381,7 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
     at.n_kv = M->cfg.n_kv;
     at.hd = M->cfg.head_dim;
     at.max_seq = K->max_seq;
-    at.pv_whole = pv_whole_bytes(K->max_seq) <= kPVWholeLimit;
+    choose_attention(at);
     launch = [&]() {
       const cudaError_t e = launch_attention(at, st, false, 0);
       return e != cudaSuccess ? e : launch_attention(at, st, false, 1);
@@ -2365,11 +2427,34 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
   return LLMQ_OK;
 }
 
+// Attention launches per layer of a batch-1 step for these dimensions: 1 (the
+// fused kernel) or 2.
+LLMQ_API int llmq_attention_launches(int n_heads, int n_kv, int head_dim, int max_seq) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  if (!get_ctx()) return -1;
+  AttnArgs probe{};
+  probe.n_heads = n_heads;
+  probe.n_kv = n_kv;
+  probe.hd = head_dim;
+  probe.max_seq = max_seq;
+  choose_attention(probe);
+  return probe.fused_chunk > 0 ? 1 : 2;
+}
+
 // Number of kernels one decode step launches (for the benchmark's gpu_launches).
 LLMQ_API int llmq_kernels_per_step(const QLlamaModel *m) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   const DevModel *M = find_model(m);
-  return (M && M->tp_world > 1 ? 8 : 6) * m->n_layers + 2;  // + the absmax exchange per row-parallel product
+  if (!M) return 0;
+  AttnArgs probe{};
+  probe.n_heads = M->cfg.n_heads;
+  probe.n_kv = M->cfg.n_kv;
+  probe.hd = M->cfg.head_dim;
+  probe.max_seq = M->cfg.max_seq;
+  choose_attention(probe);
+  const int attn = probe.fused_chunk > 0 ? 1 : 2;
+  // QKV, attention, Wo, W1|W3, W2 (+ the absmax exchange per row-parallel product); lm-head, finish
+  return (4 + attn + (M->tp_world > 1 ? 2 : 0)) * m->n_layers + 2;
 }
 
 // ------------------------------------------------- tensor-parallel group API

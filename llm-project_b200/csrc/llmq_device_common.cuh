@@ -98,6 +98,42 @@ __device__ __forceinline__ float seq_sum(const float *v, int stride, int n, floa
   return acc;
 }
 
+// seq_sum for a contiguous, 16-byte aligned v: 16 values in flight as four
+// 16-byte loads, so a single thread's chain keeps running while the shared
+// memory is busy with other traffic (e.g. copies landing).
+__device__ __forceinline__ float seq_sum_a16(const float *v, int n, float acc) {
+  const float4 *v4 = reinterpret_cast<const float4 *>(v);
+  int i = 0;
+  if (n >= 16) {
+    float4 c[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) c[u] = v4[u];
+    for (i = 16; i + 16 <= n; i += 16) {
+      float4 nx[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) nx[u] = v4[(i >> 2) + u];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc = __fadd_rn(acc, c[u].x);
+        acc = __fadd_rn(acc, c[u].y);
+        acc = __fadd_rn(acc, c[u].z);
+        acc = __fadd_rn(acc, c[u].w);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) c[u] = nx[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc = __fadd_rn(acc, c[u].x);
+      acc = __fadd_rn(acc, c[u].y);
+      acc = __fadd_rn(acc, c[u].z);
+      acc = __fadd_rn(acc, c[u].w);
+    }
+  }
+  for (; i < n; ++i) acc = __fadd_rn(acc, v[i]);
+  return acc;
+}
+
 // Sequential f32 dot product acc + a[0]*b[0] + a[1]*b[sb] + ..., each product
 // and each sum rounded on its own in C order.  Software-pipelined: the loads of
 // the next group of 8 are issued before the 8 adds of the current group, so

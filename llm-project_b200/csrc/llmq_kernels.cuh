@@ -14,7 +14,11 @@
 #include "libm_expf.h"
 #include "llmq_device_common.cuh"
 
+#include <cooperative_groups.h>
+
 namespace llmq {
+
+namespace cg = cooperative_groups;
 
 // Phase timestamps for profiling builds (-DLLMQ_PHASE_TIMING): thread 0 of the
 // first 64 CTAs records %globaltimer at numbered points.  Compiled out otherwise.
@@ -640,6 +644,7 @@ struct AttnArgs {
   const float *rope_cos, *rope_sin;  // [max_seq][hd/2]
   int n_heads, n_kv, hd, max_seq;
   int pv_whole;  // k_attn_pv stages the whole value slice at once (it fits in shared memory)
+  int fused_chunk;  // > 0: k_attn_fused with key chunks of this many rows (0: the two-kernel path)
 };
 
 constexpr int kScoreChunk = 32;    // key positions per scores CTA
@@ -761,8 +766,8 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
   const int nchunks = (np + kPVChunk - 1) / kPVChunk;
   if (a.pv_whole) {
     // The whole slice [0, np) x [d0, d0 + w) is staged while the softmax runs;
-    // then one uninterrupted chain per output dimension, with w = e * (1/sum)
-    // formed inside it (same rounded products, no separate pass).
+    // then w = e * (1/sum) for every position, and one uninterrupted chain per
+    // output dimension (one lane each).
     float *vs = ring;  // [np][kPVSlice]
     stage_rows(vs, kPVSlice, vc, hd, 0, np, d0, w, tid, kPVThreads);
     cp_async_commit();
@@ -778,16 +783,15 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
     for (int p = tid; p < np; p += kPVThreads) wts[p] = libm_expf(__fsub_rn(wts[p], m));
     __syncthreads();
     LLMQ_TSTAMP(2);
-    if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum(wts, 1, np, 0.0f));  // llama.c:567
+    if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum_a16(wts, np, 0.0f));  // llama.c:567
     LLMQ_TSTAMP(3);
+    __syncthreads();
+    const float inv = s_inv;
+    for (int p = tid; p < np; p += kPVThreads) wts[p] = __fmul_rn(wts[p], inv);
     cp_async_wait<0>();
     __syncthreads();
     LLMQ_TSTAMP(4);
-    if (2 * tid < w) {  // dims d0 + 2 tid and d0 + 2 tid + 1, two chains in packed lanes (hd is even)
-      const float2 o2 = seq_dot2<true>(wts, s_inv, reinterpret_cast<const float2 *>(vs) + tid, kPVSlice / 2, np,
-                                       make_float2(0.0f, 0.0f));
-      *reinterpret_cast<float2 *>(a.out + (size_t)h * hd + d0 + 2 * tid) = o2;
-    }
+    if (tid < w) a.out[(size_t)h * hd + d0 + tid] = seq_dot(wts, vs + tid, kPVSlice, np, 0.0f);  // llama.c:574
     LLMQ_TSTAMP(5);
     return;
   }
@@ -811,7 +815,7 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
   __syncthreads();
   LLMQ_TSTAMP(2);
   if (tid == 0) {
-    const float sum = seq_sum(wts, 1, np, 0.0f);  // llama.c:567
+    const float sum = seq_sum_a16(wts, np, 0.0f);  // llama.c:567
     s_inv = __fdiv_rn(1.0f, sum);
   }
   __syncthreads();
@@ -835,6 +839,111 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
   }
   LLMQ_TSTAMP(4);
   if (tid < w) a.out[(size_t)h * hd + d0 + tid] = o;
+}
+
+// Attention of one query head in one launch (llama.c:558-575), for batch-1
+// decode: a cluster of nsl = ceil(hd / 32) CTAs per head, CTA r owning the
+// output dimensions [32 r, 32 r + 32) and the key positions [pa, pb) of the
+// r-th part of [0, pos].
+//  1. q (and, in the part holding `pos`, this step's k) get RoPE; the part's
+//     keys stream through a two-chunk ring and each score is the sequential
+//     dot product over hd, times 1/sqrt(hd), into e[p] (own shared memory).
+//     The whole value slice [0, pos] x [32 r, 32 r + 32) is staged meanwhile.
+//  2. The cluster's maximum: each CTA reads the others' part maxima through
+//     distributed shared memory; each exponentiates its own part.
+//  3. Each CTA copies the other parts' exponentials into its own e, so every
+//     CTA holds e[0 .. pos]; then the sequential sum, w = e * (1/sum), and one
+//     chain per output dimension over the positions.
+// The arithmetic and its order are the two-kernel path's (k_attn_scores,
+// k_attn_pv), so the outputs are the same bits.
+// Shared memory: q and rotated k (2 hd4), e (max_seq, rounded to 4), the value
+// slice (max_seq x 32), the key chunks (one or two slots of a.fused_chunk rows
+// of hd + 4 (or + 1) floats).
+constexpr int kFusedThreads = 256;
+__global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) {
+  extern __shared__ __align__(16) float sm_f[];
+  __shared__ float s_red[32];
+  __shared__ float s_part_max;
+  __shared__ float s_inv;
+  cg::cluster_group cluster = cg::this_cluster();
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x;
+  const int h = blockIdx.y;
+  const int nsl = gridDim.x, r = blockIdx.x;  // the cluster spans gridDim.x: rank r = blockIdx.x
+  const int pos = a.step->pos;
+  if (pos < 0 || pos >= a.max_seq) return;  // same for every CTA of the cluster; flagged by the QKV epilogue
+  const int np = pos + 1, hd = a.hd, half = hd / 2, group = a.n_heads / a.n_kv, kvh = h / group;
+  const int hd4 = (hd + 3) & ~3, stride = (hd & 3) == 0 ? hd + 4 : hd + 1;
+  const int d0 = r * kPVSlice, w = max(0, min(kPVSlice, hd - d0));
+  const int pa = (int)((long long)r * np / nsl), pb = (int)((long long)(r + 1) * np / nsl);
+  float *qs = sm_f;                                                 // [hd4]
+  float *kn = qs + hd4;                                             // [hd4] this step's rotated k
+  float *e = kn + hd4;                                              // [max_seq] scores, then exps, then weights
+  float *vs = e + (((size_t)a.max_seq + 3) & ~size_t(3));           // [max_seq][32]
+  float *kring = vs + (size_t)a.max_seq * kPVSlice;                 // [1 or 2][KC][stride]
+  const int KC = a.fused_chunk;
+  const float *kc = a.kcache + (size_t)kvh * a.max_seq * hd;
+  const float *vc = a.vcache + (size_t)kvh * a.max_seq * hd;
+  // the value slice (its row `pos` is this step's, written by the QKV epilogue)
+  if (w > 0) stage_rows(vs, kPVSlice, vc, hd, 0, np, d0, w, tid, kFusedThreads);
+  cp_async_commit();
+  const int nchunks = (pb - pa + KC - 1) / KC;  // one slot when a part fits in one chunk, else two
+  auto stage_keys = [&](int c) {  // cached keys of chunk c (not the row `pos`, rotated below)
+    const int r0 = pa + c * KC, r1 = min(pa + (c + 1) * KC, pb);
+    stage_rows(kring + (size_t)(c & 1) * KC * stride, stride, kc, hd, r0, min(r1, pos), 0, hd, tid, kFusedThreads);
+  };
+  if (nchunks > 0) stage_keys(0);
+  cp_async_commit();
+  const float *cs = a.rope_cos + (size_t)pos * half, *sn = a.rope_sin + (size_t)pos * half;
+  const bool own_pos = pos >= pa && pos < pb;
+  for (int d = tid; d < hd; d += kFusedThreads) {
+    qs[d] = rope_elem(a.q + (size_t)h * hd, d, half, cs, sn);
+    if (own_pos) {
+      const float kr = rope_elem(a.q + (size_t)a.n_heads * hd + (size_t)kvh * hd, d, half, cs, sn);
+      kn[d] = kr;
+      if (h % group == 0) a.kcache[((size_t)kvh * a.max_seq + pos) * hd + d] = kr;  // llama.c:551
+    }
+  }
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));  // llama.c:532
+  float m = -INFINITY;
+  for (int c = 0; c < nchunks; ++c) {
+    if (c + 1 < nchunks) stage_keys(c + 1);
+    cp_async_commit();
+    cp_async_wait<1>();  // chunk c (and the value slice, committed first) have landed
+    __syncthreads();
+    const float *ring = kring + (size_t)(c & 1) * KC * stride;
+    const int r0 = pa + c * KC, rows = min(KC, pb - r0);
+    for (int i = tid; i < rows; i += kFusedThreads) {
+      const int p = r0 + i;
+      const float *kr = p == pos ? kn : ring + (size_t)i * stride;
+      const float dot = (hd & 3) == 0 ? seq_dot_v4(qs, kr, hd, 0.0f) : seq_dot(qs, kr, 1, hd, 0.0f);  // llama.c:561
+      const float sv = __fmul_rn(dot, scale);
+      e[p] = sv;
+      m = fmaxf(m, sv);
+    }
+    __syncthreads();  // the slot is free for chunk c + 2
+  }
+  m = block_max<kFusedThreads>(m, s_red);
+  if (tid == 0) s_part_max = m;
+  cluster.sync();  // every part's maximum is published
+  for (int q = 0; q < nsl; ++q) m = fmaxf(m, *cluster.map_shared_rank(&s_part_max, q));
+  for (int p = pa + tid; p < pb; p += kFusedThreads) e[p] = libm_expf(__fsub_rn(e[p], m));  // llama.c:566
+  cluster.sync();  // every part's exponentials are published
+  for (int q = 0; q < nsl; ++q) {
+    if (q == r) continue;
+    const int qa = (int)((long long)q * np / nsl), qb = (int)((long long)(q + 1) * np / nsl);
+    const float *pe = cluster.map_shared_rank(e, q);
+    for (int p = qa + tid; p < qb; p += kFusedThreads) e[p] = pe[p];
+  }
+  cluster.sync();  // no CTA reads another's shared memory after this point
+  if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum_a16(e, np, 0.0f));  // llama.c:567
+  __syncthreads();
+  const float inv = s_inv;
+  for (int p = tid; p < np; p += kFusedThreads) e[p] = __fmul_rn(e[p], inv);
+  cp_async_wait<0>();
+  __syncthreads();
+  if (tid < w) a.out[(size_t)h * hd + d0 + tid] = seq_dot(e, vs + tid, kPVSlice, np, 0.0f);  // llama.c:574
 }
 
 // Final step bookkeeping: publish the argmax and error flags, advance the

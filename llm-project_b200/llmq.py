@@ -131,6 +131,7 @@ SIGNATURES = {
     "llmq_bench_gemv": (C.c_int, [C.POINTER(QLlamaModel), C.c_int, C.c_int, C.c_int, c_float_p,
                                   C.POINTER(C.c_double)]),
     "llmq_kernels_per_step": (C.c_int, [C.POINTER(QLlamaModel)]),
+    "llmq_attention_launches": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "q_llama_set_device": (C.c_int, [C.c_int]),
     "llmq_step_profile": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(LlamaKV), C.c_int, c_float_p, C.c_int]),
     "qmatmul_device_noalloc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int,

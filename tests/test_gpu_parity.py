@@ -154,6 +154,29 @@ def test_decode_long_cache_vs_oracle(lib, orc):
     lib.q_llama_model_free(C.byref(m))
 
 
+def test_attention_path_choice(lib):
+    """The fused cluster attention is taken wherever its shared memory fits
+    (the 8B headline cache, a 1400-position cache with 32-row key chunks); the
+    two-kernel path beyond (TINY heads at max_seq 2048, covered above)."""
+    assert lib.llmq_attention_launches(32, 8, 128, 768) == 1
+    assert lib.llmq_attention_launches(4, 2, 128, 1400) == 1
+    assert lib.llmq_attention_launches(TINY["n_heads"], TINY["n_kv"], TINY["head_dim"], 2048) == 2
+
+
+def test_decode_fused_attention_key_chunks_vs_oracle(lib, orc):
+    """hd 128 at max_seq 1400: a part of the positions does not fit in shared
+    memory at once, so the fused kernel streams its keys through two slots;
+    300 positions, GQA 4/2."""
+    cfg = dict(vocab=512, d_model=256, n_layers=2, n_heads=4, n_kv=2, head_dim=128, d_ff=512, max_seq=1400,
+               rope_base=10000.0, eps=1e-5)
+    m = synth(lib, cfg, seed=41, with_bias=True)
+    ids = np.random.default_rng(4).integers(0, cfg["vocab"], 300).tolist()
+    ologits, _ = orc_decode(orc, m, ids)
+    glogits, _ = gpu_decode(lib, m, ids)
+    assert bits_equal(glogits, ologits)
+    lib.q_llama_model_free(C.byref(m))
+
+
 def test_generate_matches_stepwise_argmax(lib):
     m = synth(lib, TINY, seed=77)
     kv1 = lib.q_llama_kv_create(C.byref(m))
