@@ -676,10 +676,27 @@ __device__ __forceinline__ float rope_elem(const float *x, int d, int half, cons
 __device__ __forceinline__ void stage_rows(float *dst, int sld, const float *src, int ld, int r0, int r1, int c0,
                                            int w, int tid, int nthreads) {
   if (((ld | c0 | w | sld) & 3) == 0) {
+    // 16-byte pieces i = r * q + j; the (r, j) of a thread's next piece follow
+    // from one division up front (no division per copy: the issue loop is on
+    // the critical path of the attention kernels)
     const int q = w >> 2;
-    for (int i = tid; i < (r1 - r0) * q; i += nthreads) {
-      const int r = i / q, c = (i - r * q) * 4;
-      cp_async16(dst + (size_t)r * sld + c, src + (size_t)(r0 + r) * ld + c0 + c);
+    if (q <= 0 || r1 <= r0) return;
+    const int dr = nthreads / q, dj = nthreads - dr * q;
+    int r = tid / q, j = tid - r * q;
+    const float *s = src + (size_t)(r0 + r) * ld + c0;
+    float *d = dst + (size_t)r * sld;
+    while (r < r1 - r0) {
+      cp_async16(d + 4 * j, s + 4 * j);
+      r += dr;
+      s += (size_t)dr * ld;
+      d += (size_t)dr * sld;
+      j += dj;
+      if (j >= q) {
+        j -= q;
+        ++r;
+        s += ld;
+        d += sld;
+      }
     }
   } else {
     for (int i = tid; i < (r1 - r0) * w; i += nthreads) {
@@ -849,11 +866,11 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
 //     keys stream through a two-chunk ring and each score is the sequential
 //     dot product over hd, times 1/sqrt(hd), into e[p] (own shared memory).
 //     The whole value slice [0, pos] x [32 r, 32 r + 32) is staged meanwhile.
-//  2. The cluster's maximum: each CTA reads the others' part maxima through
-//     distributed shared memory; each exponentiates its own part.
-//  3. Each CTA copies the other parts' exponentials into its own e, so every
-//     CTA holds e[0 .. pos]; then the sequential sum, w = e * (1/sum), and one
-//     chain per output dimension over the positions.
+//  2. The cluster's maximum: each CTA stores its part's maximum into every
+//     CTA (distributed shared memory); after a cluster barrier each takes the
+//     maximum, exponentiates its own part and stores it into every CTA's e.
+//  3. After a second barrier every CTA holds e[0 .. pos]: the sequential sum,
+//     w = e * (1/sum), and one chain per output dimension over the positions.
 // The arithmetic and its order are the two-kernel path's (k_attn_scores,
 // k_attn_pv), so the outputs are the same bits.
 // Shared memory: q and rotated k (2 hd4), e (max_seq, rounded to 4), the value
@@ -863,7 +880,7 @@ constexpr int kFusedThreads = 256;
 __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) {
   extern __shared__ __align__(16) float sm_f[];
   __shared__ float s_red[32];
-  __shared__ float s_part_max;
+  __shared__ float s_part_max[8];  // [rank]: stored by that CTA
   __shared__ float s_inv;
   cg::cluster_group cluster = cg::this_cluster();
   pdl_launch_dependents();
@@ -925,18 +942,14 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
     __syncthreads();  // the slot is free for chunk c + 2
   }
   m = block_max<kFusedThreads>(m, s_red);
-  if (tid == 0) s_part_max = m;
-  cluster.sync();  // every part's maximum is published
-  for (int q = 0; q < nsl; ++q) m = fmaxf(m, *cluster.map_shared_rank(&s_part_max, q));
-  for (int p = pa + tid; p < pb; p += kFusedThreads) e[p] = libm_expf(__fsub_rn(e[p], m));  // llama.c:566
-  cluster.sync();  // every part's exponentials are published
-  for (int q = 0; q < nsl; ++q) {
-    if (q == r) continue;
-    const int qa = (int)((long long)q * np / nsl), qb = (int)((long long)(q + 1) * np / nsl);
-    const float *pe = cluster.map_shared_rank(e, q);
-    for (int p = qa + tid; p < qb; p += kFusedThreads) e[p] = pe[p];
+  if (tid < nsl) *cluster.map_shared_rank(&s_part_max[r], tid) = m;  // this part's maximum, into CTA tid
+  cluster.sync();  // every part's maximum is in every CTA
+  for (int q = 0; q < nsl; ++q) m = fmaxf(m, s_part_max[q]);
+  for (int p = pa + tid; p < pb; p += kFusedThreads) {
+    const float ex = libm_expf(__fsub_rn(e[p], m));  // llama.c:566
+    for (int q = 0; q < nsl; ++q) *cluster.map_shared_rank(&e[p], q) = ex;  // into every CTA's e
   }
-  cluster.sync();  // no CTA reads another's shared memory after this point
+  cluster.sync();  // every part's exponentials are in every CTA; no remote accesses after this point
   if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum_a16(e, np, 0.0f));  // llama.c:567
   __syncthreads();
   const float inv = s_inv;
