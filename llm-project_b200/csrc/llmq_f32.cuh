@@ -280,7 +280,7 @@ __global__ void __launch_bounds__(MAXT, 1) k_gemv_f32(const F32Args a) {
     for (int k = tid; k < K; k += nthr) sq[k] = __fmul_rn(xs[k], xs[k]);
     __syncthreads();
     if (tid == 0) {
-      float ms = seq_sum(sq, 1, K, 0.0f);
+      float ms = seq_sum_a16(sq, K, 0.0f);  // sq is 16-byte aligned
       ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
       s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
     }

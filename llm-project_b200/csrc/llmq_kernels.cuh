@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     for (int k = tid; k < K; k += kThreads) sq[k] = __fmul_rn(xs[k], xs[k]);
     __syncthreads();
     if (tid == 0) {
-      float ms = seq_sum(sq, 1, K, 0.0f);
+      float ms = seq_sum_a16(sq, K, 0.0f);  // sq is 16-byte aligned
       ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
       s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
       LLMQ_TSTAMP(4);
