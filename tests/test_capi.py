@@ -97,6 +97,9 @@ def test_no_gpu_fails_loudly(lib):
     m = llmq.QLlamaModel()
     assert lib.q_llama_model_load(os.path.join(GOLDEN, "mini.llmq").encode(), C.byref(m)) == 1
     lib.q_llama_clear_error()
+    # the attention-path query needs the device's shared-memory limit
+    assert lib.llmq_attention_launches(32, 8, 128, 768) == -1
+    lib.q_llama_clear_error()
 
 
 def test_save_roundtrip_and_reference_loader(lib, orc, ref, tmp_path):
