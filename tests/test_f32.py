@@ -15,6 +15,9 @@ from conftest import GOLDEN
 from helpers import TINY, bits_equal, fp, orc_sample
 
 F32_TINY = dict(TINY, max_seq=64)
+# chain lengths that are not multiples of 4 or 8 (d_model 50, q width 50, d_ff 71)
+ODD_F32 = dict(vocab=1001, d_model=50, n_layers=2, n_heads=5, n_kv=1, head_dim=10, d_ff=71, max_seq=16,
+               rope_base=10000.0, eps=1e-5)
 
 
 def synth_f32(lib, cfg, seed=1234, with_bias=True, stddev=0.02):
@@ -69,6 +72,11 @@ def test_oracle_f32_decode_matches_reference(lib, orc, ref):
     ref.llama_model_free(C.byref(rm))
     m = synth_f32(lib, dict(F32_TINY, n_layers=2), seed=7)
     ids = [5, 77, 31999, 0, 1234]
+    assert bits_equal(orc_f32_decode(orc, m, ids), ref_f32_decode(ref, m, ids))
+    lib.llmq_llama_model_free(C.byref(m))
+    # the odd shapes of the GPU test (chains of 50 and 71 terms)
+    m = synth_f32(lib, ODD_F32, seed=77)
+    ids = [0, 1000, 5, 77, 3, 999]
     assert bits_equal(orc_f32_decode(orc, m, ids), ref_f32_decode(ref, m, ids))
     lib.llmq_llama_model_free(C.byref(m))
 
@@ -141,9 +149,7 @@ def test_f32_decode_tiny_matches_oracle(lib, orc):
 def test_f32_decode_odd_shapes_matches_oracle(lib, orc):
     """Chain lengths that are not multiples of 4 or 8 (d_model 50, q width
     50, d_ff 71): the short tails of the tile rows and of the input rows."""
-    cfg = dict(vocab=1001, d_model=50, n_layers=2, n_heads=5, n_kv=1, head_dim=10, d_ff=71, max_seq=16,
-               rope_base=10000.0, eps=1e-5)
-    m = synth_f32(lib, cfg, seed=77)
+    m = synth_f32(lib, ODD_F32, seed=77)
     ids = [0, 1000, 5, 77, 3, 999]
     assert bits_equal(gpu_f32_decode(lib, m, ids), orc_f32_decode(orc, m, ids))
     lib.llmq_llama_model_free(C.byref(m))
