@@ -8,7 +8,7 @@
  * convention below is the reference's, so a caller written against quant.h /
  * llama.h compiles and links unchanged.  All arithmetic runs on the GPU: the
  * results are bit-identical to the reference CPU code (same int8 codes, same
- * int32 accumulators, same fp32 rounding sequence), see DESIGN.md.
+ * int32 accumulators, same fp32 rounding sequence, the same libm expf results).
  *
  * Additions (new names, same C style) carry a comment saying so.  No entry point
  * takes or returns a torch or CUDA type.  Compute functions that return void in the
@@ -116,22 +116,22 @@ typedef struct {
 /* quant.h entry points                                                       */
 /* ========================================================================= */
 
-/* Replaces quant.c:45-62 (declared quant.h:15).  Per-column symmetric int8
+/* Replaces quant.c:10-27 (declared quant.h:15).  Per-column symmetric int8
  * quantisation of a row-major (rows, cols) f32 matrix, computed on the GPU:
  * scale[j] = max_i|w[i,j]|/127 (1 for an all-zero column),
  * q = clamp(lrintf(w * (1/scale[j])), -127, 127).  Bit-identical to the
  * reference.  Host pointers in and out. */
 void quantize_int8_percol(const float *w, int rows, int cols, signed char *q, float *scale);
 
-/* Replaces quant.c:64-68 (quant.h:16).  w[i,j] = q[i,j] * scale[j], on the GPU. */
+/* Replaces quant.c:29-33 (quant.h:16).  w[i,j] = q[i,j] * scale[j], on the GPU. */
 void dequantize_int8_percol(const signed char *q, const float *scale, int rows, int cols, float *w);
 
-/* Replace quant.c:70-85 (quant.h:28-30).  Host allocation, as in the reference. */
+/* Replace quant.c:35-50 (quant.h:28-30).  Host allocation, as in the reference. */
 QTensor qtensor_create(int rows, int cols);
 void qtensor_free(QTensor *t);
 void qtensor_quantize(QTensor *t, const float *w);
 
-/* Replaces quant.c:95-120 (quant.h:33).  C(M,N) = W8A8 product of A(M,K) with W:
+/* Replaces quant.c:60-85 (quant.h:33).  C(M,N) = W8A8 product of A(M,K) with W:
  * each row of A is quantised to int8 with its own absmax scale, multiplied
  * exactly in int32 against W's codes, and rescaled as a_scale*w_scale[j]*acc.
  * A, W and C are host memory, read and written on every call exactly like the
@@ -444,7 +444,7 @@ int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, i
 /* ---- allocation-free entry point ---- */
 
 /* No counterpart in the reference (it has no GPU).  The qmatmul product
- * (quant.c:95-120, bit-identical results) on buffers the caller already holds on
+ * (quant.c:60-85, bit-identical results) on buffers the caller already holds on
  * the current GPU, for callers that cannot call cudaMalloc where they multiply:
  * a host framework whose own memory pool already owns the GPU's memory, a plugin
  * that must not change the application's device-memory accounting, or a
@@ -453,14 +453,17 @@ int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, i
  *   A      device f32 [M][K]          Wq  device int8 [K][N], row-major (QTensor.q layout)
  *   Wscale device f32 [N]             C   device f32 [M][N], written
  *   stream a cudaStream_t (NULL: the default stream); the call only enqueues work.
- * It allocates nothing: its scratch (split-K int32 sums and counters) is one
- * fixed __device__ array of 513 KiB inside the library, held by every GPU that
- * loads it until the process exits; hence N <= 131072 (larger N is rejected with
- * LLMQ_ERR_ARG, nothing launched).  The first call on a device looks up that
- * array's address (cudaGetSymbolAddress) with the device current; make that first
- * call before any stream capture.  All calls share the array: calls that overlap
- * on the GPU (other streams, other threads) race and must be serialised by the
- * caller.  Returns 0 or an error code. */
+ * M = 0 or N = 0 enqueue nothing; K = 0 writes zeros (A and Wq may then be NULL).
+ * It allocates nothing: its scratch (split-K int32 sums, counters and the row's
+ * activation scale) is one fixed __device__ array of 513 KiB inside the library,
+ * held by every GPU that loads it until the process exits; hence N <= 131072
+ * (larger N is rejected with LLMQ_ERR_ARG, nothing launched).  Every call looks
+ * up that array's address (cudaGetSymbolAddress) with the caller's device
+ * current; the first call on a device also loads it, so make that first call
+ * before any stream capture.  All calls share the array and each clears the
+ * words it sums into: calls that overlap on the GPU (other streams, other
+ * threads) race and must be serialised by the caller.  Returns 0 or an error
+ * code. */
 int qmatmul_device_noalloc(const float *A, int M, int K, const signed char *Wq, const float *Wscale, int N,
                            float *C, void *stream);
 

@@ -1402,9 +1402,9 @@ DevKV *get_kv(DevModel *M, const LlamaKV *kv) {
 // A row-parallel product of one decode step (Wo or W2 shard, this rank's rows
 // of K), as two kernels over NVLink peer memory: k_tp_absmax forms the group's
 // absmax of the input (the reference quantises with the whole row's absmax,
-// quant.c:104-106); the GEMV then forms this rank's exact int32 partial sums
+// quant.c:69-71); the GEMV then forms this rank's exact int32 partial sums
 // and, per slab, exchanges them with the other ranks and applies
-// as * ws * sum + residual itself (quant.c:117, llama.c:578 / 589).  Integer
+// as * ws * sum + residual itself (quant.c:82, llama.c:578 / 589).  Integer
 // sums: bit-identical to one GPU.  pidx numbers the step's products.
 int row_parallel(DevModel *M, const Mat &w, const GemvPlan &p, const float *in, int pidx, cudaStream_t st) {
   TpExchange t{};
@@ -1801,7 +1801,7 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   // A row-parallel product of a tensor-parallel shard (Wo, W2: this rank's
   // rows of K), with residual epilogue into x: the rows' absmax max-reduced
   // over the ranks, codes with that scale, the exact int32 partial sums
-  // sum-reduced, then as * ws * acc + x (quant.c:104-117, llama.c:578 / 589).
+  // sum-reduced, then as * ws * acc + x (quant.c:69-82, llama.c:578 / 589).
   auto row_parallel_rows = [&](const Mat &m, const float *in) -> int {
     CK(launch_pdl(k_rows_absmax, dim3(rows), dim3(256), 0, st, in, m.K, R.tp_max));
     NK(g_nccl.AllReduce(R.tp_max, R.tp_max, (size_t)rows, ncclFloat32, ncclMax, g_tp.comm, st));

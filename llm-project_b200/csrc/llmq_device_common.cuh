@@ -11,7 +11,7 @@ namespace llmq {
 // ------------------------------------------------------- reference arithmetic
 // (int)lrintf(v) as the reference's x86-64 build evaluates it (cvtss2si to a
 // 64-bit long, then truncation to int), followed by the clamp to +-127
-// (quant.c:56-58, quant.c:109-111).
+// (quant.c:21-23, quant.c:74-76).
 __device__ __forceinline__ int8_t code_of(float v) {
   int c;
   if (fabsf(v) < 2147483648.0f) {
@@ -25,7 +25,7 @@ __device__ __forceinline__ int8_t code_of(float v) {
   c = c < -127 ? -127 : c;
   return static_cast<int8_t>(c);
 }
-// as * ws[j] * (float)acc, left to right (quant.c:117)
+// as * ws[j] * (float)acc, left to right (quant.c:82)
 __device__ __forceinline__ float dequant(float as, float ws, int acc) {
   return __fmul_rn(__fmul_rn(as, ws), __int2float_rn(acc));
 }

@@ -356,8 +356,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         for (int k = tid; k < a.K; k += kThreads) m = fmaxf(m, fabsf(xs[k]));
         m = block_max<kThreads>(m, s_red);
       }
-      const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;  // quant.c:106
-      const float inv = __fdiv_rn(1.0f, as);                      // quant.c:107
+      const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;  // quant.c:71
+      const float inv = __fdiv_rn(1.0f, as);                      // quant.c:72
       if (tid == 0) s_as[r] = as;
       int8_t *cr = codes + (size_t)r * a.Kpad;
       for (int k = tid; k < a.Kpad; k += kThreads) cr[k] = k < a.K ? code_of(__fmul_rn(xs[k], inv)) : 0;
@@ -982,7 +982,7 @@ __global__ void k_step_finish(StepState *step, unsigned long long *argmax, int *
 }
 
 // ------------------------------------------------------------ utility kernels
-// Column absmax and codes of a row-major (rows, cols) matrix (quant.c:45-62):
+// Column absmax and codes of a row-major (rows, cols) matrix (quant.c:10-27):
 // one thread per column walks the rows, so the loads of a warp are coalesced.
 __global__ void k_quantize_percol(const float *w, int rows, int cols, int8_t *q, float *scale) {
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
@@ -1069,7 +1069,7 @@ __global__ void k_repack_plain(const int8_t *src, int K, int N, int Kpad, int Np
 
 // ---------------------------------------------------- tensor parallelism
 // Absmax of a row-parallel product's input over the whole group: this rank's
-// absmax (quant.c:104-106) goes to every rank's region, the group maximum of
+// absmax (quant.c:69-71) goes to every rank's region, the group maximum of
 // all ranks' values to *out.  One CTA.
 __global__ void __launch_bounds__(kThreads) k_tp_absmax(const float *x, int n, float *out, TpExchange t, int *err) {
   __shared__ float s_red[32];

@@ -8,10 +8,11 @@
 // an allocation, and the device synchronisation of the matching cudaFree, cannot
 // be afforded.  The caller passes device pointers for A, W (the reference's
 // (in, out) row-major int8 codes plus per-column scales) and C; the only
-// scratch, the split-K int32 partial sums and the per-slab arrival counters,
-// lives in one file-scope __device__ array of fixed size.
+// scratch, the split-K int32 partial sums, the per-slab arrival counters and
+// the row's activation scale, lives in one file-scope __device__ array of
+// fixed size.
 //
-// Arithmetic is the reference's qmatmul (quant.c:95-120): per-row absmax
+// Arithmetic is the reference's qmatmul (quant.c:60-85): per-row absmax
 // activation codes, exact int32 products, c = a_scale * w_scale[j] * (float)acc.
 #include <cuda_runtime.h>
 
@@ -25,12 +26,13 @@ constexpr int kNaSlab = 256;                 // output columns per CTA
 constexpr int kNaMaxSlabs = kNaMaxN / kNaSlab;
 constexpr int kNaKChunk = 256;               // k rows per CTA (split-K)
 constexpr int kNaThreads = 256;
+constexpr int kNaScaleWord = kNaMaxN + kNaMaxSlabs;  // the row's activation scale (f32 bits)
 
-// acc[kNaMaxN] then cnt[kNaMaxSlabs]: 513 KiB, held by every GPU that loads the
-// library until the process exits.
-static __device__ __align__(256) int g_noalloc_scratch[kNaMaxN + kNaMaxSlabs];
-
-int *g_scratch_addr[64];  // host copy of the array's device address, per device
+// acc[kNaMaxN], cnt[kNaMaxSlabs], then one word for the row's activation
+// scale: 513 KiB, held by every GPU that loads the library until the process
+// exits.  Host code must not pass this name to a kernel (on the host it is only
+// a stand-in); it passes the address cudaGetSymbolAddress returns.
+static __device__ __align__(256) int g_noalloc_scratch[kNaMaxN + kNaMaxSlabs + 64];
 
 // Four rows w0..w3 of four int8 columns each -> four words, word c holding the
 // column c values of rows 0..3 (dp4a operand order).
@@ -53,26 +55,32 @@ __device__ __forceinline__ uint32_t load4(const int8_t *w, long long K, int N, l
   return v;
 }
 
+// The activation scale of one row (quant.c:69-71), computed once per row by one
+// CTA so that the product's CTAs each read only their own k rows of A.
+__global__ void __launch_bounds__(kNaThreads) k_qmm_row_scale(const float *__restrict__ a, int K, int *scratch) {
+  __shared__ float s_red[32];
+  float m = 0.0f;
+  for (int k = threadIdx.x; k < K; k += kNaThreads) m = fmaxf(m, fabsf(a[k]));
+  m = llmq::block_max<kNaThreads>(m, s_red);
+  if (threadIdx.x == 0) scratch[kNaScaleWord] = __float_as_int(m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f);
+}
+
 // One row of C.  Grid (ceil(N/256), ceil(K/256)): CTA (slab, split) multiplies
 // k rows [split*256, +256) of columns [slab*256, +256); the CTA that completes a
 // slab's splits applies the epilogue and re-zeroes the slab's scratch.
 __global__ void __launch_bounds__(kNaThreads) k_qmm_noalloc(const float *__restrict__ a, const int8_t *__restrict__ w,
                                                              const float *__restrict__ ws, float *__restrict__ c,
-                                                             int K, int N) {
-  __shared__ float s_red[32];
+                                                             int K, int N, int *scratch) {
   __shared__ __align__(16) int8_t codes[kNaKChunk];
   __shared__ int red[kNaThreads * 4];
   __shared__ int s_last;
-  int *acc = g_noalloc_scratch;
-  int *cnt = g_noalloc_scratch + kNaMaxN;
+  int *acc = scratch;
+  int *cnt = scratch + kNaMaxN;
   const int tid = threadIdx.x;
   const int slab = blockIdx.x;
   const long long k0 = (long long)blockIdx.y * kNaKChunk;
-  // activation scale over the whole row (quant.c:104-107), codes for our k rows
-  float m = 0.0f;
-  for (int k = tid; k < K; k += kNaThreads) m = fmaxf(m, fabsf(a[k]));
-  m = llmq::block_max<kNaThreads>(m, s_red);
-  const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;
+  // codes of this CTA's k rows with the row's scale (quant.c:72-78)
+  const float as = __int_as_float(scratch[kNaScaleWord]);
   const float inv = __fdiv_rn(1.0f, as);
   for (int i = tid; i < kNaKChunk; i += kNaThreads) {
     const long long k = k0 + i;
@@ -113,7 +121,7 @@ __global__ void __launch_bounds__(kNaThreads) k_qmm_noalloc(const float *__restr
   if (!s_last) return;
   __threadfence();
   for (int jj = slab * kNaSlab + tid; jj < min(N, (slab + 1) * kNaSlab); jj += kNaThreads)
-    c[jj] = llmq::dequant(as, ws[jj], atomicExch(acc + jj, 0));  // quant.c:117
+    c[jj] = llmq::dequant(as, ws[jj], atomicExch(acc + jj, 0));  // quant.c:82
   if (tid == 0) cnt[slab] = 0;
 }
 
@@ -135,34 +143,31 @@ extern "C" LLMQ_API int qmatmul_device_noalloc(const float *A, int M, int K, con
     llmq_set_error(LLMQ_ERR_ARG, "qmatmul_device_noalloc: null device pointer");
     return LLMQ_ERR_ARG;
   }
-  int dev = -1;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    llmq_set_error(LLMQ_ERR_NO_DEVICE, "qmatmul_device_noalloc: no CUDA device (%s)", cudaGetErrorString(e));
-    return LLMQ_ERR_NO_DEVICE;
-  }
-  // Set-up, once per device with that device current: the host needs the
-  // array's device address (the host-side symbol is only a stand-in).
-  if (!g_scratch_addr[dev]) {
-    int *p = nullptr;
-    e = cudaGetSymbolAddress(reinterpret_cast<void **>(&p), g_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      llmq_set_error(LLMQ_ERR_CUDA, "qmatmul_device_noalloc: cudaGetSymbolAddress failed (%s)",
-                     cudaGetErrorString(e));
-      return LLMQ_ERR_CUDA;
-    }
-    g_scratch_addr[dev] = p;
+  // The array's device address, looked up on every call with the caller's
+  // device and context current (the host-side symbol is only a stand-in).  No
+  // copy of it is kept: one taken earlier would be stale after a
+  // cudaDeviceReset or under another context, and a per-device table would be
+  // shared by the caller's threads.
+  int *scratch = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void **>(&scratch), g_noalloc_scratch);
+  if (e != cudaSuccess || !scratch) {
+    llmq_set_error(e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ? LLMQ_ERR_NO_DEVICE : LLMQ_ERR_CUDA,
+                   "qmatmul_device_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
+    return e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver ? LLMQ_ERR_NO_DEVICE : LLMQ_ERR_CUDA;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int slabs = (N + kNaSlab - 1) / kNaSlab;
   // The array keeps the last call's contents: clear the words this call sums into.
-  e = cudaMemsetAsync(g_scratch_addr[dev], 0, (size_t)slabs * kNaSlab * sizeof(int), st);
-  if (e == cudaSuccess)
-    e = cudaMemsetAsync(g_scratch_addr[dev] + kNaMaxN, 0, (size_t)slabs * sizeof(int), st);
+  e = cudaMemsetAsync(scratch, 0, (size_t)slabs * kNaSlab * sizeof(int), st);
+  if (e == cudaSuccess) e = cudaMemsetAsync(scratch + kNaMaxN, 0, (size_t)slabs * sizeof(int), st);
   const dim3 grid(slabs, K > 0 ? (K + kNaKChunk - 1) / kNaKChunk : 1);
   for (int r = 0; r < M && e == cudaSuccess; ++r) {
-    k_qmm_noalloc<<<grid, kNaThreads, 0, st>>>(A + (size_t)r * K, reinterpret_cast<const int8_t *>(Wq), Wscale,
-                                                C + (size_t)r * N, K, N);
+    const float *ar = K > 0 ? A + (size_t)r * K : A;
+    k_qmm_row_scale<<<1, kNaThreads, 0, st>>>(ar, K, scratch);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) break;
+    k_qmm_noalloc<<<grid, kNaThreads, 0, st>>>(ar, reinterpret_cast<const int8_t *>(Wq), Wscale, C + (size_t)r * N, K,
+                                                N, scratch);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess) {

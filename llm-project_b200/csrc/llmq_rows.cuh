@@ -36,7 +36,7 @@ struct RowNormArgs {
 };
 
 // RMSNorm of one row (rmsnorm.c:7-21, the arithmetic of k_gemv's RMSNorm
-// prologue), then its activation codes (quant.c:104-113).  One CTA per row;
+// prologue), then its activation codes (quant.c:69-78).  One CTA per row;
 // dynamic shared memory 2 * K floats.
 __global__ void __launch_bounds__(kRowThreads) k_rows_norm_codes(const RowNormArgs a) {
   extern __shared__ __align__(16) float xs[];
@@ -80,8 +80,8 @@ __global__ void __launch_bounds__(kRowThreads) k_rows_norm_codes(const RowNormAr
   }
   m = block_max<kRowThreads>(m, s_red);
   __syncthreads();
-  const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;  // quant.c:106
-  const float inv = __fdiv_rn(1.0f, as);                      // quant.c:107
+  const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;  // quant.c:71
+  const float inv = __fdiv_rn(1.0f, as);                      // quant.c:72
   if (tid == 0) a.as[r] = as;
   for (int ch = tid; ch < a.Kpad / 16; ch += kRowThreads)
     *reinterpret_cast<int4 *>(a.codes + tc_code_offset(r, ch, a.Kpad, a.KT)) = tc_pack16(xs, ch * 16, K, inv);

@@ -3,7 +3,7 @@
  * Element e of tensor t is drawn from N(0, stddev): splitmix64 (Vigna) keyed by
  * (seed, t) gives two uniforms per element pair (e>>1), Box-Muller turns them
  * into two normals (cos half for even e, sin half for odd e).  2-D tensors are
- * then quantised per column with the reference rule of quant.c:45-62.  Work is
+ * then quantised per column with the reference rule of quant.c:10-27.  Work is
  * split over column strips across threads; every value depends only on
  * (seed, t, e), so the model is the same for any thread count.
  */
@@ -45,7 +45,7 @@ static float draw(uint64_t key, uint64_t e, float stddev) {
   return (float)((double)stddev * ((e & 1) ? z1 : z0));
 }
 
-/* quant.c:56-58 */
+/* quant.c:21-23 */
 static signed char code_of(float v) {
   int c = (int)lrintf(v);
   if (c > 127) c = 127;

@@ -1,7 +1,7 @@
 // llmq_tc_gemm.cuh - the W8A8 product for 64..128 activation rows per launch
 // on the 5th-generation tensor cores: tcgen05.mma.kind::i8, int8 x int8 with
 // int32 accumulators in tensor memory (TMEM).  Integer sums are exact, so the
-// result equals the reference's qmatmul (quant.c:95-120) bit for bit.
+// result equals the reference's qmatmul (quant.c:60-85) bit for bit.
 //
 // Operands, both K-major without swizzle (the canonical core-matrix layout:
 // 8 rows x 16 bytes per 128-byte core matrix):
@@ -77,7 +77,7 @@ __device__ __forceinline__ size_t tc_code_offset(int m, int chunk, int Kpad, int
 }
 
 // Codes of 16 consecutive values x[0..16) (k >= K gives 0) times `inv`
-// (quant.c:108-112), packed little-endian into one 16-byte chunk.
+// (quant.c:73-77), packed little-endian into one 16-byte chunk.
 __device__ __forceinline__ int4 tc_pack16(const float *x, int k0, int K, float inv) {
   uint32_t w[4];
 #pragma unroll
@@ -94,7 +94,7 @@ __device__ __forceinline__ int4 tc_pack16(const float *x, int k0, int K, float i
   return make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);
 }
 
-// Per-row activation quantisation (quant.c:104-113) of rows [0, rows) of a
+// Per-row activation quantisation (quant.c:69-78) of rows [0, rows) of a
 // (row stride K), written as tcgen05 A tiles; the row's absmax comes from
 // absmax_in when given.  One CTA per row.
 __global__ void __launch_bounds__(256) k_act_codes(const float *a, int rows, int K, int Kpad, int KT, int8_t *codes,
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(256) k_act_codes(const float *a, int rows, int
 }
 
 // Absmax of each row of a (row stride K), the local part of a row-parallel
-// product's activation scale (quant.c:104-106).  One CTA per row.
+// product's activation scale (quant.c:69-71).  One CTA per row.
 __global__ void __launch_bounds__(256) k_rows_absmax(const float *a, int K, float *out) {
   __shared__ float s_red[32];
   pdl_launch_dependents();
@@ -133,7 +133,7 @@ __global__ void __launch_bounds__(256) k_rows_absmax(const float *a, int K, floa
 }
 
 // ------------------------------------------------------------------- GEMM
-// Epilogues applied to y = a_scale[m] * w_scale[p] * acc (quant.c:117) of
+// Epilogues applied to y = a_scale[m] * w_scale[p] * acc (quant.c:82) of
 // physical column p of the tiled matrix.
 enum TcEpilogue : int {
   TC_PLAIN = 0,   // out[m][p] = y                                  (qmatmul)

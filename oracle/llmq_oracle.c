@@ -14,7 +14,7 @@
 #include <unistd.h>
 
 /* The reference's code rounding: (int)lrintf(v) then clamp to +-127
- * (quant.c:56-58 and quant.c:109-111 use the same three steps). */
+ * (quant.c:21-23 and quant.c:74-76 use the same three steps). */
 static signed char code_of(float v) {
   int c = (int)lrintf(v);
   if (c > 127) c = 127;
@@ -23,7 +23,7 @@ static signed char code_of(float v) {
 }
 
 void orc_quantize_int8_percol(const float *w, int rows, int cols, signed char *q, float *scale) {
-  /* quant.c:45-62: column absmax, s = mx/127 (1 if zero), codes use 1/s. */
+  /* quant.c:10-27: column absmax, s = mx/127 (1 if zero), codes use 1/s. */
   for (int j = 0; j < cols; j++) {
     float amax = 0.0f;
     for (int i = 0; i < rows; i++) {
@@ -38,13 +38,13 @@ void orc_quantize_int8_percol(const float *w, int rows, int cols, signed char *q
 }
 
 void orc_dequantize_int8_percol(const signed char *q, const float *scale, int rows, int cols, float *w) {
-  /* quant.c:64-68 */
+  /* quant.c:29-33 */
   for (int i = 0; i < rows; i++)
     for (int j = 0; j < cols; j++) w[(size_t)i * cols + j] = (float)q[(size_t)i * cols + j] * scale[j];
 }
 
 float orc_quantize_row(const float *a, int K, signed char *qa) {
-  /* quant.c:104-113 */
+  /* quant.c:69-78 */
   float amax = 0.0f;
   for (int k = 0; k < K; k++) {
     const float t = fabsf(a[k]);
@@ -68,7 +68,7 @@ void orc_qacc_columns(const signed char *qa, const signed char *qw, int K, int N
 
 void orc_qmatmul(const float *A, int M, int K, const signed char *wq, const float *wscale, int N,
                  float *C) {
-  /* quant.c:95-120: per row: quantise, int32 accumulate, c = as * ws[j] * acc. */
+  /* quant.c:60-85: per row: quantise, int32 accumulate, c = as * ws[j] * acc. */
   signed char *qa = (signed char *)malloc((size_t)K > 0 ? (size_t)K : 1);
   int32_t *acc = (int32_t *)malloc(((size_t)N > 0 ? (size_t)N : 1) * sizeof(int32_t));
   for (int m = 0; m < M; m++) {

@@ -20,15 +20,15 @@
 extern "C" {
 #endif
 
-/* quant.c:45-62 */
+/* quant.c:10-27 */
 void orc_quantize_int8_percol(const float *w, int rows, int cols, signed char *q, float *scale);
-/* quant.c:64-68 */
+/* quant.c:29-33 */
 void orc_dequantize_int8_percol(const signed char *q, const float *scale, int rows, int cols, float *w);
-/* quant.c:104-113: per-row activation quantisation; returns the row scale. */
+/* quant.c:69-78: per-row activation quantisation; returns the row scale. */
 float orc_quantize_row(const float *a, int K, signed char *qa);
 /* matrix.c:354-374: acc[j] = sum_k qa[k]*qw[k*N+j] (int32). */
 void orc_qacc_columns(const signed char *qa, const signed char *qw, int K, int N, int32_t *acc);
-/* quant.c:95-120 on raw pointers: A (M,K) f32, W codes (K,N) + scale[N], C (M,N). */
+/* quant.c:60-85 on raw pointers: A (M,K) f32, W codes (K,N) + scale[N], C (M,N). */
 void orc_qmatmul(const float *A, int M, int K, const signed char *wq, const float *wscale, int N,
                  float *C);
 /* rmsnorm.c:7-21 for one row. */

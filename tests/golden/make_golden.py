@@ -13,7 +13,8 @@ oracle/Makefile) on:
   * mini.*       - a larger randomised model (non-zero biases, rope_base 5e5)
                    decoded greedily from a 16-id prompt to position 300: every
                    argmax id, and the logits at selected steps
-Usage: python tests/golden/make_golden.py   (needs /root/reference, built oracle/)
+Usage: python tests/golden/make_golden.py
+(needs oracle/_ref/ built from the reference sources: make -C oracle REF=<reference checkout>)
 """
 from __future__ import annotations
 

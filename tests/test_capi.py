@@ -125,7 +125,7 @@ def test_synth_is_seeded_and_follows_the_quantisation_rule(lib):
     qa, _ = llmq.qtensor_arrays(a.blocks[0].Wq)
     qc, _ = llmq.qtensor_arrays(c.blocks[0].Wq)
     assert not np.array_equal(qa, qc)
-    # per-column absmax maps to +-127 exactly (quant.c:52-58)
+    # per-column absmax maps to +-127 exactly (quant.c:17-23)
     for name in ("Wq", "Wk", "Wv", "Wo", "Wgate", "Wup", "Wdown"):
         q, s = llmq.qtensor_arrays(getattr(a.blocks[0], name))
         assert np.all(np.abs(q).max(axis=0) == 127), name
