@@ -441,6 +441,15 @@ int llmq_bench_qmatmul(const QTensor *W, int M, int iters, float *ms);
  * kernels do not overlap here.  Returns 0 or an error code. */
 int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, int max_n);
 
+/* Failure detection on one GPU (no reference counterpart): runs a two-rank
+ * tensor-parallel exchange whose second rank is a local region nothing writes,
+ * so the peer-flag waits give up after `polls` polls.  which 0: the absmax
+ * exchange kernel; 1: the row-parallel GEMV.  The kernel returns by itself;
+ * *err_word receives the device error word (1 = timeout) and *ms its duration.
+ * Returns LLMQ_ERR_CUDA when the error word is set (as a decode step does),
+ * else 0; frees everything it allocated. */
+int llmq_tp_wait_timeout_check(int which, unsigned polls, int *err_word, float *ms);
+
 /* ---- allocation-free entry point ---- */
 
 /* No counterpart in the reference (it has no GPU).  The qmatmul product

@@ -2659,3 +2659,111 @@ extern "C" LLMQ_API int llmq_bench_qmatmul(const QTensor *W, int M, int iters, f
   free_mat(m);
   return rc;
 }
+
+// Failure detection on one GPU: drives the tensor-parallel peer-flag waits to
+// their limit.  A two-rank exchange is set up whose second "rank" is a local
+// region that nothing writes, so every wait on that rank's flag gives up after
+// `polls` polls (0 would be the production bound of about a second; the test
+// passes a few thousand).  which 0: k_tp_absmax (the absmax exchange); 1: the
+// row-parallel GEMV (EPI_TP_RESID) on a 512 x 512 matrix, whose slab-completing
+// CTAs wait for the missing rank's partial sums.  The kernel must return by
+// itself: *err_word receives the device error word (ERR_TIMEOUT expected) and
+// *ms the kernel's duration.  Returns LLMQ_ERR_CUDA when the error word is set,
+// as the decode path does, LLMQ_OK when it is not; everything the check
+// allocated is freed, and the device stays usable.
+extern "C" LLMQ_API int llmq_tp_wait_timeout_check(int which, unsigned polls, int *err_word, float *ms) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevCtx *c = get_ctx();
+  if (!c) return q_llama_last_error();
+  if ((which != 0 && which != 1) || polls == 0 || !err_word || !ms) {
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_tp_wait_timeout_check: bad arguments");
+    return LLMQ_ERR_ARG;
+  }
+  constexpr int kW = 2, kDm = 512, kK = 512;
+  const size_t rb = tpx_bytes(kW, kDm);
+  char *region[kW] = {nullptr, nullptr};
+  char **peers = nullptr;
+  unsigned *seq = nullptr;
+  int *err = nullptr, *acc = nullptr, *cnt = nullptr;
+  float *x = nullptr, *out = nullptr;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  Mat m;
+  int rc = LLMQ_OK;
+  std::vector<float> hx(kK);
+  for (int k = 0; k < kK; ++k) hx[k] = (float)((k * 37) % 101 - 50) * 0.03125f;
+  std::vector<signed char> hq((size_t)kK * kDm);
+  for (size_t i = 0; i < hq.size(); ++i) hq[i] = (signed char)((int)((i * 2654435761u) >> 24) % 255 - 127);
+  std::vector<float> hs(kDm, 0.004f);
+  QTensor W{kK, kDm, hq.data(), hs.data()};
+  bool ok = cudaMalloc(&region[0], rb) == cudaSuccess && cudaMalloc(&region[1], rb) == cudaSuccess &&
+            cudaMemset(region[0], 0, rb) == cudaSuccess && cudaMemset(region[1], 0, rb) == cudaSuccess &&
+            cudaMalloc(&peers, sizeof(region)) == cudaSuccess &&
+            cudaMemcpy(peers, region, sizeof(region), cudaMemcpyHostToDevice) == cudaSuccess &&
+            cudaMalloc(&seq, sizeof(unsigned)) == cudaSuccess && cudaMemset(seq, 0, sizeof(unsigned)) == cudaSuccess &&
+            cudaMalloc(&err, sizeof(int)) == cudaSuccess && cudaMemset(err, 0, sizeof(int)) == cudaSuccess &&
+            cudaMalloc(&x, kK * sizeof(float)) == cudaSuccess &&
+            cudaMemcpy(x, hx.data(), kK * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess &&
+            cudaMalloc(&out, kDm * sizeof(float)) == cudaSuccess && cudaMemset(out, 0, kDm * sizeof(float)) == cudaSuccess;
+  ok = ok && build_plain(m, W, 1);
+  GemvPlan plan;
+  ok = ok && plan_gemv(*c, m, PRO_ABSMAX, 1, plan);
+  ok = ok && cudaMalloc(&acc, (size_t)m.Npad * sizeof(int)) == cudaSuccess &&
+       cudaMemset(acc, 0, (size_t)m.Npad * sizeof(int)) == cudaSuccess &&
+       cudaMalloc(&cnt, (size_t)m.n_slabs * sizeof(int)) == cudaSuccess &&
+       cudaMemset(cnt, 0, (size_t)m.n_slabs * sizeof(int)) == cudaSuccess;
+  if (!ok) {
+    if (q_llama_last_error() == LLMQ_OK) llmq_set_error(LLMQ_ERR_OOM, "llmq_tp_wait_timeout_check: set-up failed");
+    rc = q_llama_last_error();
+  } else {
+    TpExchange t{};
+    t.peers = peers;
+    t.seq = seq;
+    t.rank = 0;
+    t.world = kW;
+    t.dm = kDm;
+    t.pidx = 0;
+    t.poll_limit = polls;
+    cudaStream_t st = c->stream;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, st);
+    cudaError_t e;
+    if (which == 0) {
+      k_tp_absmax<<<1, kThreads, 0, st>>>(x, kK, out, t, err);
+      e = cudaGetLastError();
+    } else {
+      GemvArgs a = base_args(m, plan, acc, cnt, err);
+      a.in = x;
+      a.out = out;
+      a.tp = t;
+      e = launch_gemv<PRO_ABSMAX, EPI_TP_RESID, 1>(a, plan, st, false);
+    }
+    cudaEventRecord(e1, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+      llmq_set_error(LLMQ_ERR_CUDA, "llmq_tp_wait_timeout_check: %s", cudaGetErrorString(e));
+      rc = LLMQ_ERR_CUDA;
+    } else {
+      cudaEventElapsedTime(ms, e0, e1);
+      cudaMemcpy(err_word, err, sizeof(int), cudaMemcpyDeviceToHost);
+      if (*err_word) {
+        llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: device reported error flags 0x%x (peer flag wait gave up)",
+                       *err_word);
+        rc = LLMQ_ERR_CUDA;
+      }
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+  }
+  cudaFree(region[0]);
+  cudaFree(region[1]);
+  cudaFree(peers);
+  cudaFree(seq);
+  cudaFree(err);
+  cudaFree(x);
+  cudaFree(out);
+  cudaFree(acc);
+  cudaFree(cnt);
+  free_mat(m);
+  return rc;
+}

@@ -182,6 +182,7 @@ struct TpExchange {
   char *const *peers;      // [W] region base of every rank, this rank's own included
   const unsigned *seq;     // products completed before this step
   int rank, world, dm, pidx;  // pidx: the product's index within the step (epoch = *seq + pidx + 1)
+  unsigned poll_limit;     // polls before a flag wait gives up (0: kFlagPolls)
 };
 __host__ __device__ inline size_t tpx_data_off() { return 0; }
 __host__ __device__ inline size_t tpx_amax_off(int W, int dm) { return (size_t)2 * W * dm * 4; }
@@ -201,9 +202,13 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
 __device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Bounded wait until *p >= epoch; false after ~2^24 polls (about a second).
-__device__ __forceinline__ bool wait_flag(const unsigned *p, unsigned epoch) {
-  for (uint32_t it = 0; it < (1u << 24); ++it) {
+// Bounded wait until *p >= epoch; false after `limit` polls (0: kFlagPolls,
+// 2^24 polls of ~32 ns sleep each, about a second).  A wait that gives up
+// leaves the kernel to record ERR_TIMEOUT and return.
+constexpr uint32_t kFlagPolls = 1u << 24;
+__device__ __forceinline__ bool wait_flag(const unsigned *p, unsigned epoch, uint32_t limit) {
+  const uint32_t n = limit ? limit : kFlagPolls;
+  for (uint32_t it = 0; it < n; ++it) {
     if (ld_acquire_u32(p) >= epoch) return true;
     __nanosleep(32);
   }
@@ -468,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       if (tid < x.world) {
         st_release_u32(reinterpret_cast<unsigned *>(x.peers[tid] + fs) + (size_t)slab * x.world + x.rank, epoch);
         const unsigned *own = reinterpret_cast<const unsigned *>(x.peers[x.rank] + fs) + (size_t)slab * x.world + tid;
-        if (!wait_flag(own, epoch)) {
+        if (!wait_flag(own, epoch, x.poll_limit)) {
           atomicOr(a.err, ERR_TIMEOUT);
           s_abort = 1;
         }
@@ -1089,7 +1094,8 @@ __global__ void __launch_bounds__(kThreads) k_tp_absmax(const float *x, int n, f
     reinterpret_cast<float *>(peer + ao)[par * t.world + t.rank] = m;
     __threadfence_system();
     st_release_u32(reinterpret_cast<unsigned *>(peer + fo) + t.rank, epoch);
-    if (!wait_flag(reinterpret_cast<const unsigned *>(t.peers[t.rank] + fo) + threadIdx.x, epoch)) s_bad = 1;
+    if (!wait_flag(reinterpret_cast<const unsigned *>(t.peers[t.rank] + fo) + threadIdx.x, epoch, t.poll_limit))
+      s_bad = 1;
   }
   __syncthreads();
   if (threadIdx.x == 0) {

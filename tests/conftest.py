@@ -17,6 +17,16 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 GOLDEN = os.path.join(ROOT, "tests", "golden")
 
 
+def reference_dir() -> str | None:
+    """The reference checkout ($LLMQ_REFERENCE_DIR, else a directory named
+    `reference` beside this repository) when it is present; None elsewhere
+    (the GPU box has none)."""
+    for d in (os.environ.get("LLMQ_REFERENCE_DIR"), os.path.join(os.path.dirname(ROOT), "reference")):
+        if d and os.path.exists(os.path.join(d, "llama.h")):
+            return d
+    return None
+
+
 def has_gpu() -> bool:
     return os.path.exists("/dev/nvidiactl") or os.path.exists("/dev/nvidia0")
 

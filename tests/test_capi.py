@@ -138,3 +138,18 @@ def test_synth_is_seeded_and_follows_the_quantisation_rule(lib):
     np.testing.assert_array_equal(llmq.vec_array(a.blocks[0].attn_norm), 1.0)
     for m in (a, b, c):
         lib.q_llama_model_free(C.byref(m))
+
+
+def test_link_check_compiles_against_the_reference_headers(tmp_path):
+    """A C caller that includes the reference's own tensor.h, quant.h, llama.h
+    and sampler.h, then llmq_cuda.h, compiles with -Werror (every shared
+    declaration agrees, the include guards interlock) and links against
+    libllmq_cuda.so alone (every call resolves in this library)."""
+    from conftest import reference_dir
+    ref = reference_dir()
+    if ref is None:
+        pytest.skip("no reference checkout on this machine")
+    r = subprocess.run(["make", "-C", os.path.join(ROOT, "tests"), f"REF={ref}", f"OUT={tmp_path}"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert os.access(tmp_path / "link_check", os.X_OK)

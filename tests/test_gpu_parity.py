@@ -60,6 +60,8 @@ def test_dequantize_bit_exact(lib, orc):
 @pytest.mark.parametrize("M,K,N", [(1, 1, 1), (1, 16, 256), (2, 37, 19), (3, 100, 300), (1, 288, 32000),
                                    (8, 768, 288), (9, 64, 1000), (17, 288, 96), (1, 4096, 4096),
                                    (1, 14336, 4096), (4, 4096, 1024),
+                                   # 8 rows at K = 14336: the GEMV's 16 KB tiles (KT = 64)
+                                   (8, 14336, 4096), (8, 28672, 1024),
                                    # tcgen05 tensor-core path (M > 8): one and several 128-row blocks
                                    (64, 4096, 4096), (128, 4096, 1024), (200, 768, 300), (256, 4096, 4096), (64, 14336, 1024),
                                    (33, 37, 19), (64, 4096, 14336)])
@@ -140,6 +142,47 @@ def test_decode_8b_shapes_two_layers_vs_oracle(lib, orc):
     ologits, _ = orc_decode(orc, m, ids)
     glogits, _ = gpu_decode(lib, m, ids)
     assert bits_equal(glogits, ologits)
+    lib.q_llama_model_free(C.byref(m))
+
+
+def test_70b_shapes_two_layers_vs_oracle(lib, orc):
+    """LLaMA-3-70B layer and head shapes (dm 8192, GQA 64/8, hd 128, dff 28672,
+    vocab 128256, rope 5e5) with 2 layers: the 8192-term RMSNorm chains, the
+    28672-deep W2 product and the 8-head query groups.  Single-sequence steps,
+    a prefill and a 3-row batched step, all against the oracle's sequential
+    decode, bit for bit."""
+    cfg = dict(vocab=128256, d_model=8192, n_layers=2, n_heads=64, n_kv=8, head_dim=128, d_ff=28672,
+               max_seq=32, rope_base=500000.0, eps=1e-5)
+    m = synth(lib, cfg, seed=4321)
+    ids = [17, 128000, 42, 9999, 5]
+    # oracle: the five ids, then one more step of token 77 on the same cache
+    okv = orc.orc_kv_create(C.byref(m))
+    want = np.zeros((len(ids) + 1, cfg["vocab"]), np.float32)
+    for i, tok in enumerate(ids + [77]):
+        orc.orc_decode_step(C.byref(m), C.byref(okv), int(tok), fp(want[i]))
+    orc.orc_kv_free(C.byref(okv))
+    # single-sequence steps
+    kv1 = lib.q_llama_kv_create(C.byref(m))
+    got, _ = gpu_decode(lib, m, ids, kv=kv1)
+    assert bits_equal(got, want[:len(ids)])
+    # a prefill of the first four ids (logits of the last row)
+    kv2 = lib.q_llama_kv_create(C.byref(m))
+    row = np.zeros((1, cfg["vocab"]), np.float32)
+    t = llmq.host_tensor(row)
+    lib.q_llama_prefill(C.byref(m), C.byref(kv2), llmq.int_array(ids[:4]), 4, C.byref(t))
+    llmq.check(lib)
+    assert bits_equal(row[0], want[3])
+    # one batched step of three sequences at positions 5, 4 and 0
+    kv3 = lib.q_llama_kv_create(C.byref(m))
+    out = np.zeros((3, cfg["vocab"]), np.float32)
+    to = llmq.host_tensor(out)
+    lib.q_llama_decode_batch(C.byref(m), llmq.kv_pointers([kv1, kv2, kv3]), llmq.int_array([77, ids[4], ids[0]]), 3,
+                             C.byref(to))
+    llmq.check(lib)
+    assert bits_equal(out[0], want[5]) and bits_equal(out[1], want[4]) and bits_equal(out[2], want[0])
+    assert (kv1.len, kv2.len, kv3.len) == (6, 5, 1)
+    for kv in (kv1, kv2, kv3):
+        lib.llama_kv_free(C.byref(kv))
     lib.q_llama_model_free(C.byref(m))
 
 

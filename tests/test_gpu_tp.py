@@ -1,4 +1,5 @@
-"""Tensor parallelism on 2 GPUs: every rank holds its shard (llmq_synth_model_shard)
+"""Tensor parallelism on 2, 4 and 8 GPUs (as many as the machine has): every
+rank holds its shard (llmq_synth_model_shard)
 and the group decodes as one model; logits and greedy ids must equal the
 oracle's single-sequence decode of the whole model bit for bit
 (tests/tp_worker.py does the work, one process per GPU)."""
@@ -21,14 +22,15 @@ def gpu_count() -> int:
     return torch.cuda.device_count()
 
 
-def test_tp2_decode_matches_oracle(tmp_path):
-    if gpu_count() < 2:
-        pytest.skip("tensor parallelism needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_decode_matches_oracle(tmp_path, world):
+    if gpu_count() < world:
+        pytest.skip(f"tensor parallelism over {world} ranks needs {world} GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     cmd = ["timeout", "-k", "30", "900", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+           f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(port),
            os.path.join(HERE, "tp_worker.py"), str(tmp_path)]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)

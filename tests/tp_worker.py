@@ -1,11 +1,12 @@
-"""One rank of the 2-GPU tensor-parallel parity check run by test_gpu_tp.py
-(launched with torch.distributed.run, one process per GPU).
+"""One rank of the tensor-parallel parity check run by test_gpu_tp.py
+(launched with torch.distributed.run, one process per GPU, 2, 4 or 8 ranks).
 
 Every rank decodes its shard of the same synthetic model; rank 0 compares the
 whole logits rows (gathered by the library on every rank), the greedy ids of
 q_llama_generate and the sampled ids of q_llama_generate_sample with the
 oracle's single-sequence decode of the whole model, bit for bit, and writes the
-verdicts to <out_dir>/tp.json."""
+verdicts to <out_dir>/tp.json.  The cases are those whose heads, KV heads, d_ff
+and vocabulary divide by the group size (8 KV heads: one per rank at 8)."""
 from __future__ import annotations
 
 import ctypes as C
@@ -25,11 +26,20 @@ import llmq  # noqa: E402
 import oracle  # noqa: E402
 from helpers import TINY, bits_equal, fp, orc_decode, orc_sample, synth  # noqa: E402
 
+# GQA 16/8, hd 32, with biases: shards at 2, 4 and 8 ranks
+GQA8 = dict(vocab=32000, d_model=512, n_layers=3, n_heads=16, n_kv=8, head_dim=32, d_ff=1024, max_seq=128,
+            rope_base=10000.0, eps=1e-5)
+
 CASES = [
     ("tiny_bias", TINY, True, [5, 77, 31999, 0, 1234, 42, 9, 17, 256, 3000]),
+    ("gqa8_bias", GQA8, True, [5, 77, 31999, 0, 1234, 42, 9, 17]),
     ("8b_shapes_2_layers", dict(vocab=128256, d_model=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128,
                                 d_ff=14336, max_seq=64, rope_base=500000.0, eps=1e-5), False, [17, 128000, 42]),
 ]
+
+
+def shardable(cfg, world):
+    return all(cfg[k] % world == 0 for k in ("n_heads", "n_kv", "d_ff", "vocab"))
 
 
 def main():
@@ -42,6 +52,8 @@ def main():
     llmq.tp_bootstrap(lib, rank, world)
     verdicts = {}
     for name, cfg, bias, ids in CASES:
+        if not shardable(cfg, world):
+            continue
         sh = llmq.synth_shard(lib, cfg, 1234, rank, world, with_bias=bias)
         kv = lib.q_llama_kv_create(C.byref(sh))
         llmq.check(lib)
@@ -91,7 +103,8 @@ def main():
     # batched passes on the shards: three prompts of different lengths
     # prefilled, then three batched steps with logits; every row equals the
     # oracle's single-sequence decode of the whole model
-    cfg = TINY
+    cfg = TINY if shardable(TINY, world) else GQA8
+    bname = "tiny_bias" if cfg is TINY else "gqa8_bias"
     sh = llmq.synth_shard(lib, cfg, 1234, rank, world, with_bias=True)
     rng = np.random.default_rng(9)
     lens, steps = [5, 1, 12], 3
@@ -118,8 +131,8 @@ def main():
             want, _ = orc_decode(orc, full, sq)
             ok_rows &= bits_equal(got[b], want[n:])
             ok_first &= firsts[b] == int(np.argmax(want[n - 1]))
-        verdicts["tiny_bias.batch_logits"] = bool(ok_rows)
-        verdicts["tiny_bias.prefill_ids"] = bool(ok_first)
+        verdicts[bname + ".batch_logits"] = bool(ok_rows)
+        verdicts[bname + ".prefill_ids"] = bool(ok_first)
         lib.q_llama_model_free(C.byref(full))
     dist.barrier()
     for kv in kvs:
