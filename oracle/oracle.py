@@ -1,6 +1,8 @@
 """TEST INFRASTRUCTURE ONLY: Python access to the CPU checkers.
 
 * `load_oracle()`: our C restatement of the reference path (llmq_oracle.c).
+* `load_synth()`: the seeded synthetic-model generator built on its own
+  (oracle/_build/libsynth.so), the reference arm's input maker.
 * `load_reference()`: the reference's own quant.c / matrix.c / llama.c /
   rmsnorm.c / rope.c / gqa.c / swiglu.c / tensor.c / sampler.c, compiled here
   by oracle/Makefile into oracle/_ref/ (None when not built).
@@ -24,6 +26,7 @@ from llmq import (LlamaKV, LlamaModel, QLlamaModel, QTensor, Rng, Tensor, c_byte
                   c_float_p, c_int_p)
 
 ORACLE_PATH = os.path.join(HERE, "_build", "liboracle.so")
+SYNTH_PATH = os.path.join(HERE, "_build", "libsynth.so")
 REF_DIR = os.path.join(HERE, "_ref")
 
 
@@ -117,6 +120,27 @@ def load_oracle() -> C.CDLL:
             raise FileNotFoundError(f"{ORACLE_PATH} not built (make -C oracle)")
         _cache["orc"] = _bind(C.CDLL(ORACLE_PATH), _ORC_SIGS)
     return _cache["orc"]
+
+
+_SYNTH_SIGS = {
+    "llmq_synth_model": (C.c_int, [C.POINTER(llmq.LlmqConfig), C.c_uint64, C.c_float, C.c_int,
+                                   C.POINTER(QLlamaModel)]),
+    "llmq_synth_model_fast_shard": (C.c_int, [C.POINTER(llmq.LlmqConfig), C.c_uint64, C.c_int, C.c_int,
+                                              C.POINTER(QLlamaModel)]),
+    "llmq_synth_qtensor": (None, [C.POINTER(QTensor), C.c_uint64]),
+    "qtensor_create": (QTensor, [C.c_int, C.c_int]),
+}
+
+
+def load_synth() -> C.CDLL:
+    """The synthetic-model generator without the product library: the same
+    source (llmq_synth.c) built into oracle/_build/libsynth.so.  Its models are
+    malloc'd like the reference's, so ref.q_llama_model_free releases them."""
+    if "synth" not in _cache:
+        if not os.path.exists(SYNTH_PATH):
+            raise FileNotFoundError(f"{SYNTH_PATH} not built (make -C oracle)")
+        _cache["synth"] = _bind(C.CDLL(SYNTH_PATH), _SYNTH_SIGS)
+    return _cache["synth"]
 
 
 def load_reference() -> C.CDLL | None:

@@ -64,3 +64,31 @@ def test_warmup_below_three_is_refused():
     r = subprocess.run([sys.executable, BENCH, "--impl", "reference", "--workload", "tiny", "--steps", "2",
                         "--warmup", "2"], capture_output=True, text=True, timeout=300, cwd=ROOT)
     assert r.returncode != 0 and "warmup" in r.stderr
+
+
+def test_reference_arm_maps_no_library_of_ours(have_reference):
+    """The reference arm builds its inputs with oracle/_build/libsynth.so and
+    runs oracle/_ref alone: libllmq_cuda.so is never mapped into its process."""
+    code = ("import runpy, sys\n"
+            f"sys.argv = ['bench.py'] + {ARGS!r}\n"
+            f"runpy.run_path({BENCH!r}, run_name='__main__')\n"
+            "maps = open('/proc/self/maps').read()\n"
+            "print('MAPPED', 'libllmq_cuda' in maps, 'libllmq_ref' in maps)\n")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300, cwd=ROOT)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert "MAPPED False True" in r.stdout
+
+
+def test_both_arms_print_the_same_config():
+    """Both arms take their batch-1 `config` from one function."""
+    sys.path.insert(0, ROOT)
+    import argparse
+
+    import bench
+    args = argparse.Namespace(workload="8b", prompt=0)
+    wl = bench.WORKLOADS["8b"]
+    a = bench.bs1_config(args, wl, 512, 5, 20, 1)
+    assert a == bench.bs1_config(args, wl, 512, 5, 20, 1)
+    assert a["kv_len_start"] == 517 and a["kv_len_end"] == 537 and "seeded" in a["prompt_cache"]
+    src = open(BENCH).read()
+    assert src.count('"config": bs1_config(args, wl, P, W, K, world)') == 2
