@@ -283,14 +283,15 @@ def run_ours(args, rank, world):
     g_bytes, g_ms, per_kind = 0.0, 0.0, {}
     for which, count in kinds:
         msl, by = C.c_float(), C.c_double()
-        if lib.llmq_bench_gemv(C.byref(m), which, 0, 20, C.byref(msl), C.byref(by)) != 0:
+        # one launch per layer (different weights each time), from one CUDA graph
+        if lib.llmq_bench_gemv(C.byref(m), which, 0, cfg["n_layers"], C.byref(msl), C.byref(by)) != 0:
             llmq.check(lib)
         g_bytes += count * by.value
         g_ms += count * msl.value
         per_kind[["qkv", "wo", "w13", "w2", "lm_head"][which]] = {
             "ms": round(msl.value, 5), "GBps": round(by.value / msl.value / 1e6, 1)}
     msl, by = C.c_float(), C.c_double()
-    if lib.llmq_bench_gemv(C.byref(m), 5, 0, 20, C.byref(msl), C.byref(by)) != 0:
+    if lib.llmq_bench_gemv(C.byref(m), 5, 0, cfg["n_layers"], C.byref(msl), C.byref(by)) != 0:
         llmq.check(lib)
     per_kind["attention"] = {"ms": round(msl.value, 5), "GBps": round(by.value / msl.value / 1e6, 1)}
     peaks = measured_peaks()

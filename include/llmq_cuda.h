@@ -409,8 +409,11 @@ int llmq_expf_device(const float *x, float *y, long long n);
 
 /* Times `iters` back-to-back launches of one kernel of an uploaded model
  * (which: 0 fused QKV, 1 Wo, 2 fused W1|W3, 3 W2, 4 lm-head GEMV, 5 attention
- * over the first KV cache at its current position; `layer` selects the block)
- * with CUDA events on the model's stream.  *ms_per_launch receives the mean
+ * over the first KV cache at its current position) with CUDA events on the
+ * model's stream.  Launch i takes block (layer + i) mod n_layers, so
+ * consecutive launches stream different weights; the launches are replayed
+ * from one CUDA graph with programmatic dependent launch, as inside a decode
+ * step, so the host's launch rate is not timed.  *ms_per_launch receives the mean
  * launch time and *bytes_per_launch the algorithmic bytes of one launch (GEMV:
  * int8 weights + f32 scales + f32 input + f32 output; attention: the K and V
  * rows read plus q and the output).  Returns 0 or an error code. */
@@ -440,6 +443,13 @@ int llmq_bench_qmatmul(const QTensor *W, int M, int iters, float *ms);
  * kv->len like a decode step.  For attributing step time to kernels; the
  * kernels do not overlap here.  Returns 0 or an error code. */
 int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, int max_n);
+
+/* RMSNorm of the row x[W->rows] with gain gamma and epsilon eps
+ * (rmsnorm.c:7-21), then qmatmul of the normalised row by W (quant.c:60-85):
+ * out[W->cols], host arrays, computed by the GEMV with the RMSNorm prologue that
+ * QKV, W1|W3 and the lm-head use in a decode step (for tests on chosen rows).
+ * Returns 0 or an error code. */
+int llmq_rmsnorm_qmatmul(const float *x, const float *gamma, float eps, const QTensor *W, float *out);
 
 /* Failure detection on one GPU (no reference counterpart): runs a two-rank
  * tensor-parallel exchange whose second rank is a local region nothing writes,

@@ -42,6 +42,22 @@ namespace {
 constexpr int kMaxDevices = 64;
 
 size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+
+// Zeroes device memory and waits until it is done.  cudaMemset runs on the
+// legacy default stream, which the library's non-blocking streams do not wait
+// for: without the wait, a kernel on a model or context stream could run
+// before (or during) the zeroing.
+cudaError_t zero_sync(void *p, size_t bytes) {
+  const cudaError_t e = cudaMemset(p, 0, bytes);
+  return e != cudaSuccess ? e : cudaStreamSynchronize(nullptr);
+}
+// Host -> device copy that has landed on return.  A cudaMemcpy from pageable
+// host memory may return before its last DMA completes, on the legacy stream,
+// which the library's non-blocking streams do not wait for.
+cudaError_t upload_sync(void *dst, const void *src, size_t bytes) {
+  const cudaError_t e = cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+  return e != cudaSuccess ? e : cudaStreamSynchronize(nullptr);
+}
 int roundup(int v, int m) { return (v + m - 1) / m * m; }
 
 // Tile depth: 32 KB tiles (KT 128) once a matrix spans at least 16 of them per
@@ -225,7 +241,7 @@ int init_expf_table(DevCtx &c) {
     table[h] = key;
   }
   CK(cudaMalloc(&c.expf_keys, cap * sizeof(uint32_t)));
-  CK(cudaMemcpy(c.expf_keys, table.data(), cap * sizeof(uint32_t), cudaMemcpyHostToDevice));
+  CK(upload_sync(c.expf_keys, table.data(), cap * sizeof(uint32_t)));
   ExpfTable t{c.expf_keys, cap - 1};
   CK(cudaMemcpyToSymbol(g_expf_table, &t, sizeof(t)));
   return 1;
@@ -298,7 +314,7 @@ DevCtx *get_ctx() {
     llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: cudaFuncSetAttribute failed (%s)", cudaGetErrorString(ea));
     return nullptr;
   }
-  if (cudaMalloc(&c.err, 16) != cudaSuccess || cudaMemset(c.err, 0, 16) != cudaSuccess) {
+  if (cudaMalloc(&c.err, 16) != cudaSuccess || zero_sync(c.err, 16) != cudaSuccess) {
     llmq_set_error(LLMQ_ERR_OOM, "libllmq_cuda: device allocation failed");
     return nullptr;
   }
@@ -315,7 +331,7 @@ int ensure(T **p, size_t *have, size_t need, bool zero) {
   *have = 0;
   const size_t n = std::max<size_t>(need, 1);
   CK(cudaMalloc(p, n * sizeof(T)));
-  if (zero) CK(cudaMemset(*p, 0, n * sizeof(T)));
+  if (zero) CK(zero_sync(*p, n * sizeof(T)));
   *have = n;
   return 1;
 }
@@ -343,12 +359,12 @@ int build_mat(Mat &out, int K, int Nlog, int NT, const std::vector<int> &colsrc,
     if (!src[i] || K == 0 || srcN[i] == 0) continue;
     const size_t bytes = (size_t)K * srcN[i];
     CK(cudaMalloc(&tmp[i], bytes));
-    CK(cudaMemcpy(tmp[i], src[i], bytes, cudaMemcpyHostToDevice));
+    CK(upload_sync(tmp[i], src[i], bytes));
     rs.m[i] = tmp[i];
   }
   int *dcol = nullptr;
   CK(cudaMalloc(&dcol, colsrc.size() * sizeof(int)));
-  CK(cudaMemcpy(dcol, colsrc.data(), colsrc.size() * sizeof(int), cudaMemcpyHostToDevice));
+  CK(upload_sync(dcol, colsrc.data(), colsrc.size() * sizeof(int)));
   const long long chunks = (long long)out.Kpad / 16 * out.Npad;
   const int blocks = static_cast<int>(std::min<long long>((chunks + 255) / 256, 148LL * 64));
   k_repack<<<std::max(blocks, 1), 256>>>(rs, dcol, K, out.Kpad, out.Npad, NT, out.KT, out.w);
@@ -358,7 +374,7 @@ int build_mat(Mat &out, int K, int Nlog, int NT, const std::vector<int> &colsrc,
     const int cs = colsrc[p];
     if (cs >= 0) ws[p] = srcScale[cs >> 24][cs & 0xffffff];
   }
-  CK(cudaMemcpy(out.ws, ws.data(), ws.size() * sizeof(float), cudaMemcpyHostToDevice));
+  CK(upload_sync(out.ws, ws.data(), ws.size() * sizeof(float)));
   CK(cudaDeviceSynchronize());
   for (int i = 0; i < 3; ++i) cudaFree(tmp[i]);
   cudaFree(dcol);
@@ -384,6 +400,7 @@ struct GemvPlan {
   size_t smem = 0;
 };
 
+
 int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
   const size_t tile = (size_t)kNT * m.KT;
   const size_t codes = align16((size_t)rows * m.Kpad);
@@ -393,16 +410,16 @@ int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
   xs = std::max<size_t>(xs, (size_t)(pro == PRO_ABSMAX ? 1 : 2) * (((size_t)m.K + 3) & ~size_t(3)) * 4);
   const size_t fixed = codes + align16(xs);
   const size_t budget = (size_t)c.max_smem;
-  if (fixed + 2 * (tile + 16) + 16 > budget) {
+  if (fixed + 2 * (tile + 16) + 32 > budget) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: GEMV K=%d x %d rows does not fit in shared memory", m.K, rows);
     return 0;
   }
-  int S = static_cast<int>((budget - fixed - 16) / (tile + 16));
+  int S = static_cast<int>((budget - fixed - 32) / (tile + 16));
   S = std::min(S, 12);
   const long long T = (long long)m.n_slabs * m.n_ktiles;
   p.kt = m.KT;
   p.stages = S;
-  p.smem = align16((size_t)S * tile + 16 * (size_t)S) + codes + align16(xs);
+  p.smem = (size_t)S * tile + gemv_bar_bytes(S) + codes + align16(xs);
   p.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(T, c.num_sms)));
   return 1;
 }
@@ -800,13 +817,13 @@ void release_model(DevModel *M) {
 template <typename T>
 int dev_upload(T **dst, const T *src, size_t n) {
   CK(cudaMalloc(dst, std::max<size_t>(n, 1) * sizeof(T)));
-  if (n) CK(cudaMemcpy(*dst, src, n * sizeof(T), cudaMemcpyHostToDevice));
+  if (n) CK(upload_sync(*dst, src, n * sizeof(T)));
   return 1;
 }
 template <typename T>
 int dev_zeros(T **dst, size_t n) {
   CK(cudaMalloc(dst, std::max<size_t>(n, 1) * sizeof(T)));
-  CK(cudaMemset(*dst, 0, std::max<size_t>(n, 1) * sizeof(T)));
+  CK(zero_sync(*dst, std::max<size_t>(n, 1) * sizeof(T)));
   return 1;
 }
 
@@ -821,7 +838,7 @@ int tp_map_peers(DevModel *M) {
   std::vector<cudaIpcMemHandle_t> all(W);
   unsigned char *dh = nullptr;
   CK(cudaMalloc(&dh, sizeof(cudaIpcMemHandle_t) * (size_t)(W + 1)));
-  CK(cudaMemcpy(dh, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+  CK(upload_sync(dh, &mine, sizeof(mine)));
   const ncclResult_t r = g_nccl.AllGather(dh, dh + sizeof(mine), sizeof(mine), ncclUint8, g_tp.comm, M->stream);
   const cudaError_t es = cudaStreamSynchronize(M->stream);
   const cudaError_t ec = cudaMemcpy(all.data(), dh + sizeof(mine), sizeof(mine) * (size_t)W, cudaMemcpyDeviceToHost);
@@ -843,7 +860,7 @@ int tp_map_peers(DevModel *M) {
     M->tpx_peer[q] = static_cast<char *>(p);
   }
   CK(cudaMalloc(&M->tpx_peers_dev, sizeof(char *) * (size_t)W));
-  CK(cudaMemcpy(M->tpx_peers_dev, M->tpx_peer.data(), sizeof(char *) * (size_t)W, cudaMemcpyHostToDevice));
+  CK(upload_sync(M->tpx_peers_dev, M->tpx_peer.data(), sizeof(char *) * (size_t)W));
   return 1;
 }
 
@@ -1895,7 +1912,7 @@ int llmqd_quantize(const float *w, int rows, int cols, signed char *q, float *sc
     llmq_set_error(LLMQ_ERR_OOM, "quantize_int8_percol: device allocation of %zu bytes failed", n * 5);
     ok = 0;
   }
-  if (ok && n && cudaMemcpy(dw, w, n * 4, cudaMemcpyHostToDevice) != cudaSuccess) ok = 0;
+  if (ok && n && upload_sync(dw, w, n * 4) != cudaSuccess) ok = 0;
   if (ok) {
     k_quantize_percol<<<(cols + 127) / 128, 128, 0, c->stream>>>(dw, rows, cols, dq, ds);
     if (cudaGetLastError() != cudaSuccess || cudaStreamSynchronize(c->stream) != cudaSuccess) ok = 0;
@@ -1924,8 +1941,8 @@ int llmqd_dequantize(const signed char *q, const float *scale, int rows, int col
   int8_t *dq = nullptr;
   int ok = cudaMalloc(&dw, n * 4) == cudaSuccess && cudaMalloc(&dq, n) == cudaSuccess &&
            cudaMalloc(&ds, (size_t)cols * 4) == cudaSuccess;
-  ok = ok && cudaMemcpy(dq, q, n, cudaMemcpyHostToDevice) == cudaSuccess &&
-       cudaMemcpy(ds, scale, (size_t)cols * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+  ok = ok && upload_sync(dq, q, n) == cudaSuccess &&
+       upload_sync(ds, scale, (size_t)cols * 4) == cudaSuccess;
   if (ok) {
     k_dequantize_percol<<<std::min<long long>((n + 255) / 256, 148 * 32), 256, 0, c->stream>>>(dq, ds, rows, cols, dw);
     ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(c->stream) == cudaSuccess;
@@ -2005,9 +2022,9 @@ int llmqd_qmatmul(const float *A, int M, const QTensor *W, float *C) {
   CK(cudaMemcpyAsync(&flags, c->err, sizeof(int), cudaMemcpyDeviceToHost, st));
   CK(cudaStreamSynchronize(st));
   if (flags) {
-    cudaMemset(c->err, 0, 16);
-    cudaMemset(c->acc, 0, c->acc_n * sizeof(int));
-    cudaMemset(c->cnt, 0, c->cnt_n * sizeof(int));
+    zero_sync(c->err, 16);
+    zero_sync(c->acc, c->acc_n * sizeof(int));
+    zero_sync(c->cnt, c->cnt_n * sizeof(int));
     llmq_set_error(LLMQ_ERR_CUDA, "qmatmul: device reported error flags 0x%x", flags);
     return 0;
   }
@@ -2198,7 +2215,7 @@ int llmqd_sample_row(const float *row, int V, LlmqSample *smp, int *id) {
     c->sample_buf = nullptr;
     c->sample_n = 0;
     CK(cudaMalloc(&c->sample_buf, need));
-    CK(cudaMemset(c->sample_buf, 0, head));
+    CK(zero_sync(c->sample_buf, head));
     c->sample_n = need;
   }
   SampleState *d_st = reinterpret_cast<SampleState *>(c->sample_buf);
@@ -2333,7 +2350,7 @@ LLMQ_API int llmq_expf_device(const float *x, float *y, long long n) {
   if (!c) return q_llama_last_error();
   float *dx = nullptr, *dy = nullptr;
   int ok = cudaMalloc(&dx, n * 4) == cudaSuccess && cudaMalloc(&dy, n * 4) == cudaSuccess &&
-           cudaMemcpy(dx, x, n * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+           upload_sync(dx, x, n * 4) == cudaSuccess;
   if (ok) {
     k_expf_batch<<<148 * 8, 256, 0, c->stream>>>(dx, dy, n);
     ok = cudaGetLastError() == cudaSuccess && cudaStreamSynchronize(c->stream) == cudaSuccess &&
@@ -2349,9 +2366,12 @@ LLMQ_API int llmq_expf_device(const float *x, float *y, long long n) {
 }
 
 // Times `iters` back-to-back launches of one of the model's GEMVs on the model
-// stream (which: 0 QKV, 1 Wo, 2 W1|W3, 3 W2, 4 lm-head) with CUDA events, using
-// the activations left by the last step.  Reports the mean time per launch and
-// the algorithmic bytes of one launch (int8 weights + scales + input + output).
+// stream (which: 0 QKV, 1 Wo, 2 W1|W3, 3 W2, 4 lm-head; 5 the batch-1
+// attention) with CUDA events, using the activations left by the last step.
+// The launches go through the layers in turn, starting at `layer`, and run
+// from one captured CUDA graph with programmatic dependent launch, as in a
+// decode step.  Reports the mean time per launch and the algorithmic bytes of
+// one launch (int8 weights + scales + input + output).
 LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int iters, float *ms_per_launch,
                              double *bytes_per_launch) {
   std::lock_guard<std::recursive_mutex> lk(g_mu);
@@ -2366,6 +2386,7 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
   std::function<cudaError_t()> launch;
   GemvArgs a{};
   AttnArgs at{};
+  int next = layer;  // the layer of the next launch
   if (which == 5) {  // attention over the first cache at its current position
     DevKV *K = M->kvs.front();
     const size_t per_layer = (size_t)K->max_seq * M->kvd;
@@ -2382,37 +2403,61 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
     at.hd = M->cfg.head_dim;
     at.max_seq = K->max_seq;
     choose_attention(at);
-    launch = [&]() {
-      const cudaError_t e = launch_attention(at, st, false, 0);
-      return e != cudaSuccess ? e : launch_attention(at, st, false, 1);
+    launch = [&at, &next, M, K, per_layer, st]() {
+      const int l = next++ % M->cfg.n_layers;
+      at.kcache = K->k + l * per_layer;
+      at.vcache = K->v + l * per_layer;
+      const cudaError_t e = launch_attention(at, st, true, 0);
+      return e != cudaSuccess ? e : launch_attention(at, st, true, 1);
     };
   } else {
-    const Mat *mt[5] = {&M->qkv[layer], &M->wo[layer], &M->w13[layer], &M->w2[layer], &M->lm};
+    // Launch i takes layer (layer + i) mod n_layers, so consecutive launches
+    // stream different weights (a layer's QKV, Wo or W2 alone fits in L2).
     const GemvPlan *pl[5] = {&M->p_qkv, &M->p_wo, &M->p_w13, &M->p_w2, &M->p_lm};
     const bool rms[5] = {true, false, true, false, true};
-    float *ins[5] = {M->x, M->o, M->x, M->h, M->x};
-    const Mat &mm = *mt[which];
-    const GemvPlan &p = *pl[which];
-    a = base_args(mm, p, M->acc, M->cnt, M->err);
-    a.in = ins[which];
-    a.gamma = M->final_norm;
-    a.eps = M->cfg.eps;
-    a.out = M->logits;
+    float *const ins[5] = {M->x, M->o, M->x, M->h, M->x};
+    const GemvPlan *p = pl[which];
+    float *in = ins[which];
+    const int L = M->cfg.n_layers;
+    auto mat_of = [M, which, L](int l) -> const Mat & {
+      const int ll = l % L;
+      return which == 0 ? M->qkv[ll] : which == 1 ? M->wo[ll] : which == 2 ? M->w13[ll] : which == 3 ? M->w2[ll]
+                                                                                                   : M->lm;
+    };
+    const Mat &mm = mat_of(layer);
     const bool r = rms[which];
-    launch = [&a, &p, st, r]() {
-      return r ? launch_gemv<PRO_RMSNORM, EPI_PLAIN, 1>(a, p, st, false)
-               : launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, p, st, false);
+    launch = [&a, &next, mat_of, p, in, M, st, r]() {
+      a = base_args(mat_of(next++), *p, M->acc, M->cnt, M->err);
+      a.in = in;
+      a.gamma = M->final_norm;
+      a.eps = M->cfg.eps;
+      a.out = M->logits;
+      return r ? launch_gemv<PRO_RMSNORM, EPI_PLAIN, 1>(a, *p, st, true)
+               : launch_gemv<PRO_ABSMAX, EPI_PLAIN, 1>(a, *p, st, true);
     };
     const int logical_n = which == 2 ? 2 * mm.N : mm.N;
     *bytes_per_launch = (double)mm.K * logical_n + 4.0 * logical_n + 4.0 * mm.K + 4.0 * mm.N;
   }
-  for (int i = 0; i < 3; ++i)
-    if (launch() != cudaSuccess) return LLMQ_ERR_CUDA;
-  if (cudaEventRecord(M->ev0, st) != cudaSuccess) return LLMQ_ERR_CUDA;
-  for (int i = 0; i < iters; ++i)
-    if (launch() != cudaSuccess) return LLMQ_ERR_CUDA;
-  if (cudaEventRecord(M->ev1, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
-    llmq_set_error(LLMQ_ERR_CUDA, "llmq_bench_gemv: CUDA failure");
+  // The `iters` launches are captured into one CUDA graph, back to back with
+  // programmatic dependent launch as inside a decode step's graph, so the
+  // timing is the kernels' own and not the host's launch rate; the graph is
+  // replayed once to warm up, then once between the two events.
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t ge = nullptr;
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  for (int i = 0; i < iters && e == cudaSuccess; ++i) e = launch();
+  const cudaError_t ee = cudaStreamEndCapture(st, &g);
+  if (e == cudaSuccess) e = ee;
+  if (e == cudaSuccess) e = cudaGraphInstantiate(&ge, g, 0);
+  if (g) cudaGraphDestroy(g);
+  if (e == cudaSuccess) e = cudaGraphLaunch(ge, st);
+  if (e == cudaSuccess) e = cudaEventRecord(M->ev0, st);
+  if (e == cudaSuccess) e = cudaGraphLaunch(ge, st);
+  if (e == cudaSuccess) e = cudaEventRecord(M->ev1, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (ge) cudaGraphExecDestroy(ge);
+  if (e != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "llmq_bench_gemv: %s", cudaGetErrorString(e));
     return LLMQ_ERR_CUDA;
   }
   float ms = 0.0f;
@@ -2584,6 +2629,25 @@ extern "C" LLMQ_API int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int
 extern "C" LLMQ_API int llmq_phase_ts(unsigned long long *out) {
   return cudaMemcpyFromSymbol(out, g_phase_ts, sizeof(unsigned long long) * 64 * 16) == cudaSuccess ? 0 : 2;
 }
+// Profiling builds only: phase timestamps from launch `grid` (%gridid) only (0: all).
+extern "C" LLMQ_API int llmq_phase_grid(unsigned long long grid) {
+  static const unsigned long long zero[64][16] = {};
+  if (cudaMemcpyToSymbol(g_phase_ts, zero, sizeof(zero)) != cudaSuccess) return 2;
+  return cudaMemcpyToSymbol(g_phase_grid, &grid, sizeof(grid)) == cudaSuccess ? 0 : 2;
+}
+// Profiling builds only: copies the launch spans (4096 x {gridid, first start,
+// last end}) to out (when given), then resets them.
+extern "C" LLMQ_API int llmq_launch_spans(unsigned long long *out) {
+  static unsigned long long tab[4096][3];
+  if (cudaDeviceSynchronize() != cudaSuccess) return 2;
+  if (out && cudaMemcpyFromSymbol(out, g_launch_tab, sizeof(tab)) != cudaSuccess) return 2;
+  for (auto &e : tab) {
+    e[0] = 0;
+    e[1] = ~0ull;
+    e[2] = 0;
+  }
+  return cudaMemcpyToSymbol(g_launch_tab, tab, sizeof(tab)) == cudaSuccess ? 0 : 2;
+}
 #endif
 
 // Times `iters` device-resident products C(M, N) = A(M, K) x W on the path
@@ -2611,7 +2675,7 @@ extern "C" LLMQ_API int llmq_bench_qmatmul(const QTensor *W, int M, int iters, f
   float *dA = nullptr, *dC = nullptr;
   int rc = LLMQ_OK;
   if (cudaMalloc(&dA, hA.size() * 4) != cudaSuccess || cudaMalloc(&dC, (size_t)M * N * 4) != cudaSuccess ||
-      cudaMemcpy(dA, hA.data(), hA.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      upload_sync(dA, hA.data(), hA.size() * 4) != cudaSuccess ||
       !ensure(&c->acc, &c->acc_n, (size_t)8 * m.Npad, true) || !ensure(&c->cnt, &c->cnt_n, (size_t)m.n_slabs, true)) {
     llmq_set_error(LLMQ_ERR_OOM, "llmq_bench_qmatmul: allocation failed");
     rc = LLMQ_ERR_OOM;
@@ -2647,7 +2711,7 @@ extern "C" LLMQ_API int llmq_bench_qmatmul(const QTensor *W, int M, int iters, f
     int flags = 0;
     cudaMemcpy(&flags, c->err, sizeof(int), cudaMemcpyDeviceToHost);
     if (flags) {
-      cudaMemset(c->err, 0, 16);
+      zero_sync(c->err, 16);
       llmq_set_error(LLMQ_ERR_CUDA, "llmq_bench_qmatmul: device error flags 0x%x", flags);
       rc = LLMQ_ERR_CUDA;
     }
@@ -2696,21 +2760,21 @@ extern "C" LLMQ_API int llmq_tp_wait_timeout_check(int which, unsigned polls, in
   std::vector<float> hs(kDm, 0.004f);
   QTensor W{kK, kDm, hq.data(), hs.data()};
   bool ok = cudaMalloc(&region[0], rb) == cudaSuccess && cudaMalloc(&region[1], rb) == cudaSuccess &&
-            cudaMemset(region[0], 0, rb) == cudaSuccess && cudaMemset(region[1], 0, rb) == cudaSuccess &&
+            zero_sync(region[0], rb) == cudaSuccess && zero_sync(region[1], rb) == cudaSuccess &&
             cudaMalloc(&peers, sizeof(region)) == cudaSuccess &&
-            cudaMemcpy(peers, region, sizeof(region), cudaMemcpyHostToDevice) == cudaSuccess &&
-            cudaMalloc(&seq, sizeof(unsigned)) == cudaSuccess && cudaMemset(seq, 0, sizeof(unsigned)) == cudaSuccess &&
-            cudaMalloc(&err, sizeof(int)) == cudaSuccess && cudaMemset(err, 0, sizeof(int)) == cudaSuccess &&
+            upload_sync(peers, region, sizeof(region)) == cudaSuccess &&
+            cudaMalloc(&seq, sizeof(unsigned)) == cudaSuccess && zero_sync(seq, sizeof(unsigned)) == cudaSuccess &&
+            cudaMalloc(&err, sizeof(int)) == cudaSuccess && zero_sync(err, sizeof(int)) == cudaSuccess &&
             cudaMalloc(&x, kK * sizeof(float)) == cudaSuccess &&
-            cudaMemcpy(x, hx.data(), kK * sizeof(float), cudaMemcpyHostToDevice) == cudaSuccess &&
-            cudaMalloc(&out, kDm * sizeof(float)) == cudaSuccess && cudaMemset(out, 0, kDm * sizeof(float)) == cudaSuccess;
+            upload_sync(x, hx.data(), kK * sizeof(float)) == cudaSuccess &&
+            cudaMalloc(&out, kDm * sizeof(float)) == cudaSuccess && zero_sync(out, kDm * sizeof(float)) == cudaSuccess;
   ok = ok && build_plain(m, W, 1);
   GemvPlan plan;
   ok = ok && plan_gemv(*c, m, PRO_ABSMAX, 1, plan);
   ok = ok && cudaMalloc(&acc, (size_t)m.Npad * sizeof(int)) == cudaSuccess &&
-       cudaMemset(acc, 0, (size_t)m.Npad * sizeof(int)) == cudaSuccess &&
+       zero_sync(acc, (size_t)m.Npad * sizeof(int)) == cudaSuccess &&
        cudaMalloc(&cnt, (size_t)m.n_slabs * sizeof(int)) == cudaSuccess &&
-       cudaMemset(cnt, 0, (size_t)m.n_slabs * sizeof(int)) == cudaSuccess;
+       zero_sync(cnt, (size_t)m.n_slabs * sizeof(int)) == cudaSuccess;
   if (!ok) {
     if (q_llama_last_error() == LLMQ_OK) llmq_set_error(LLMQ_ERR_OOM, "llmq_tp_wait_timeout_check: set-up failed");
     rc = q_llama_last_error();
@@ -2764,6 +2828,63 @@ extern "C" LLMQ_API int llmq_tp_wait_timeout_check(int which, unsigned polls, in
   cudaFree(out);
   cudaFree(acc);
   cudaFree(cnt);
+  free_mat(m);
+  return rc;
+}
+
+// RMSNorm of one row (rmsnorm.c:7-21) followed by qmatmul of the normalised
+// row (quant.c:60-85), as the GEMV with the RMSNorm prologue computes it for
+// QKV, W1|W3 and the lm-head inside a decode step: out[N] = qmatmul(rmsnorm(x,
+// gamma, eps), W).  For tests of that prologue on chosen rows.
+extern "C" LLMQ_API int llmq_rmsnorm_qmatmul(const float *x, const float *gamma, float eps, const QTensor *W,
+                                             float *out) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevCtx *c = get_ctx();
+  if (!c) return q_llama_last_error();
+  if (!x || !gamma || !W || !out || W->rows <= 0 || W->cols <= 0) {
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_rmsnorm_qmatmul: bad arguments");
+    return LLMQ_ERR_ARG;
+  }
+  const int K = W->rows, N = W->cols;
+  Mat m;
+  if (!build_plain(m, *W, 1)) return q_llama_last_error();
+  GemvPlan plan;
+  float *dx = nullptr, *dg = nullptr, *dout = nullptr;
+  int rc = LLMQ_OK;
+  if (!plan_gemv(*c, m, PRO_RMSNORM, 1, plan)) {
+    rc = q_llama_last_error();
+  } else if (cudaMalloc(&dx, (size_t)K * 4) != cudaSuccess || cudaMalloc(&dg, (size_t)K * 4) != cudaSuccess ||
+             cudaMalloc(&dout, (size_t)N * 4) != cudaSuccess ||
+             !ensure(&c->acc, &c->acc_n, (size_t)8 * m.Npad, true) ||
+             !ensure(&c->cnt, &c->cnt_n, (size_t)m.n_slabs, true)) {
+    llmq_set_error(LLMQ_ERR_OOM, "llmq_rmsnorm_qmatmul: allocation failed");
+    rc = LLMQ_ERR_OOM;
+  } else {
+    cudaStream_t st = c->stream;
+    GemvArgs a = base_args(m, plan, c->acc, c->cnt, c->err);
+    a.in = dx;
+    a.gamma = dg;
+    a.eps = eps;
+    a.out = dout;
+    int flags = 0;
+    cudaError_t e = cudaMemcpyAsync(dx, x, (size_t)K * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dg, gamma, (size_t)K * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = launch_gemv<PRO_RMSNORM, EPI_PLAIN, 1>(a, plan, st, false);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out, dout, (size_t)N * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(&flags, c->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) {
+      llmq_set_error(LLMQ_ERR_CUDA, "llmq_rmsnorm_qmatmul: %s", cudaGetErrorString(e));
+      rc = LLMQ_ERR_CUDA;
+    } else if (flags) {
+      zero_sync(c->err, 16);
+      llmq_set_error(LLMQ_ERR_CUDA, "llmq_rmsnorm_qmatmul: device error flags 0x%x", flags);
+      rc = LLMQ_ERR_CUDA;
+    }
+  }
+  cudaFree(dx);
+  cudaFree(dg);
+  cudaFree(dout);
   free_mat(m);
   return rc;
 }

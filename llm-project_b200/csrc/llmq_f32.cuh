@@ -244,8 +244,10 @@ __global__ void __launch_bounds__(MAXT, 1) k_gemv_f32(const F32Args a) {
   int issued = 0;
   if (producing)
     for (; issued < S && issued < n_chunks; ++issued) issue(issued);
-  pdl_launch_dependents();
   pdl_wait();
+  // The next kernel may start once every CTA is past its wait (the attention
+  // kernel reads the step state and earlier cache rows before its own wait).
+  pdl_launch_dependents();
 
   // ------------------------------------------------------------ prologue
   // The input row (or embedding row) arrives with one bulk copy: a CTA of few

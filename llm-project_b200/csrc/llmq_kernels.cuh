@@ -24,17 +24,51 @@ namespace cg = cooperative_groups;
 // first 64 CTAs records %globaltimer at numbered points.  Compiled out otherwise.
 #ifdef LLMQ_PHASE_TIMING
 __device__ unsigned long long g_phase_ts[64][16];
+__device__ unsigned long long g_phase_grid;  // record only this launch (%gridid; 0: every launch)
 #define LLMQ_TSTAMP(i)                                                  \
   do {                                                                  \
     if (threadIdx.x == 0 && blockIdx.x < 64 && blockIdx.y == 0) {       \
-      unsigned long long t_;                                            \
+      unsigned long long t_, g_;                                        \
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));           \
-      g_phase_ts[blockIdx.x][i] = t_;                                   \
+      asm volatile("mov.u64 %0, %%gridid;" : "=l"(g_));                \
+      if (g_phase_grid == 0 || g_phase_grid == g_) g_phase_ts[blockIdx.x][i] = t_; \
     }                                                                   \
+  } while (0)
+// Launch spans: per grid launch (%gridid), the earliest CTA start and the
+// latest CTA end, so a graph replay's kernels can be laid out in time.
+__device__ unsigned long long g_launch_tab[4096][3];  // gridid, first start, last end
+__device__ __forceinline__ unsigned long long llmq_now() {
+  unsigned long long t_;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));
+  return t_;
+}
+__device__ __forceinline__ unsigned long long llmq_gridid() {
+  unsigned long long g_;
+  asm volatile("mov.u64 %0, %%gridid;" : "=l"(g_));
+  return g_;
+}
+#define LLMQ_LAUNCH_ENTER()                                              \
+  do {                                                                   \
+    if (threadIdx.x == 0) {                                              \
+      const unsigned long long g_ = llmq_gridid();                       \
+      unsigned long long *e_ = g_launch_tab[g_ & 4095];                  \
+      e_[0] = g_;                                                        \
+      atomicMin(&e_[1], llmq_now());                                     \
+    }                                                                    \
+  } while (0)
+#define LLMQ_LAUNCH_EXIT()                                               \
+  do {                                                                   \
+    if (threadIdx.x == 0) atomicMax(&g_launch_tab[llmq_gridid() & 4095][2], llmq_now()); \
   } while (0)
 #else
 #define LLMQ_TSTAMP(i) \
   do {               \
+  } while (0)
+#define LLMQ_LAUNCH_ENTER() \
+  do {                    \
+  } while (0)
+#define LLMQ_LAUNCH_EXIT() \
+  do {                   \
   } while (0)
 #endif
 
@@ -224,6 +258,10 @@ constexpr int kNT = 256;
 constexpr int kParts = kThreads / kNT;  // threads per column
 static_assert(kParts * kNT == kThreads, "tile geometry");
 
+// Shared memory of a GEMV's mbarriers: full[S] and empty[S] of the ring and
+// the input row's, rounded to 16 bytes.
+__host__ __device__ inline size_t gemv_bar_bytes(int S) { return ((size_t)(2 * S + 1) * 8 + 15) & ~size_t(15); }
+
 struct StepState {
   int token;
   int pos;
@@ -290,12 +328,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   __shared__ int s_abort;
 
   LLMQ_TSTAMP(0);
+  LLMQ_LAUNCH_ENTER();
   const int tid = threadIdx.x;
   const int S = a.stages;
   uint8_t *stage0 = sm;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + (size_t)S * kTileBytes);  // full[S], then empty[S]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + (size_t)S * kTileBytes);  // full[S], empty[S], row
   uint64_t *empty = bars + S;
-  int8_t *codes = reinterpret_cast<int8_t *>(sm + (((size_t)S * kTileBytes + 16 * S + 15) & ~size_t(15)));
+  uint64_t *rowbar = bars + 2 * S;  // the input row's bulk copy
+  int8_t *codes = reinterpret_cast<int8_t *>(sm + (size_t)S * kTileBytes + gemv_bar_bytes(S));
   float *xs = reinterpret_cast<float *>(codes + (((size_t)a.rows * a.Kpad + 15) & ~size_t(15)));
   float *ebuf = xs;  // epilogue exchange buffer (prologue vector is dead by then)
 
@@ -310,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       mbar_init(&bars[s], 1);               // the stage's copy landed
       mbar_init(&empty[s], kThreads / 32);  // every warp has read the stage
     }
+    mbar_init(rowbar, 1);
     fence_mbar_init();
     s_abort = 0;
   }
@@ -332,23 +373,31 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   };
   issue_to(2);
   LLMQ_TSTAMP(1);
-  pdl_launch_dependents();
   pdl_wait();
+  // The next kernel may start once every CTA is past its wait: whatever it
+  // reads before its own wait was then written by kernels already complete.
+  pdl_launch_dependents();
   LLMQ_TSTAMP(2);
 
   // ------------------------------------------------------------ prologue
   // The input rows come from the previous kernel: copied into xs with one bulk
-  // copy per row once that kernel's writes are visible (plain loads when the
-  // row is not 16-byte sized and aligned).
+  // copy per row once that kernel's writes are visible, ahead of the rest of
+  // the ring (plain loads when the row is not 16-byte sized and aligned).
   const bool vec_in = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.in) & 15) == 0;
+  uint32_t row_phase = 0;
   auto load_row = [&](const float *src) {
     if (vec_in) {
-      const float4 *s4 = reinterpret_cast<const float4 *>(src);
-      for (int k = tid; k < a.K / 4; k += kThreads) reinterpret_cast<float4 *>(xs)[k] = s4[k];
+      if (tid == 0) {
+        mbar_expect_tx(rowbar, static_cast<uint32_t>(a.K) * 4u);
+        bulk_load(xs, src, static_cast<uint32_t>(a.K) * 4u, rowbar);
+      }
+      issue_to(S);
+      if (!mbar_wait_bounded(rowbar, row_phase)) s_abort = 1;
+      row_phase ^= 1u;
     } else {
       for (int k = tid; k < a.K; k += kThreads) xs[k] = src[k];
+      issue_to(S);
     }
-    issue_to(S);
     __syncthreads();
   };
   if (PRO == PRO_ABSMAX) {
@@ -634,6 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   LLMQ_TSTAMP(6);
   if (n > 0) flush(cur);
   LLMQ_TSTAMP(7);
+  LLMQ_LAUNCH_EXIT();
 }
 
 // --------------------------------------------------------------- attention
@@ -888,8 +938,13 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   __shared__ float s_part_max[8];  // [rank]: stored by that CTA
   __shared__ float s_inv;
   cg::cluster_group cluster = cg::this_cluster();
+  LLMQ_TSTAMP(0);
+  LLMQ_LAUNCH_ENTER();
   pdl_launch_dependents();
-  pdl_wait();
+  // Before the wait: the previous kernel (this layer's QKV product) starts its
+  // dependents only once all its CTAs are past their own wait, so the step
+  // state and the cache rows [0, pos) (written by earlier steps) are final
+  // here; only this step's value row `pos` (the QKV epilogue) is read after.
   const int tid = threadIdx.x;
   const int h = blockIdx.y;
   const int nsl = gridDim.x, r = blockIdx.x;  // the cluster spans gridDim.x: rank r = blockIdx.x
@@ -907,8 +962,8 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   const int KC = a.fused_chunk;
   const float *kc = a.kcache + (size_t)kvh * a.max_seq * hd;
   const float *vc = a.vcache + (size_t)kvh * a.max_seq * hd;
-  // the value slice (its row `pos` is this step's, written by the QKV epilogue)
-  if (w > 0) stage_rows(vs, kPVSlice, vc, hd, 0, np, d0, w, tid, kFusedThreads);
+  // the value slice rows [0, pos) (row `pos` is this step's: loaded after the wait)
+  if (w > 0) stage_rows(vs, kPVSlice, vc, hd, 0, pos, d0, w, tid, kFusedThreads);
   cp_async_commit();
   const int nchunks = (pb - pa + KC - 1) / KC;  // one slot when a part fits in one chunk, else two
   auto stage_keys = [&](int c) {  // cached keys of chunk c (not the row `pos`, rotated below)
@@ -917,6 +972,9 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   };
   if (nchunks > 0) stage_keys(0);
   cp_async_commit();
+  pdl_wait();
+  LLMQ_TSTAMP(1);
+  if (tid < w) vs[(size_t)pos * kPVSlice + tid] = vc[(size_t)pos * hd + d0 + tid];  // llama.c:552, this step's v
   const float *cs = a.rope_cos + (size_t)pos * half, *sn = a.rope_sin + (size_t)pos * half;
   const bool own_pos = pos >= pa && pos < pb;
   for (int d = tid; d < hd; d += kFusedThreads) {
@@ -947,21 +1005,29 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
     __syncthreads();  // the slot is free for chunk c + 2
   }
   m = block_max<kFusedThreads>(m, s_red);
+  LLMQ_TSTAMP(2);
   if (tid < nsl) *cluster.map_shared_rank(&s_part_max[r], tid) = m;  // this part's maximum, into CTA tid
   cluster.sync();  // every part's maximum is in every CTA
+  LLMQ_TSTAMP(3);
   for (int q = 0; q < nsl; ++q) m = fmaxf(m, s_part_max[q]);
   for (int p = pa + tid; p < pb; p += kFusedThreads) {
     const float ex = libm_expf(__fsub_rn(e[p], m));  // llama.c:566
     for (int q = 0; q < nsl; ++q) *cluster.map_shared_rank(&e[p], q) = ex;  // into every CTA's e
   }
   cluster.sync();  // every part's exponentials are in every CTA; no remote accesses after this point
+  LLMQ_TSTAMP(4);
   if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum_a16(e, np, 0.0f));  // llama.c:567
   __syncthreads();
+  LLMQ_TSTAMP(5);
   const float inv = s_inv;
   for (int p = tid; p < np; p += kFusedThreads) e[p] = __fmul_rn(e[p], inv);
   cp_async_wait<0>();
   __syncthreads();
+  LLMQ_TSTAMP(6);
   if (tid < w) a.out[(size_t)h * hd + d0 + tid] = seq_dot(e, vs + tid, kPVSlice, np, 0.0f);  // llama.c:574
+  __syncwarp();
+  LLMQ_TSTAMP(7);
+  LLMQ_LAUNCH_EXIT();
 }
 
 // Final step bookkeeping: publish the argmax and error flags, advance the
@@ -969,6 +1035,7 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
 // record the generated id, and reset the argmax cell and error word.
 __global__ void k_step_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
                               int max_seq, unsigned *tp_seq, unsigned tp_products) {
+  LLMQ_LAUNCH_ENTER();
   pdl_wait();
   if (tp_seq) *tp_seq += tp_products;  // the step's row-parallel products are done on this rank
   const unsigned long long key = *argmax;
@@ -984,6 +1051,7 @@ __global__ void k_step_finish(StepState *step, unsigned long long *argmax, int *
   step->pos = pos + 1;
   *argmax = 0ull;
   *err = 0;
+  LLMQ_LAUNCH_EXIT();
 }
 
 // ------------------------------------------------------------ utility kernels

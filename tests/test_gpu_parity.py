@@ -309,3 +309,85 @@ def test_device_expf_equals_host_libm_on_every_float(lib, orc):
         same |= np.isnan(dev) & np.isnan(host)
         mismatches += int((~same).sum())
     assert mismatches == 0
+
+
+# ----------------------------------------- RMSNorm prologue on rounding ties
+def _emulated_code_flips(x, g, eps=np.float32(1e-5)):
+    """How many activation codes differ between the exact scale (the
+    sequential f32 sum of squares, rmsnorm.c:15) and a scale from the
+    double-precision sum of the same squares: how sensitive the row is to the
+    order of that sum."""
+    f32 = np.float32
+
+    def r_of(ms):
+        ms = f32(ms * f32(f32(1) / f32(len(x))))
+        return f32(f32(1) / np.sqrt(f32(ms + eps)))
+
+    def codes(r):
+        y = ((x * r).astype(f32) * g).astype(f32)
+        a = f32(np.max(np.abs(y)) / f32(127))
+        return np.clip(np.rint((y * f32(f32(1) / a)).astype(f32)), -127, 127)
+
+    sq = (x * x).astype(f32)
+    ms = f32(0)
+    for v in sq:
+        ms = f32(ms + v)
+    return int(np.sum(codes(r_of(ms)) != codes(r_of(f32(np.sum(sq.astype(np.float64)))))))
+
+
+@pytest.mark.parametrize("ties", [4095, 60, 20, 0])
+def test_rmsnorm_gemv_on_rounding_ties(lib, orc, ties):
+    """Rows whose normalised values sit at .5 rounding ties, so that any
+    deviation from the reference's sequential sum of squares would flip codes:
+    with the scale from an exactly rounded sum, 560, 47 and 4 of the codes
+    differ; and a plain row.  The GEMV with the RMSNorm prologue must equal
+    rmsnorm + qmatmul of the oracle bit for bit."""
+    f32 = np.float32
+    rng = np.random.default_rng(7 + ties)
+    K, N = 4096, 1000
+    x = (rng.standard_normal(K) * 10).astype(f32)
+    if ties:
+        x[1:1 + ties] = ((rng.integers(-126, 126, ties) + 0.5) * 100.0 / 127).astype(f32)
+        x[0] = f32(100.0)
+    g = np.ones(K, f32) if ties else rng.uniform(0.5, 1.5, K).astype(f32)
+    flips = _emulated_code_flips(x, g)
+    if ties == 4095:
+        assert flips > 256
+    elif ties:
+        assert 0 < flips <= 256
+    q = rng.integers(-127, 128, size=(K, N)).astype(np.int8)
+    s = rng.uniform(1e-3, 1e-2, size=N).astype(f32)
+    y = np.zeros(K, f32)
+    orc.orc_rmsnorm_row(fp(x), fp(g), K, f32(1e-5), fp(y))
+    want = orc_qmatmul(orc, y.reshape(1, K), q, s)[0]
+    got = np.full(N, np.nan, f32)
+    qt = llmq.qtensor_view(q, s)
+    assert lib.llmq_rmsnorm_qmatmul(fp(x), fp(g), f32(1e-5), C.byref(qt), fp(got)) == 0, \
+        lib.q_llama_last_error_message()
+    assert bits_equal(got, want)
+
+
+def test_measurement_hooks_run(lib):
+    """The timing entry points bench.py reads (per-kind GEMV and attention
+    timings from a captured graph, the per-kernel step profile, the isolated
+    product) run and report positive times."""
+    m = synth(lib, dict(TINY, n_layers=3), seed=9)
+    kv = lib.q_llama_kv_create(C.byref(m))
+    gpu_decode(lib, m, [1, 2, 3], kv=kv)
+    for which in range(6):
+        ms, by = C.c_float(), C.c_double()
+        assert lib.llmq_bench_gemv(C.byref(m), which, 1, 5, C.byref(ms), C.byref(by)) == 0, \
+            lib.q_llama_last_error_message()
+        assert ms.value > 0 and by.value > 0, which
+    nk = lib.llmq_kernels_per_step(C.byref(m))
+    prof = np.zeros(nk, np.float32)
+    assert lib.llmq_step_profile(C.byref(m), C.byref(kv), 4, prof.ctypes.data_as(llmq.c_float_p), nk) == 0
+    assert kv.len == 4 and np.all(prof > 0)
+    t = lib.qtensor_create(288, 768)
+    lib.llmq_synth_qtensor(C.byref(t), 5)
+    for M in (1, 3, 64):
+        ms = C.c_float()
+        assert lib.llmq_bench_qmatmul(C.byref(t), M, 3, C.byref(ms)) == 0 and ms.value > 0
+    lib.qtensor_free(C.byref(t))
+    lib.llama_kv_free(C.byref(kv))
+    lib.q_llama_model_free(C.byref(m))
