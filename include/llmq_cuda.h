@@ -332,6 +332,12 @@ int q_llama_kv_sync_host(const QLlamaModel *m, LlamaKV *kv);
  * rename.  Returns 0 on success, 1 with a message on stderr on error. */
 int q_llama_model_save(const char *path, const QLlamaModel *m);
 
+/* Replaces tools/upgrade_llma.py: an LLMA v1 checkpoint (no q/k/v biases)
+ * becomes v2 with three zero bias vectors per layer inserted after Wv,
+ * streamed in 4 MiB pieces.  Refuses non-LLMA, already-v2, truncated and
+ * overlong files with the tool's messages; 0 on success, 1 on error. */
+int llmq_llma_upgrade_v1(const char *src, const char *dst);
+
 /* Model configuration, in LLMQ header order (llama.c:241-243). */
 typedef struct {
   int vocab, d_model, n_layers, n_heads, n_kv, head_dim, d_ff, max_seq;
@@ -380,6 +386,16 @@ int q_llama_model_shard(const QLlamaModel *m, int rank, int world, QLlamaModel *
 /* Fills an existing QTensor with uniform codes in [-127, 127] and uniform scales
  * in [1e-3, 1e-2), seeded (the isolated matvec sweep's weights). */
 void llmq_synth_qtensor(QTensor *t, uint64_t seed);
+
+/* Addition (the writer tools/convert_llama.py:73-97 is for converted models):
+ * the model llmq_synth_model (fast = 0) or llmq_synth_model_fast_shard with
+ * one shard (fast = 1, stddev and with_bias ignored) builds, written straight
+ * to an LLMQ v2 file tensor by tensor, so no more than one tensor is ever in
+ * host memory (a 70B-shaped file needs ~1 GB of RAM, not ~70 GB).  Byte for byte
+ * what q_llama_model_save writes for that model; atomic like llama.c:230-269.
+ * Returns 0 or an error code. */
+int llmq_synth_model_save(const LlmqConfig *cfg, uint64_t seed, float stddev, int with_bias, int fast,
+                          const char *path);
 
 /* Upload / release the device copy of a model explicitly (both are otherwise
  * implicit).  Returns 0 or an error code. */

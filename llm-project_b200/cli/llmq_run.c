@@ -2,6 +2,7 @@
  * branch) on the GPU path of libllmq_cuda.so.
  *
  *   llmq_run llama <checkpoint.bin> [n_new=40]
+ *   llmq_run upgrade-llma <v1.bin> <v2.bin>
  *
  * Same protocol as `transformer llama`: each stdin line holds space-separated
  * token ids; the sequence restarts (kv.len = 0), the ids are fed, and n_new
@@ -19,7 +20,10 @@
  * llama_decode_step_argmax, the last step's logits sampled, then
  * llama_decode_step_sample.  The ids equal the reference CLI's.  The LLMA
  * text mode (a tokenizer as 4th argument, main.c:584-622) needs the
- * reference's tokenizer and is not provided. */
+ * reference's tokenizer and is not provided.
+ *
+ * `upgrade-llma` is the reference's tools/upgrade_llma.py: an LLMA v1
+ * checkpoint rewritten as v2 (zero q/k/v biases inserted), streamed. */
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -187,6 +191,8 @@ static int run_llama(int argc, char **argv) {
 
 int main(int argc, char **argv) {
   if (argc > 1 && strcmp(argv[1], "llama") == 0) return run_llama(argc, argv);
-  fprintf(stderr, "usage: llmq_run llama <checkpoint.bin> [n_new=40]\n");
+  if (argc == 4 && strcmp(argv[1], "upgrade-llma") == 0) return llmq_llma_upgrade_v1(argv[2], argv[3]);
+  fprintf(stderr, "usage: llmq_run llama <checkpoint.bin> [n_new=40]\n"
+                  "       llmq_run upgrade-llma <v1.bin> <v2.bin>   (tools/upgrade_llma.py)\n");
   return 2;
 }

@@ -349,3 +349,123 @@ LLMQ_API int llama_generate_sample(const LlamaModel *m, LlamaKV *kv, int token, 
   kv->len = kv->len + n;
   return LLMQ_OK;
 }
+
+/* ------------------------------------------------------- LLMA v1 -> v2 upgrade */
+/* Copies n f32 values from src to dst in 4 MiB pieces; 0 when src runs short. */
+static int copy_floats(FILE *src, FILE *dst, size_t n, char *buf) {
+  size_t left = n * sizeof(float);
+  while (left) {
+    const size_t take = left < ((size_t)1 << 22) ? left : ((size_t)1 << 22);
+    if (fread(buf, 1, take, src) != take) return 0;
+    if (fwrite(buf, 1, take, dst) != take) return -1;
+    left -= take;
+  }
+  return 1;
+}
+
+/* The reference's tools/upgrade_llma.py in C: an LLMA v1 checkpoint (no q/k/v
+ * biases) becomes v2 by copying every tensor across and inserting three zero
+ * bias vectors after each layer's Wv (the v2 canonical order, llama.c:199-219).
+ * Streams the file in 4 MiB pieces, so a checkpoint of any size needs no more
+ * memory than that.  Refuses files that are not LLMA, are already v2 or later,
+ * are truncated or have trailing bytes, with the tool's messages on stderr;
+ * returns 0 on success, 1 on error (dst then holds no partial file). */
+LLMQ_API int llmq_llma_upgrade_v1(const char *src_path, const char *dst_path) {
+  FILE *f = fopen(src_path, "rb");
+  if (!f) {
+    fprintf(stderr, "error: cannot open '%s'\n", src_path);
+    llmq_set_error(LLMQ_ERR_IO, "llmq_llma_upgrade_v1: cannot open '%s'", src_path);
+    return 1;
+  }
+  uint32_t hdr[2];
+  int32_t cfg[8];
+  float fcfg[2];
+  if (fread(hdr, 4, 2, f) != 2 || fread(cfg, 4, 8, f) != 8 || fread(fcfg, 4, 2, f) != 2) {
+    fprintf(stderr, "error: '%s' is too small to be an LLMA checkpoint\n", src_path);
+    llmq_set_error(LLMQ_ERR_IO, "llmq_llma_upgrade_v1: '%s' is too small", src_path);
+    fclose(f);
+    return 1;
+  }
+  if (hdr[0] != 0x414D4C4Cu) {
+    fprintf(stderr, "error: '%s' is not an LLMA checkpoint (magic %#x)\n", src_path, hdr[0]);
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_llma_upgrade_v1: '%s' is not an LLMA checkpoint", src_path);
+    fclose(f);
+    return 1;
+  }
+  if (hdr[1] != 1u) {
+    fprintf(stderr, "error: '%s' is already version %u, nothing to do\n", src_path, hdr[1]);
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_llma_upgrade_v1: '%s' is already version %u", src_path, hdr[1]);
+    fclose(f);
+    return 1;
+  }
+  for (int i = 0; i < 8; i++)
+    if (cfg[i] <= 0) {
+      fprintf(stderr, "error: '%s' has an invalid config\n", src_path);
+      llmq_set_error(LLMQ_ERR_ARG, "llmq_llma_upgrade_v1: '%s' has an invalid config", src_path);
+      fclose(f);
+      return 1;
+    }
+  const size_t vocab = (size_t)cfg[0], dm = (size_t)cfg[1], qd = (size_t)cfg[3] * cfg[5], kvd = (size_t)cfg[4] * cfg[5];
+  const size_t dff = (size_t)cfg[6];
+  const int n_layers = cfg[2];
+  const size_t plen = strlen(dst_path);
+  char *tmp = (char *)malloc(plen + 5);
+  char *buf = (char *)malloc((size_t)1 << 22);
+  float *zeros = (float *)calloc(qd + 2 * kvd, sizeof(float));
+  FILE *g = NULL;
+  if (tmp && buf && zeros) {
+    memcpy(tmp, dst_path, plen);
+    memcpy(tmp + plen, ".tmp", 5);
+    g = fopen(tmp, "wb");
+  }
+  if (!g) {
+    fprintf(stderr, "error: cannot open '%s' for writing\n", dst_path);
+    llmq_set_error(LLMQ_ERR_IO, "llmq_llma_upgrade_v1: cannot write '%s'", dst_path);
+    free(tmp);
+    free(buf);
+    free(zeros);
+    fclose(f);
+    return 1;
+  }
+  const uint32_t hdr2[2] = {0x414D4C4Cu, 2u};
+  int st = fwrite(hdr2, 4, 2, g) == 2 && fwrite(cfg, 4, 8, g) == 8 && fwrite(fcfg, 4, 2, g) == 2 ? 1 : -1;
+  if (st > 0) st = copy_floats(f, g, vocab * dm, buf); /* wte */
+  for (int l = 0; l < n_layers && st > 0; l++) {
+    st = copy_floats(f, g, dm, buf);                           /* attn_norm */
+    if (st > 0) st = copy_floats(f, g, dm * qd, buf);          /* Wq */
+    if (st > 0) st = copy_floats(f, g, dm * kvd, buf);         /* Wk */
+    if (st > 0) st = copy_floats(f, g, dm * kvd, buf);         /* Wv */
+    if (st > 0 && fwrite(zeros, sizeof(float), qd + 2 * kvd, g) != qd + 2 * kvd) st = -1; /* b_q, b_k, b_v */
+    if (st > 0) st = copy_floats(f, g, qd * dm, buf);          /* Wo */
+    if (st > 0) st = copy_floats(f, g, dm, buf);               /* ffn_norm */
+    if (st > 0) st = copy_floats(f, g, dm * dff, buf);         /* Wgate */
+    if (st > 0) st = copy_floats(f, g, dm * dff, buf);         /* Wup */
+    if (st > 0) st = copy_floats(f, g, dff * dm, buf);         /* Wdown */
+  }
+  if (st > 0) st = copy_floats(f, g, dm, buf);                 /* final_norm */
+  if (st > 0) st = copy_floats(f, g, dm * vocab, buf);         /* lm_head */
+  int trailing = 0;
+  if (st > 0) trailing = fgetc(f) != EOF;
+  fclose(f);
+  int ok = st > 0 && !trailing;
+  ok = (fclose(g) == 0) && ok;
+  if (ok && rename(tmp, dst_path) != 0) {
+    remove(dst_path);
+    ok = rename(tmp, dst_path) == 0;
+  }
+  if (!ok) {
+    remove(tmp);
+    if (st == 0)
+      fprintf(stderr, "error: input '%s' truncated\n", src_path);
+    else if (trailing)
+      fprintf(stderr, "error: trailing bytes in '%s' — layout assumption wrong\n", src_path);
+    else
+      fprintf(stderr, "error: failed while writing '%s'\n", dst_path);
+    llmq_set_error(LLMQ_ERR_IO, "llmq_llma_upgrade_v1: %s", st == 0 ? "input truncated" : trailing ? "trailing bytes"
+                                                                                          : "write failed");
+  }
+  free(tmp);
+  free(buf);
+  free(zeros);
+  return ok ? 0 : 1;
+}

@@ -95,7 +95,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
                : "memory");
 }
-// One contiguous global->shared bulk copy completing on `bar` (no multicast).
+// One contiguous global->shared bulk copy into this CTA's own shared memory, completing on `bar`.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -917,10 +917,11 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
 // decode: a cluster of nsl = ceil(hd / 32) CTAs per head, CTA r owning the
 // output dimensions [32 r, 32 r + 32) and the key positions [pa, pb) of the
 // r-th part of [0, pos].
-//  1. q (and, in the part holding `pos`, this step's k) get RoPE; the part's
-//     keys stream through a two-chunk ring and each score is the sequential
-//     dot product over hd, times 1/sqrt(hd), into e[p] (own shared memory).
-//     The whole value slice [0, pos] x [32 r, 32 r + 32) is staged meanwhile.
+//  1. The value slice [0, pos) x [32 r, 32 r + 32) and the part's first key
+//     chunk are staged before the wait on the QKV product; then q (and, in the
+//     part holding `pos`, this step's k) get RoPE, the part's keys stream
+//     through a two-chunk ring and each score is the sequential dot product
+//     over hd, times 1/sqrt(hd), into e[p] (own shared memory).
 //  2. The cluster's maximum: each CTA stores its part's maximum into every
 //     CTA (distributed shared memory); after a cluster barrier each takes the
 //     maximum, exponentiates its own part and stores it into every CTA's e.

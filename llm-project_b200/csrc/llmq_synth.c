@@ -11,6 +11,7 @@
 #include <math.h>
 #include <pthread.h>
 #include <stdatomic.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 #include <unistd.h>
@@ -386,4 +387,116 @@ LLMQ_API void llmq_synth_qtensor(QTensor *t, uint64_t seed) {
     const double u = (double)(splitmix64(skey + (uint64_t)j) >> 11) * 0x1p-53;
     t->scale[j] = (float)(1e-3 + 9e-3 * u);
   }
+}
+
+/* ----------------------------------------------------------- streaming writer */
+static int wr_all(FILE *f, const void *p, size_t size, size_t n) { return n == 0 || fwrite(p, size, n, f) == n; }
+
+/* Writes one synthetic 2-D tensor (tensor id tid, full shape K x N) as LLMQ
+ * stores it: the per-column scales, then the row-major int8 codes.  Only this
+ * tensor is in memory meanwhile. */
+static int save_qtensor(FILE *f, uint64_t seed, int tid, float stddev, int fast, int K, int N) {
+  QTensor t = qtensor_create(K, N);
+  if (!t.q || !t.scale) {
+    free(t.q);
+    free(t.scale);
+    return 0;
+  }
+  if (fast)
+    synth_fast_part(&t, seed, tid, N, 0, 0);
+  else
+    synth_qtensor_normal(&t, seed, tid, stddev);
+  const int ok = wr_all(f, t.scale, sizeof(float), (size_t)N) && wr_all(f, t.q, 1, (size_t)K * N);
+  free(t.q);
+  free(t.scale);
+  return ok;
+}
+
+/* Writes one synthetic 1-D tensor: ones (norm gains), or the seeded biases
+ * (zero when with_bias is 0). */
+static int save_vec(FILE *f, uint64_t seed, int tid, float stddev, int n, int kind) {
+  Tensor t;
+  vec_alloc(&t, n);
+  if (!t.data) return 0;
+  if (kind == 1)
+    fill_ones(&t);
+  else if (kind == 2)
+    synth_vec_part(&t, seed, tid, stddev, 0);
+  const int ok = wr_all(f, t.data, sizeof(float), (size_t)n);
+  free(t.data);
+  free(t.shape);
+  return ok;
+}
+
+/* The model llmq_synth_model (fast = 0) or llmq_synth_model_fast_shard with
+ * one shard (fast = 1) builds, written straight to an LLMQ v2 file in the
+ * canonical order of llama.c:199-219 (the layout q_llama_model_load reads,
+ * llama.c:603-657): header, then each tensor as it is generated, so no more
+ * than one tensor is ever in memory (a 70B-shaped file needs ~1 GB, not 70).
+ * Written to path.tmp, then renamed over path, like llama.c:230-269.  Returns 0
+ * on success, LLMQ_ERR_ARG / LLMQ_ERR_IO / LLMQ_ERR_OOM on failure. */
+LLMQ_API int llmq_synth_model_save(const LlmqConfig *c, uint64_t seed, float stddev, int with_bias, int fast,
+                                   const char *path) {
+  if (!c || !path || c->vocab <= 0 || c->d_model <= 0 || c->n_layers <= 0 || c->n_heads <= 0 || c->n_kv <= 0 ||
+      c->head_dim <= 0 || c->d_ff <= 0 || c->max_seq <= 0 || c->n_heads % c->n_kv != 0) {
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_synth_model_save: invalid configuration");
+    return LLMQ_ERR_ARG;
+  }
+  if (fast) {
+    stddev = 0.0f;
+    with_bias = 0;
+  }
+  const size_t plen = strlen(path);
+  char *tmp = (char *)malloc(plen + 5);
+  if (!tmp) {
+    llmq_set_error(LLMQ_ERR_OOM, "llmq_synth_model_save: out of host memory");
+    return LLMQ_ERR_OOM;
+  }
+  memcpy(tmp, path, plen);
+  memcpy(tmp + plen, ".tmp", 5);
+  FILE *f = fopen(tmp, "wb");
+  if (!f) {
+    llmq_set_error(LLMQ_ERR_IO, "llmq_synth_model_save: cannot open '%s' for writing", tmp);
+    free(tmp);
+    return LLMQ_ERR_IO;
+  }
+  const int dm = c->d_model, qd = c->n_heads * c->head_dim, kvd = c->n_kv * c->head_dim, dff = c->d_ff;
+  const uint32_t hdr[2] = {0x514D4C4Cu, 2u}; /* 'LLMQ', version 2 (llama.c:192-194) */
+  const int32_t cfg[8] = {c->vocab, dm, c->n_layers, c->n_heads, c->n_kv, c->head_dim, dff, c->max_seq};
+  const float fcfg[2] = {c->rope_base, c->eps};
+  int ok = wr_all(f, hdr, sizeof(uint32_t), 2) && wr_all(f, cfg, sizeof(int32_t), 8) &&
+           wr_all(f, fcfg, sizeof(float), 2);
+  ok = ok && save_qtensor(f, seed, 0, stddev, fast, c->vocab, dm);
+  const int bias_kind = with_bias ? 2 : 0;
+  for (int l = 0; l < c->n_layers && ok; l++) {
+    const int base = 1 + 12 * l;
+    ok = ok && save_vec(f, seed, base + 0, stddev, dm, 1);               /* attn_norm */
+    ok = ok && save_qtensor(f, seed, base + 1, stddev, fast, dm, qd);    /* Wq */
+    ok = ok && save_qtensor(f, seed, base + 2, stddev, fast, dm, kvd);   /* Wk */
+    ok = ok && save_qtensor(f, seed, base + 3, stddev, fast, dm, kvd);   /* Wv */
+    ok = ok && save_vec(f, seed, base + 4, stddev, qd, bias_kind);       /* b_q */
+    ok = ok && save_vec(f, seed, base + 5, stddev, kvd, bias_kind);      /* b_k */
+    ok = ok && save_vec(f, seed, base + 6, stddev, kvd, bias_kind);      /* b_v */
+    ok = ok && save_qtensor(f, seed, base + 7, stddev, fast, qd, dm);    /* Wo */
+    ok = ok && save_vec(f, seed, base + 8, stddev, dm, 1);               /* ffn_norm */
+    ok = ok && save_qtensor(f, seed, base + 9, stddev, fast, dm, dff);   /* Wgate */
+    ok = ok && save_qtensor(f, seed, base + 10, stddev, fast, dm, dff);  /* Wup */
+    ok = ok && save_qtensor(f, seed, base + 11, stddev, fast, dff, dm);  /* Wdown */
+  }
+  ok = ok && save_vec(f, seed, 1 + 12 * c->n_layers, stddev, dm, 1); /* final_norm */
+  ok = ok && save_qtensor(f, seed, 2 + 12 * c->n_layers, stddev, fast, dm, c->vocab);
+  ok = (fflush(f) == 0) && ok;
+  ok = (fclose(f) == 0) && ok;
+  if (ok && rename(tmp, path) != 0) {
+    remove(path);
+    ok = rename(tmp, path) == 0;
+  }
+  if (!ok) {
+    remove(tmp);
+    llmq_set_error(LLMQ_ERR_IO, "llmq_synth_model_save: failed while writing '%s'", path);
+    free(tmp);
+    return LLMQ_ERR_IO;
+  }
+  free(tmp);
+  return LLMQ_OK;
 }

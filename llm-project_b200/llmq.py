@@ -98,6 +98,8 @@ SIGNATURES = {
     "llmq_synth_model": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_float, C.c_int,
                                    C.POINTER(QLlamaModel)]),
     "llmq_synth_qtensor": (None, [C.POINTER(QTensor), C.c_uint64]),
+    "llmq_synth_model_save": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_float, C.c_int, C.c_int, C.c_char_p]),
+    "llmq_llma_upgrade_v1": (C.c_int, [C.c_char_p, C.c_char_p]),
     "llmq_synth_model_shard": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_float, C.c_int, C.c_int, C.c_int,
                                          C.POINTER(QLlamaModel)]),
     "llmq_synth_model_fast_shard": (C.c_int, [C.POINTER(LlmqConfig), C.c_uint64, C.c_int, C.c_int,

@@ -8,6 +8,7 @@ import os
 import re
 import struct
 import subprocess
+import sys
 
 import numpy as np
 import pytest
@@ -153,3 +154,86 @@ def test_link_check_compiles_against_the_reference_headers(tmp_path):
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stdout + r.stderr
     assert os.access(tmp_path / "link_check", os.X_OK)
+
+
+@pytest.mark.parametrize("with_bias,fast", [(False, False), (True, False), (False, True)])
+def test_streaming_synth_writer_matches_whole_model_save(lib, tmp_path, with_bias, fast):
+    """llmq_synth_model_save writes the synthetic model tensor by tensor; the
+    file is byte for byte what q_llama_model_save writes for the whole model
+    built in memory (tools/convert_llama.py:73-97 layout)."""
+    cfg = dict(vocab=300, d_model=64, n_layers=2, n_heads=4, n_kv=2, head_dim=16, d_ff=96, max_seq=32,
+               rope_base=10000.0, eps=1e-5)
+    c = llmq.config(**cfg)
+    m = llmq.QLlamaModel()
+    if fast:
+        assert lib.llmq_synth_model_fast_shard(C.byref(c), 77, 0, 1, C.byref(m)) == 0
+    else:
+        assert lib.llmq_synth_model(C.byref(c), 77, 0.02, int(with_bias), C.byref(m)) == 0
+    whole, streamed = tmp_path / "whole.llmq", tmp_path / "streamed.llmq"
+    assert lib.q_llama_model_save(str(whole).encode(), C.byref(m)) == 0
+    assert lib.llmq_synth_model_save(C.byref(c), 77, 0.02, int(with_bias), int(fast), str(streamed).encode()) == 0
+    assert whole.read_bytes() == streamed.read_bytes()
+    assert not (tmp_path / "streamed.llmq.tmp").exists()
+    lib.q_llama_model_free(C.byref(m))
+
+
+def _llma_v2_bytes(cfg, rng, bias=True):
+    """An LLMA v2 file (llama.c:192-269 layout) with random tensors and zero
+    biases, and the v1 file it came from (the same without the biases)."""
+    V, dm, L, H, KV, hd, dff, ms = (cfg[k] for k in ("vocab", "d_model", "n_layers", "n_heads", "n_kv", "head_dim",
+                                                      "d_ff", "max_seq"))
+    qd, kvd = H * hd, KV * hd
+    f32 = lambda n: rng.standard_normal(n).astype("<f4").tobytes()  # noqa: E731
+    head = struct.pack("<8i", V, dm, L, H, KV, hd, dff, ms) + struct.pack("<2f", 10000.0, 1e-5)
+    v1, v2 = [struct.pack("<II", 0x414D4C4C, 1) + head], [struct.pack("<II", 0x414D4C4C, 2) + head]
+    wte = f32(V * dm)
+    v1.append(wte)
+    v2.append(wte)
+    for _ in range(L):
+        pre = f32(dm) + f32(dm * qd) + f32(dm * kvd) + f32(dm * kvd)
+        post = f32(qd * dm) + f32(dm) + f32(dm * dff) + f32(dm * dff) + f32(dff * dm)
+        v1 += [pre, post]
+        v2 += [pre, b"\0" * 4 * (qd + 2 * kvd), post]
+    tail = f32(dm) + f32(dm * V)
+    v1.append(tail)
+    v2.append(tail)
+    return b"".join(v1), b"".join(v2)
+
+
+def test_llma_upgrade_v1_to_v2(lib, tmp_path):
+    """llmq_llma_upgrade_v1 (and `llmq_run upgrade-llma`) turns an LLMA v1 file
+    into v2 with zero q/k/v biases (tools/upgrade_llma.py), and refuses the
+    files the tool refuses."""
+    cfg = dict(vocab=50, d_model=16, n_layers=3, n_heads=4, n_kv=2, head_dim=4, d_ff=24, max_seq=16)
+    v1, v2 = _llma_v2_bytes(cfg, np.random.default_rng(4))
+    src, dst = tmp_path / "v1.bin", tmp_path / "v2.bin"
+    src.write_bytes(v1)
+    assert lib.llmq_llma_upgrade_v1(str(src).encode(), str(dst).encode()) == 0
+    assert dst.read_bytes() == v2
+    cli = os.path.join(ROOT, "llm-project_b200", "bin", "llmq_run")
+    r = subprocess.run([cli, "upgrade-llma", str(src), str(tmp_path / "cli.bin")], capture_output=True, text=True)
+    assert r.returncode == 0 and (tmp_path / "cli.bin").read_bytes() == v2
+    for bad, msg in ((v2, b"already version 2"), (b"XXXX" + v1[4:], b"not an LLMA"), (v1[:-4], b"truncated"),
+                     (v1 + b"\0", b"trailing bytes"), (v1[:20], b"too small")):
+        src.write_bytes(bad)
+        r = subprocess.run([cli, "upgrade-llma", str(src), str(tmp_path / "bad.bin")], capture_output=True)
+        assert r.returncode == 1 and msg in r.stderr, (msg, r.stderr)
+        assert not (tmp_path / "bad.bin").exists()
+
+
+def test_llma_upgrade_matches_the_reference_tool(lib, tmp_path):
+    """Byte for byte what the reference's own tools/upgrade_llma.py writes (run
+    where a reference checkout is present)."""
+    from conftest import reference_dir
+    ref = reference_dir()
+    if ref is None or not os.path.exists(os.path.join(ref, "tools", "upgrade_llma.py")):
+        pytest.skip("no reference checkout on this machine")
+    cfg = dict(vocab=40, d_model=8, n_layers=2, n_heads=2, n_kv=1, head_dim=4, d_ff=12, max_seq=8)
+    v1, _ = _llma_v2_bytes(cfg, np.random.default_rng(9))
+    src = tmp_path / "v1.bin"
+    src.write_bytes(v1)
+    r = subprocess.run([sys.executable, os.path.join(ref, "tools", "upgrade_llma.py"), str(src),
+                        str(tmp_path / "ref.bin")], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    assert lib.llmq_llma_upgrade_v1(str(src).encode(), str(tmp_path / "ours.bin").encode()) == 0
+    assert (tmp_path / "ours.bin").read_bytes() == (tmp_path / "ref.bin").read_bytes()
