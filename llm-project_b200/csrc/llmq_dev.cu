@@ -2636,15 +2636,16 @@ extern "C" LLMQ_API int llmq_phase_grid(unsigned long long grid) {
   return cudaMemcpyToSymbol(g_phase_grid, &grid, sizeof(grid)) == cudaSuccess ? 0 : 2;
 }
 // Profiling builds only: copies the launch spans (4096 x {gridid, first start,
-// last end}) to out (when given), then resets them.
+// last end, kernel tag}) to out (when given), then resets them.
 extern "C" LLMQ_API int llmq_launch_spans(unsigned long long *out) {
-  static unsigned long long tab[4096][3];
+  static unsigned long long tab[4096][4];
   if (cudaDeviceSynchronize() != cudaSuccess) return 2;
   if (out && cudaMemcpyFromSymbol(out, g_launch_tab, sizeof(tab)) != cudaSuccess) return 2;
   for (auto &e : tab) {
     e[0] = 0;
     e[1] = ~0ull;
     e[2] = 0;
+    e[3] = 0;
   }
   return cudaMemcpyToSymbol(g_launch_tab, tab, sizeof(tab)) == cudaSuccess ? 0 : 2;
 }

@@ -36,7 +36,7 @@ __device__ unsigned long long g_phase_grid;  // record only this launch (%gridid
   } while (0)
 // Launch spans: per grid launch (%gridid), the earliest CTA start and the
 // latest CTA end, so a graph replay's kernels can be laid out in time.
-__device__ unsigned long long g_launch_tab[4096][3];  // gridid, first start, last end
+__device__ unsigned long long g_launch_tab[4096][4];  // gridid, first start, last end, kernel tag
 __device__ __forceinline__ unsigned long long llmq_now() {
   unsigned long long t_;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));
@@ -47,19 +47,27 @@ __device__ __forceinline__ unsigned long long llmq_gridid() {
   asm volatile("mov.u64 %0, %%gridid;" : "=l"(g_));
   return g_;
 }
-#define LLMQ_LAUNCH_ENTER()                                              \
+#define LLMQ_LAUNCH_ENTER_TAG(tag)                                       \
   do {                                                                   \
     if (threadIdx.x == 0) {                                              \
       const unsigned long long g_ = llmq_gridid();                       \
       unsigned long long *e_ = g_launch_tab[g_ & 4095];                  \
       e_[0] = g_;                                                        \
+      e_[3] = (tag);                                                     \
       atomicMin(&e_[1], llmq_now());                                     \
     }                                                                    \
   } while (0)
+#define LLMQ_LAUNCH_ENTER() LLMQ_LAUNCH_ENTER_TAG(0)
 #define LLMQ_LAUNCH_EXIT()                                               \
   do {                                                                   \
     if (threadIdx.x == 0) atomicMax(&g_launch_tab[llmq_gridid() & 4095][2], llmq_now()); \
   } while (0)
+// Both ends of a launch span around a whole kernel body (every return path).
+struct LaunchSpanGuard {
+  __device__ explicit LaunchSpanGuard(int tag) { LLMQ_LAUNCH_ENTER_TAG(tag); }
+  __device__ ~LaunchSpanGuard() { LLMQ_LAUNCH_EXIT(); }
+};
+#define LLMQ_LAUNCH_SPAN(tag) LaunchSpanGuard llmq_span_guard_(tag)
 #else
 #define LLMQ_TSTAMP(i) \
   do {               \
@@ -67,8 +75,14 @@ __device__ __forceinline__ unsigned long long llmq_gridid() {
 #define LLMQ_LAUNCH_ENTER() \
   do {                    \
   } while (0)
+#define LLMQ_LAUNCH_ENTER_TAG(tag) \
+  do {                           \
+  } while (0)
 #define LLMQ_LAUNCH_EXIT() \
   do {                   \
+  } while (0)
+#define LLMQ_LAUNCH_SPAN(tag) \
+  do {                      \
   } while (0)
 #endif
 
@@ -328,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   __shared__ int s_abort;
 
   LLMQ_TSTAMP(0);
-  LLMQ_LAUNCH_ENTER();
+  LLMQ_LAUNCH_ENTER_TAG(1);
   const int tid = threadIdx.x;
   const int S = a.stages;
   uint8_t *stage0 = sm;
@@ -940,7 +954,7 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   __shared__ float s_inv;
   cg::cluster_group cluster = cg::this_cluster();
   LLMQ_TSTAMP(0);
-  LLMQ_LAUNCH_ENTER();
+  LLMQ_LAUNCH_ENTER_TAG(2);
   pdl_launch_dependents();
   // Before the wait: the previous kernel (this layer's QKV product) starts its
   // dependents only once all its CTAs are past their own wait, so the step
@@ -1036,7 +1050,7 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
 // record the generated id, and reset the argmax cell and error word.
 __global__ void k_step_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
                               int max_seq, unsigned *tp_seq, unsigned tp_products) {
-  LLMQ_LAUNCH_ENTER();
+  LLMQ_LAUNCH_ENTER_TAG(3);
   pdl_wait();
   if (tp_seq) *tp_seq += tp_products;  // the step's row-parallel products are done on this rank
   const unsigned long long key = *argmax;

@@ -39,6 +39,7 @@ struct RowNormArgs {
 // prologue), then its activation codes (quant.c:69-78).  One CTA per row;
 // dynamic shared memory 2 * K floats.
 __global__ void __launch_bounds__(kRowThreads) k_rows_norm_codes(const RowNormArgs a) {
+  LLMQ_LAUNCH_SPAN(10);
   extern __shared__ __align__(16) float xs[];
   __shared__ float s_red[32];
   __shared__ float s_r;
@@ -105,6 +106,7 @@ __device__ __forceinline__ size_t row_cache_offset(const RowDesc &d, int layer, 
 // RoPE of q and k (rope.c:48-68) at the row's position; the rotated k and the
 // v of the row are appended to its cache (llama.c:551-552).  One CTA per row.
 __global__ void __launch_bounds__(256) k_rows_append(const RowAttnArgs a) {
+  LLMQ_LAUNCH_SPAN(11);
   pdl_launch_dependents();
   pdl_wait();
   const int r = blockIdx.x, tid = threadIdx.x;
@@ -140,6 +142,7 @@ __host__ __device__ inline size_t rows_scores_smem(int group, int hd) {
   return ((size_t)group * hd + (size_t)kRowScoreKeys * (hd + 4)) * sizeof(float);
 }
 __global__ void __launch_bounds__(kRowScoreThreads) k_rows_scores(const RowAttnArgs a) {
+  LLMQ_LAUNCH_SPAN(12);
   extern __shared__ __align__(16) float sm_s[];
   pdl_launch_dependents();
   pdl_wait();
@@ -186,6 +189,7 @@ __host__ __device__ inline size_t rows_pv_smem(int group, int hd, int smax) {
 }
 
 __global__ void __launch_bounds__(1024) k_rows_pv(const RowAttnArgs a) {
+  LLMQ_LAUNCH_SPAN(13);
   extern __shared__ __align__(16) float sm_a[];
   __shared__ __align__(8) uint64_t full[kPvStages];
   __shared__ float s_max[kAttnMaxGroup][32];
@@ -284,6 +288,7 @@ __global__ void __launch_bounds__(1024) k_rows_pv(const RowAttnArgs a) {
 // Greedy ids of the rows (first maximum: sampler.c:8-21) from the lm-head
 // epilogue's keys; the key cells are re-zeroed for the next pass.
 __global__ void k_rows_finish(unsigned long long *argmax, int rows, int *ids) {
+  LLMQ_LAUNCH_SPAN(14);
   pdl_wait();
   for (int r = threadIdx.x; r < rows; r += blockDim.x) {
     const unsigned long long key = argmax[r];

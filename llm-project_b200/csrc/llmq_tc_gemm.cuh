@@ -99,6 +99,7 @@ __device__ __forceinline__ int4 tc_pack16(const float *x, int k0, int K, float i
 // absmax_in when given.  One CTA per row.
 __global__ void __launch_bounds__(256) k_act_codes(const float *a, int rows, int K, int Kpad, int KT, int8_t *codes,
                                                    float *as_out, const float *absmax_in) {
+  LLMQ_LAUNCH_SPAN(20);
   __shared__ float s_red[32];
   pdl_launch_dependents();
   pdl_wait();
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(256) k_act_codes(const float *a, int rows, int
 // Absmax of each row of a (row stride K), the local part of a row-parallel
 // product's activation scale (quant.c:69-71).  One CTA per row.
 __global__ void __launch_bounds__(256) k_rows_absmax(const float *a, int K, float *out) {
+  LLMQ_LAUNCH_SPAN(21);
   __shared__ float s_red[32];
   pdl_launch_dependents();
   pdl_wait();
@@ -221,6 +223,7 @@ __device__ __forceinline__ void red_add_s32(int *p, int v) {
 // order does not matter) and k_tc_epilogue, the next launch, applies it.
 template <int KT>
 __global__ void __launch_bounds__(kTcThreads) k_tc_gemm(const TcArgs a) {
+  LLMQ_LAUNCH_SPAN(22);
   constexpr int WB = kNT * KT;       // weight tile bytes
   constexpr int AB = kTcRows * KT;   // activation tile bytes
   constexpr int SB = WB + AB;
@@ -364,6 +367,7 @@ __global__ void __launch_bounds__(kTcThreads) k_tc_gemm(const TcArgs a) {
 // int32 block from `acc`, re-zeroes it and applies the epilogue.
 // Grid ceil(rows * n_slabs / 4) x 128 threads.
 __global__ void __launch_bounds__(128) k_tc_epilogue(const TcArgs a) {
+  LLMQ_LAUNCH_SPAN(23);
   pdl_launch_dependents();
   pdl_wait();
   const int lane = threadIdx.x & 31;
