@@ -299,6 +299,9 @@ DevCtx *get_ctx() {
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_norm_codes, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_append, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_scores, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_pf_scores, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_pf_softmax, sm);
+  ea = ea != cudaSuccess ? ea : set_attr(k_pf_pv, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_pv, sm);
   ea = ea != cudaSuccess ? ea : set_attr(k_rows_finish, 0);
   ea = ea != cudaSuccess ? ea : set_attr(k_step_finish, 0);
@@ -1784,6 +1787,13 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   aa.err = M->err;
   const int group = cfg.n_heads / cfg.n_kv;
   const size_t sc_sm = rows_scores_smem(group, hd), pv_sm = rows_pv_smem(group, hd, cfg.max_seq);
+  // A prefill (every row the next position of one sequence's cache) takes the
+  // row-block tiled scores kernel.
+  bool pf_tiled = group <= kPfVecs && pf_scores_smem(hd) + 1024 <= (size_t)g_smem_optin;
+  for (int r = 1; r < rows && pf_tiled; ++r)
+    pf_tiled = rows_h[r].k == rows_h[0].k && rows_h[r].v == rows_h[0].v && rows_h[r].pos == rows_h[0].pos + r;
+  const int pf_rpb = pf_rows_per_block(group);
+  const size_t pf_sm = pf_scores_smem(hd);
   const int attn_threads = (group * hd / 2 + 31) / 32 * 32;  // k_rows_pv: two output dims per thread
   if (hd % 4 != 0 || group > kAttnMaxGroup || attn_threads > 1024 || pv_sm + 4096 > (size_t)g_smem_optin) {
     llmq_set_error(LLMQ_ERR_ARG, "libllmq_cuda: batched attention needs head_dim %% 4 == 0, group <= %d, "
@@ -1839,9 +1849,20 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
     if (!gemm(M->qkv[l], rows, TC_BIAS, M->bias_qkv[l], R.qkv, qd + 2 * kvd, nullptr)) return 0;
     aa.layer = l;
     CK(launch_pdl(k_rows_append, dim3(rows), dim3(256), 0, st, aa));
-    CK(launch_pdl(k_rows_scores, dim3((cfg.max_seq + kRowScoreKeys - 1) / kRowScoreKeys, cfg.n_kv, rows),
-                  dim3(kRowScoreThreads), sc_sm, st, aa));
-    CK(launch_pdl(k_rows_pv, dim3(cfg.n_kv, rows), dim3(attn_threads), pv_sm, st, aa));
+    if (pf_tiled)  // a prefill: each key chunk staged once per block of rows
+      CK(launch_pdl(k_pf_scores, dim3((cfg.max_seq + kPfVecs - 1) / kPfVecs, cfg.n_kv, (rows + pf_rpb - 1) / pf_rpb),
+                    dim3(256), pf_sm, st, aa, rows));
+    else
+      CK(launch_pdl(k_rows_scores, dim3((cfg.max_seq + kRowScoreKeys - 1) / kRowScoreKeys, cfg.n_kv, rows),
+                    dim3(kRowScoreThreads), sc_sm, st, aa));
+    if (pf_tiled && hd == 128 && (size_t)group * ((cfg.max_seq + 3) & ~3) * 4 + 4096 <= (size_t)g_smem_optin) {
+      // softmax in place, then the row-block tiled values
+      CK(launch_pdl(k_pf_softmax, dim3(rows, cfg.n_kv), dim3(256), (size_t)group * ((cfg.max_seq + 3) & ~3) * 4, st,
+                    aa));
+      CK(launch_pdl(k_pf_pv, dim3(cfg.n_kv, (rows + pf_rpb - 1) / pf_rpb), dim3(256), pf_pv_smem(hd), st, aa, rows));
+    } else {
+      CK(launch_pdl(k_rows_pv, dim3(cfg.n_kv, rows), dim3(attn_threads), pv_sm, st, aa));
+    }
     if (M->tp_world > 1) {
       if (!row_parallel_rows(M->wo[l], R.ao)) return 0;
     } else {

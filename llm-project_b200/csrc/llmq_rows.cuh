@@ -171,6 +171,95 @@ __global__ void __launch_bounds__(kRowScoreThreads) k_rows_scores(const RowAttnA
   }
 }
 
+// Scores of a prefill pass (every row one position of the same sequence and
+// cache): a CTA takes a block of consecutive rows, one KV head and 64 key
+// positions, so each key chunk is staged once for the block's whole query
+// group instead of once per row.  64 query vectors (rows x the group's heads)
+// times 64 keys; thread (i, j) forms the 4 x 4 scores of query vectors
+// 4 i .. 4 i + 3 and keys 4 j .. 4 j + 3, each the sequential dot product over
+// the head dimension in index order (llama.c:561), times 1/sqrt(hd); keys past
+// a row's position are skipped (llama.c:558).  q and k are staged transposed
+// ([hd][64]) so every step is two 16-byte shared loads.  Grid
+// (ceil(smax / 64), n_kv, row blocks of pf_rows_per_block(group) rows); 256
+// threads; head_dim % 4 == 0.
+constexpr int kPfVecs = 64;  // query vectors and keys per CTA
+__host__ __device__ inline int pf_rows_per_block(int group) { return kPfVecs / group; }
+__host__ __device__ inline size_t pf_scores_smem(int hd) { return (size_t)2 * hd * kPfVecs * sizeof(float); }
+__global__ void __launch_bounds__(256) k_pf_scores(const RowAttnArgs a, int rows) {
+  LLMQ_LAUNCH_SPAN(15);
+  extern __shared__ __align__(16) float sm_p[];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x, kvh = blockIdx.y;
+  const int hd = a.hd, group = a.n_heads / a.n_kv, qd = a.n_heads * hd;
+  const int rpb = pf_rows_per_block(group), r0 = blockIdx.z * rpb, r1 = min(r0 + rpb, rows);
+  const int k0 = blockIdx.x * kPfVecs;
+  const RowDesc d0 = a.rd[r0];
+  const int pos_hi = a.rd[r1 - 1].pos;  // rows are consecutive positions
+  if (d0.pos < 0 || pos_hi >= d0.max_seq || k0 > pos_hi) return;  // bad positions: flagged by k_rows_append
+  float *qT = sm_p;                          // [hd][64]
+  float *kT = sm_p + (size_t)hd * kPfVecs;   // [hd][64]
+  const int nv = (r1 - r0) * group;          // query vectors in use
+  const int hd4 = hd / 4;
+  // consecutive threads take consecutive vectors: conflict-free transposed stores
+  for (int t = tid; t < kPfVecs * hd4; t += 256) {
+    const int v = t & (kPfVecs - 1), e = 4 * (t / kPfVecs);
+    float4 q = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (v < nv) {
+      const int r = r0 + v / group, g = v - (v / group) * group;
+      q = *reinterpret_cast<const float4 *>(a.qr + (size_t)r * qd + (size_t)(kvh * group + g) * hd + e);
+    }
+    qT[(size_t)(e + 0) * kPfVecs + v] = q.x;
+    qT[(size_t)(e + 1) * kPfVecs + v] = q.y;
+    qT[(size_t)(e + 2) * kPfVecs + v] = q.z;
+    qT[(size_t)(e + 3) * kPfVecs + v] = q.w;
+  }
+  const float *kc = d0.k + row_cache_offset(d0, a.layer, a.n_kv, kvh, hd);
+  for (int t = tid; t < kPfVecs * hd4; t += 256) {
+    const int j = t & (kPfVecs - 1), e = 4 * (t / kPfVecs);
+    float4 k = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (k0 + j <= pos_hi) k = *reinterpret_cast<const float4 *>(kc + (size_t)(k0 + j) * hd + e);
+    kT[(size_t)(e + 0) * kPfVecs + j] = k.x;
+    kT[(size_t)(e + 1) * kPfVecs + j] = k.y;
+    kT[(size_t)(e + 2) * kPfVecs + j] = k.z;
+    kT[(size_t)(e + 3) * kPfVecs + j] = k.w;
+  }
+  __syncthreads();
+  const int ti = tid >> 4, tj = tid & 15;
+  float2 acc[4][2];  // query vector i, key pairs (4 tj, 4 tj + 1) and (4 tj + 2, 4 tj + 3)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i][0] = acc[i][1] = make_float2(0.0f, 0.0f);
+  const float4 *q4 = reinterpret_cast<const float4 *>(qT) + ti;
+  const float4 *k4 = reinterpret_cast<const float4 *>(kT) + tj;
+#pragma unroll 4
+  for (int e = 0; e < hd; ++e) {
+    const float4 qv = q4[(size_t)e * (kPfVecs / 4)], kv = k4[(size_t)e * (kPfVecs / 4)];
+    const float qa[4] = {qv.x, qv.y, qv.z, qv.w};
+    const float2 k01 = make_float2(kv.x, kv.y), k23 = make_float2(kv.z, kv.w);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 q2 = make_float2(qa[i], qa[i]);
+      acc[i][0] = f2_madd_rn(acc[i][0], q2, k01);  // llama.c:561
+      acc[i][1] = f2_madd_rn(acc[i][1], q2, k23);
+    }
+  }
+  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(static_cast<float>(hd)));  // llama.c:532
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = 4 * ti + i;
+    if (v >= nv) continue;
+    const int r = r0 + v / group, g = v - (v / group) * group;
+    const int pos = a.rd[r].pos;
+    float *srow = a.scores + ((size_t)r * a.n_heads + (size_t)kvh * group + g) * a.smax;
+    const float dots[4] = {acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int p = k0 + 4 * tj + j;
+      if (p <= pos) srow[p] = __fmul_rn(dots[j], scale);
+    }
+  }
+}
+
 // Softmax and values of one row for one KV head and its whole query group
 // (llama.c:566-575), in one CTA of group * hd / 2 threads (rounded up to a warp):
 // the group's scores come into shared memory; per head the max, expf(s - max),
@@ -283,6 +372,157 @@ __global__ void __launch_bounds__(1024) k_rows_pv(const RowAttnArgs a) {
     return;
   }
   if (g < group) *reinterpret_cast<float2 *>(a.out + (size_t)r * qd + (size_t)(kvh * group + g) * hd + e) = o;
+}
+
+// Softmax of one prefill row and one KV head's query group (llama.c:566-572)
+// in place: for each of the group's heads the scores [0, pos] become
+// w = expf(s - max) * (1 / sum), the sum of the exponentials taken
+// sequentially in position order (one thread per head, the group's sums side
+// by side).  Grid (rows, n_kv), 256 threads, dynamic shared memory
+// group * smax4 floats.
+__global__ void __launch_bounds__(256) k_pf_softmax(const RowAttnArgs a) {
+  LLMQ_LAUNCH_SPAN(16);
+  extern __shared__ __align__(16) float ex[];
+  __shared__ float s_max[kAttnMaxGroup][8];
+  __shared__ float s_inv[kAttnMaxGroup];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const RowDesc d = a.rd[r];
+  if (d.pos < 0 || d.pos >= d.max_seq) return;  // flagged by k_rows_append
+  const int np = d.pos + 1, group = a.n_heads / a.n_kv, smax4 = (a.smax + 3) & ~3;
+  float *sc = a.scores + ((size_t)r * a.n_heads + (size_t)kvh * group) * a.smax;
+  for (int g = 0; g < group; ++g) {
+    float m = -INFINITY;
+    for (int p = tid; p < np; p += 256) {
+      const float v = sc[(size_t)g * a.smax + p];
+      ex[(size_t)g * smax4 + p] = v;
+      m = fmaxf(m, v);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) s_max[g][warp] = m;
+  }
+  __syncthreads();
+  if (tid < group) {
+    float m = s_max[tid][0];
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, s_max[tid][w]);
+    s_max[tid][0] = m;
+  }
+  __syncthreads();
+  for (int t = tid; t < group * np; t += 256) {
+    const int g = t / np, p = t - g * np;
+    float *e = ex + (size_t)g * smax4 + p;
+    *e = libm_expf(__fsub_rn(*e, s_max[g][0]));  // llama.c:566
+  }
+  __syncthreads();
+  if (tid < group) s_inv[tid] = __fdiv_rn(1.0f, seq_sum_a16(ex + (size_t)tid * smax4, np, 0.0f));  // llama.c:567
+  __syncthreads();
+  for (int t = tid; t < group * np; t += 256) {
+    const int g = t / np, p = t - g * np;
+    sc[(size_t)g * a.smax + p] = __fmul_rn(ex[(size_t)g * smax4 + p], s_inv[g]);  // llama.c:571
+  }
+}
+
+// Weighted values of a prefill pass (llama.c:573-575): a CTA takes a block of
+// consecutive rows and one KV head, and streams the head's value rows
+// [0, last row's position] once through a two-chunk ring for the block's whole
+// query group (64 query vectors).  Thread (i, j) carries query vectors
+// 4 i .. 4 i + 3 and dims {4 j .. 4 j + 3, 64 + 4 j .. 64 + 4 j + 3}: 32
+// chains, each out[v][d] = sum of w[v][p] * v[p][d] over p = 0 .. pos(v) in
+// position order, every product rounded on its own.  The weights come from
+// k_pf_softmax.  Grid (n_kv, row blocks of pf_rows_per_block(group) rows); 256
+// threads; head_dim 128; dynamic shared memory pf_pv_smem(hd).
+constexpr int kPfKeys = 32;
+__host__ __device__ inline size_t pf_pv_smem(int hd) {
+  return (size_t)2 * kPfKeys * (hd + kPfVecs) * sizeof(float);
+}
+__global__ void __launch_bounds__(256) k_pf_pv(const RowAttnArgs a, int rows) {
+  LLMQ_LAUNCH_SPAN(17);
+  extern __shared__ __align__(16) float sm_pv[];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x, kvh = blockIdx.x;
+  const int hd = a.hd, group = a.n_heads / a.n_kv, qd = a.n_heads * hd;
+  const int rpb = pf_rows_per_block(group), r0 = blockIdx.y * rpb, r1 = min(r0 + rpb, rows);
+  const RowDesc d0 = a.rd[r0];
+  const int pos_hi = a.rd[r1 - 1].pos;
+  if (d0.pos < 0 || pos_hi >= d0.max_seq) return;  // flagged by k_rows_append
+  const int nv = (r1 - r0) * group;
+  float *Vs = sm_pv;                               // [2][kPfKeys][hd]
+  float *Ws = sm_pv + (size_t)2 * kPfKeys * hd;    // [2][kPfKeys][64]
+  const float *vc = d0.v + row_cache_offset(d0, a.layer, a.n_kv, kvh, hd);
+  const int nch = (pos_hi + kPfKeys) / kPfKeys;
+  auto stage = [&](int c) {
+    const int b = c & 1, p0 = c * kPfKeys, rows_in = min(kPfKeys, pos_hi + 1 - p0);
+    stage_rows(Vs + (size_t)b * kPfKeys * hd, hd, vc, hd, p0, p0 + rows_in, 0, hd, tid, 256);
+    cp_async_commit();
+    float *w = Ws + (size_t)b * kPfKeys * kPfVecs;
+    for (int t = tid; t < kPfVecs * kPfKeys; t += 256) {
+      const int v = t / kPfKeys, j = t - v * kPfKeys, p = p0 + j;
+      float x = 0.0f;
+      if (v < nv) {
+        const int r = r0 + v / group, g = v - (v / group) * group;
+        if (p <= a.rd[r].pos) x = a.scores[((size_t)r * a.n_heads + (size_t)kvh * group + g) * a.smax + p];
+      }
+      w[(size_t)j * kPfVecs + v] = x;
+    }
+  };
+  const int ti = tid >> 4, tj = tid & 15;
+  int lim[4];  // the last position each of the thread's vectors adds
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = 4 * ti + i;
+    lim[i] = v < nv ? a.rd[r0 + v / group].pos : -1;
+  }
+  float2 acc[4][4];  // dims pairs (4 tj, 4 tj + 1), (4 tj + 2, + 3), (64 + 4 tj, ..), (64 + 4 tj + 2, ..)
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[i][k] = make_float2(0.0f, 0.0f);
+  const int lim_lo = min(min(lim[0], lim[1]), min(lim[2], lim[3]));
+  stage(0);
+  for (int c = 0; c < nch; ++c) {
+    if (c + 1 < nch) {
+      stage(c + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int b = c & 1, p0 = c * kPfKeys, cnt = min(kPfKeys, pos_hi + 1 - p0);
+    const float *vb = Vs + (size_t)b * kPfKeys * hd;
+    const float *wb = Ws + (size_t)b * kPfKeys * kPfVecs;
+    // keys every vector of the thread adds, then the ones past some vector's position
+    const int full = max(0, min(cnt, lim_lo - p0 + 1));
+    auto step = [&](int j, bool masked) {
+      const float4 w4 = reinterpret_cast<const float4 *>(wb + (size_t)j * kPfVecs)[ti];
+      const float4 va = reinterpret_cast<const float4 *>(vb + (size_t)j * hd)[tj];
+      const float4 vb4 = reinterpret_cast<const float4 *>(vb + (size_t)j * hd + 64)[tj];
+      const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+      const float2 vv[4] = {make_float2(va.x, va.y), make_float2(va.z, va.w), make_float2(vb4.x, vb4.y),
+                            make_float2(vb4.z, vb4.w)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        if (masked && p0 + j > lim[i]) continue;
+        const float2 w2 = make_float2(wv[i], wv[i]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[i][k] = f2_madd_rn(acc[i][k], w2, vv[k]);  // llama.c:574
+      }
+    };
+    for (int j = 0; j < full; ++j) step(j, false);
+    for (int j = full; j < cnt; ++j) step(j, true);
+    __syncthreads();  // the buffer is free for chunk c + 2
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = 4 * ti + i;
+    if (v >= nv) continue;
+    const int r = r0 + v / group, g = v - (v / group) * group;
+    float *o = a.out + (size_t)r * qd + (size_t)(kvh * group + g) * hd;
+    *reinterpret_cast<float4 *>(o + 4 * tj) = make_float4(acc[i][0].x, acc[i][0].y, acc[i][1].x, acc[i][1].y);
+    *reinterpret_cast<float4 *>(o + 64 + 4 * tj) = make_float4(acc[i][2].x, acc[i][2].y, acc[i][3].x, acc[i][3].y);
+  }
 }
 
 // Greedy ids of the rows (first maximum: sampler.c:8-21) from the lm-head
