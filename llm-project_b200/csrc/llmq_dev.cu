@@ -650,7 +650,8 @@ cudaError_t launch_attention(const AttnArgs &a, cudaStream_t st, bool pdl, int p
 }
 
 cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
-                          int max_seq, cudaStream_t st, unsigned *tp_seq = nullptr, unsigned tp_products = 0) {
+                          int max_seq, cudaStream_t st, unsigned *tp_seq, unsigned tp_products, float *amax,
+                          int n_amax) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(1);
   cfg.blockDim = dim3(1);
@@ -660,7 +661,8 @@ cudaError_t launch_finish(StepState *step, unsigned long long *argmax, int *err,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_step_finish, step, argmax, err, result, tokens, max_seq, tp_seq, tp_products);
+  return cudaLaunchKernelEx(&cfg, k_step_finish, step, argmax, err, result, tokens, max_seq, tp_seq, tp_products,
+                            amax, n_amax);
 }
 
 // Launches `kern` with programmatic dependent launch (the kernel itself waits
@@ -734,6 +736,7 @@ struct DevModel {
   // shard's head, d_ff and vocab counts; these keep the whole model's)
   int tp_rank = 0, tp_world = 1, vocab_full = 0, kvd_full = 0;
   float *tp_max = nullptr;      // reduced activation absmax of a row-parallel product
+  float *amax = nullptr;        // [n_layers][2]: absmax of Wo's and W2's inputs, published by their producers
   int *tp_acc = nullptr;        // [d_model] partial / reduced int32 sums
   float *logits_full = nullptr; // [vocab_full] gathered logits
   // peer-memory exchange of the single-sequence step (see TpExchange)
@@ -791,6 +794,7 @@ void release_model(DevModel *M) {
     for (float *p : *v) cudaFree(p);
   for (int q = 0; q < (int)M->tpx_peer.size(); ++q)
     if (q != M->tp_rank && M->tpx_peer[q]) cudaIpcCloseMemHandle(M->tpx_peer[q]);
+  cudaFree(M->amax);
   void *tp_ptrs[] = {M->tp_max, M->tp_acc, M->logits_full, M->tpx, M->tpx_peers_dev, M->tp_seq};
   for (void *p : tp_ptrs) cudaFree(p);
   void *dev_ptrs[] = {M->final_norm, M->wte_q, M->wte_s, M->rope_cos, M->rope_sin, M->x, M->q, M->o, M->scores,
@@ -1022,6 +1026,7 @@ int upload_model(DevCtx &c, const QLlamaModel *m, DevModel *M) {
   if (M->tp_world > 1 && (!dev_zeros(&M->tp_max, 1) || !dev_zeros(&M->tp_acc, dm) ||
                           !dev_zeros(&M->logits_full, M->vocab_full)))
     return 0;
+  if (M->tp_world == 1 && !dev_zeros(&M->amax, 2 * (size_t)L)) return 0;
   if (M->tp_world > 1 && !tp_map_peers(M)) return 0;
   CK(cudaDeviceSynchronize());
   return 1;
@@ -1536,6 +1541,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       a.n_kv = cfg.n_kv;
       a.hd = cfg.head_dim;
       a.max_seq = K->max_seq;
+      a.amax_out = M->amax ? M->amax + 2 * l : nullptr;  // Wo's absmax_in
       choose_attention(a);
       CK(launch_attention(a, st, true, 0));
       PROF_MARK();
@@ -1556,6 +1562,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       GemvArgs a = base_args(M->wo[l], M->p_wo, M->acc, M->cnt, M->err);
       a.in = M->o;
       a.out = M->x;
+      a.absmax_in = M->amax + 2 * l;
       CK((launch_gemv<PRO_ABSMAX, EPI_RESID, 1>(a, M->p_wo, st, true)));
       PROF_MARK();
     }
@@ -1573,6 +1580,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       a.gamma = M->ffn_norm[l];
       a.eps = cfg.eps;
       a.out = M->h;
+      a.amax_out = M->amax ? M->amax + 2 * l + 1 : nullptr;  // W2's absmax_in
       CK((launch_gemv<PRO_RMSNORM, EPI_SWIGLU, 1>(a, M->p_w13, st, true)));
       PROF_MARK();
     }
@@ -1588,6 +1596,7 @@ int record_step(DevModel *M, DevKV *K, int mode) {
       GemvArgs a = base_args(M->w2[l], M->p_w2, M->acc, M->cnt, M->err);
       a.in = M->h;
       a.out = M->x;
+      a.absmax_in = M->amax + 2 * l + 1;
       CK((launch_gemv<PRO_ABSMAX, EPI_RESID, 1>(a, M->p_w2, st, true)));
       PROF_MARK();
     }
@@ -1631,7 +1640,8 @@ int record_step(DevModel *M, DevKV *K, int mode) {
     PROF_MARK();
   }
   CK(launch_finish(M->step, M->argmax, M->err, M->result, M->tokens, K->max_seq, st,
-                   M->tp_world > 1 ? M->tp_seq : nullptr, 2u * (unsigned)cfg.n_layers));
+                   M->tp_world > 1 ? M->tp_seq : nullptr, 2u * (unsigned)cfg.n_layers, M->amax,
+                   M->amax ? 2 * cfg.n_layers : 0));
       PROF_MARK();
   if (host_io) CK(cudaMemcpyAsync(M->h_result, M->result, 4 * sizeof(int), cudaMemcpyDeviceToHost, st));
   if (host_io && sampled)
@@ -1682,6 +1692,7 @@ int reset_after_device_error(DevModel *M, int flags) {
   cudaMemsetAsync(M->cnt, 0, (size_t)M->max_slabs * sizeof(int), M->stream);
   cudaMemsetAsync(M->argmax, 0, sizeof(unsigned long long), M->stream);
   cudaMemsetAsync(M->err, 0, 4 * sizeof(int), M->stream);
+  if (M->amax) cudaMemsetAsync(M->amax, 0, 2 * (size_t)M->cfg.n_layers * sizeof(float), M->stream);
   cudaStreamSynchronize(M->stream);
   llmq_set_error(LLMQ_ERR_CUDA, "libllmq_cuda: device reported error flags 0x%x (%s%s%s)", flags,
                  (flags & ERR_TIMEOUT) ? "copy timeout " : "", (flags & ERR_BAD_TOKEN) ? "bad token " : "",
@@ -2450,6 +2461,7 @@ LLMQ_API int llmq_bench_gemv(const QLlamaModel *m, int which, int layer, int ite
     launch = [&a, &next, mat_of, p, in, M, st, r]() {
       a = base_args(mat_of(next++), *p, M->acc, M->cnt, M->err);
       a.in = in;
+      if (!r) a.absmax_in = M->amax;  // Wo / W2 take their absmax from the producer, as in a step
       a.gamma = M->final_norm;
       a.eps = M->cfg.eps;
       a.out = M->logits;

@@ -304,9 +304,21 @@ struct GemvArgs {
   float *vcache;       // EPI_QKV: this layer's [n_kv][max_seq][hd]
   unsigned long long *argmax;
   int idx_offset;      // EPI_LOGITS: global index of column 0 (vocab shard)
-  const float *absmax_in;  // PRO_ABSMAX: if set, the row's absmax over all shards (else computed here)
+  const float *absmax_in;  // PRO_ABSMAX, one row: the row's absmax, published by the producer (else computed
+                           // here); only the CTA's own k-tiles of the row are then loaded and quantised
+  float *amax_out;         // EPI_SWIGLU: max |out| is folded in here (the next product's absmax_in)
   TpExchange tp;           // EPI_TP_RESID
 };
+
+// Folds max |v| over this warp's values into *dst (a non-negative float kept
+// as its bit pattern, which orders like the float).  NaN values are left out,
+// as the reference's absmax loop leaves them out (quant.c:70).
+__device__ __forceinline__ void warp_amax_publish(float v, float *dst) {
+  float m = v == v ? fabsf(v) : 0.0f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0 && m > 0.0f) atomicMax(reinterpret_cast<unsigned *>(dst), __float_as_uint(m));
+}
 
 // Owner CTA of tile t under the contiguous split [c*T/G, (c+1)*T/G).
 __device__ __forceinline__ long long tile_owner(long long t, long long T, long long G) {
@@ -414,7 +426,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     }
     __syncthreads();
   };
-  if (PRO == PRO_ABSMAX) {
+  if (PRO == PRO_ABSMAX && a.absmax_in && a.rows == 1 && vec_in) {
+    // The absmax comes from the producer: only the k-tiles of this CTA's tiles
+    // are loaded and quantised (its range spans one slab, two, or whole ones).
+    const long long nk = a.n_ktiles, s0 = t_begin / nk, s1 = (t_end - 1) / nk;
+    int ra0 = 0, ra1 = a.n_ktiles, rb0 = 0, rb1 = 0;  // k-tiles [ra0, ra1) and [rb0, rb1)
+    if (s0 == s1) {
+      ra0 = static_cast<int>(t_begin - s0 * nk);
+      ra1 = static_cast<int>(t_end - s0 * nk);
+    } else if (s1 == s0 + 1 && t_end - s1 * nk < t_begin - s0 * nk) {
+      ra0 = static_cast<int>(t_begin - s0 * nk);
+      rb1 = static_cast<int>(t_end - s1 * nk);
+    }
+    auto bytes_of = [&](int t0, int t1) -> uint32_t {
+      const int k0 = t0 * KT, k1 = min(t1 * KT, a.K);
+      return k1 > k0 ? static_cast<uint32_t>(k1 - k0) * 4u : 0u;
+    };
+    if (tid == 0) {
+      const uint32_t ba = bytes_of(ra0, ra1), bb = bytes_of(rb0, rb1);
+      mbar_expect_tx(rowbar, ba + bb);
+      if (ba) bulk_load(xs + (size_t)ra0 * KT, a.in + (size_t)ra0 * KT, ba, rowbar);
+      if (bb) bulk_load(xs + (size_t)rb0 * KT, a.in + (size_t)rb0 * KT, bb, rowbar);
+    }
+    issue_to(S);
+    if (!mbar_wait_bounded(rowbar, 0)) s_abort = 1;
+    __syncthreads();
+    const float m = *a.absmax_in;
+    const float as = m > 0.0f ? __fdiv_rn(m, 127.0f) : 1.0f;  // quant.c:71
+    const float inv = __fdiv_rn(1.0f, as);                      // quant.c:72
+    if (tid == 0) s_as[0] = as;
+    for (int k = ra0 * KT + tid; k < ra1 * KT; k += kThreads) codes[k] = k < a.K ? code_of(__fmul_rn(xs[k], inv)) : 0;
+    for (int k = rb0 * KT + tid; k < rb1 * KT; k += kThreads) codes[k] = k < a.K ? code_of(__fmul_rn(xs[k], inv)) : 0;
+  } else if (PRO == PRO_ABSMAX) {
     for (int r = 0; r < a.rows && r < MR; ++r) {
       load_row(a.in + (size_t)r * a.K);
       float m = 0.0f;
@@ -592,12 +635,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         const int j = static_cast<int>(slab) * half + c;  // d_ff index
         const int vg = atomicExch(a.acc + p0 + c, 0);
         const int vu = atomicExch(a.acc + p0 + half + c, 0);
+        float h = 0.0f;
         if (j < a.N) {
           const float z = dequant(as, a.ws[p0 + c], vg);
           const float u = dequant(as, a.ws[p0 + half + c], vu);
           const float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, libm_expf(-z)));  // llama.c:585
-          a.out[j] = __fmul_rn(__fmul_rn(z, s), u);                         // llama.c:586
+          h = __fmul_rn(__fmul_rn(z, s), u);                                // llama.c:586
+          a.out[j] = h;
         }
+        if (a.amax_out) warp_amax_publish(h, a.amax_out);  // the W2 product's row absmax
       }
     } else if (EPI == EPI_QKV) {
       // q, k (before RoPE, which the attention kernel applies) and v of this step
@@ -714,6 +760,7 @@ struct AttnArgs {
   int n_heads, n_kv, hd, max_seq;
   int pv_whole;  // k_attn_pv stages the whole value slice at once (it fits in shared memory)
   int fused_chunk;  // > 0: k_attn_fused with key chunks of this many rows (0: the two-kernel path)
+  float *amax_out;  // if set, max |out| is folded in here (the Wo product's absmax_in)
 };
 
 constexpr int kScoreChunk = 32;    // key positions per scores CTA
@@ -877,7 +924,9 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
     cp_async_wait<0>();
     __syncthreads();
     LLMQ_TSTAMP(4);
-    if (tid < w) a.out[(size_t)h * hd + d0 + tid] = seq_dot(wts, vs + tid, kPVSlice, np, 0.0f);  // llama.c:574
+    const float o = tid < w ? seq_dot(wts, vs + tid, kPVSlice, np, 0.0f) : 0.0f;  // llama.c:574
+    if (tid < w) a.out[(size_t)h * hd + d0 + tid] = o;
+    if (a.amax_out && tid < 32) warp_amax_publish(o, a.amax_out);
     LLMQ_TSTAMP(5);
     return;
   }
@@ -925,6 +974,7 @@ __global__ void __launch_bounds__(kPVThreads) k_attn_pv(const AttnArgs a) {
   }
   LLMQ_TSTAMP(4);
   if (tid < w) a.out[(size_t)h * hd + d0 + tid] = o;
+  if (a.amax_out && tid < 32) warp_amax_publish(tid < w ? o : 0.0f, a.amax_out);
 }
 
 // Attention of one query head in one launch (llama.c:558-575), for batch-1
@@ -1039,7 +1089,9 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   cp_async_wait<0>();
   __syncthreads();
   LLMQ_TSTAMP(6);
-  if (tid < w) a.out[(size_t)h * hd + d0 + tid] = seq_dot(e, vs + tid, kPVSlice, np, 0.0f);  // llama.c:574
+  const float o = tid < w ? seq_dot(e, vs + tid, kPVSlice, np, 0.0f) : 0.0f;  // llama.c:574
+  if (tid < w) a.out[(size_t)h * hd + d0 + tid] = o;
+  if (a.amax_out && tid < 32) warp_amax_publish(o, a.amax_out);  // the Wo product's row absmax
   __syncwarp();
   LLMQ_TSTAMP(7);
   LLMQ_LAUNCH_EXIT();
@@ -1049,7 +1101,7 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
 // device-side token and position (used when steps are chained on the device),
 // record the generated id, and reset the argmax cell and error word.
 __global__ void k_step_finish(StepState *step, unsigned long long *argmax, int *err, int *result, int *tokens,
-                              int max_seq, unsigned *tp_seq, unsigned tp_products) {
+                              int max_seq, unsigned *tp_seq, unsigned tp_products, float *amax, int n_amax) {
   LLMQ_LAUNCH_ENTER_TAG(3);
   pdl_wait();
   if (tp_seq) *tp_seq += tp_products;  // the step's row-parallel products are done on this rank
@@ -1066,6 +1118,7 @@ __global__ void k_step_finish(StepState *step, unsigned long long *argmax, int *
   step->pos = pos + 1;
   *argmax = 0ull;
   *err = 0;
+  for (int i = 0; i < n_amax; ++i) amax[i] = 0.0f;  // the step's published absmax cells, for the next step
   LLMQ_LAUNCH_EXIT();
 }
 
