@@ -408,9 +408,11 @@ int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
   const size_t tile = (size_t)kNT * m.KT;
   const size_t codes = align16((size_t)rows * m.Kpad);
   // xs holds one input row (both prologues) and later the epilogue exchange
-  // (RMSNorm prologues also keep the K squares after the row)
+  // (RMSNorm prologues also keep the K squares after the row, then the sum's
+  // scratch)
   size_t xs = std::max<size_t>((size_t)kNT * 4, (size_t)kThreads * 4);
-  xs = std::max<size_t>(xs, (size_t)(pro == PRO_ABSMAX ? 1 : 2) * (((size_t)m.K + 3) & ~size_t(3)) * 4);
+  xs = std::max<size_t>(xs, pro == PRO_ABSMAX ? (((size_t)m.K + 3) & ~size_t(3)) * 4
+                                              : 2 * (((size_t)m.K + 3) & ~size_t(3)) * 4 + spec_sum_bytes(kThreads));
   const size_t fixed = codes + align16(xs);
   const size_t budget = (size_t)c.max_smem;
   if (fixed + 2 * (tile + 16) + 32 > budget) {
@@ -1105,10 +1107,11 @@ int build_matf(DevCtx &c, MatF &out, int K, const std::vector<int> &colsrc, cons
   out.threads = threads;
   out.tw = kF32Tile;
   // each consumer warp's share of shared memory beside the input row (and, for
-  // RMSNorm, its squares).  32-column tiles: slots of 256 rows (the kernel's
+  // RMSNorm, its squares and the sum's scratch).  32-column tiles: slots of 256 rows (the kernel's
   // unrolled full-slot path) when two or more fit; otherwise, and for 64-column
   // tiles, slots of up to 128 rows (16 or 32 KB), as many as fit, at most 8.
-  const long long xs_bytes = ((pro == F32_PRO_PLAIN ? 1LL : 2LL) * roundup(K, 4) + 8) * 4;
+  const long long xs_bytes = ((pro == F32_PRO_PLAIN ? 1LL : 2LL) * roundup(K, 4) + 8) * 4 +
+                             (pro == F32_PRO_PLAIN ? 0LL : (long long)spec_sum_bytes(threads));
   const long long per_warp = ((long long)c.max_smem - 1024 - xs_bytes) / nc - 2LL * 2 * kF32MaxSlots * 8;
   int rows = 0, slots = 0;
   if (kF32Tile == 32 && per_warp / (kF32RowsFull * 128LL) >= 2) {
@@ -1782,7 +1785,7 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   na.codes = c.tc_codes;
   na.as = c.tc_as;
   na.err = M->err;
-  const size_t norm_smem = 2 * (size_t)((dm + 3) & ~3) * sizeof(float);
+  const size_t norm_smem = 2 * (size_t)((dm + 3) & ~3) * sizeof(float) + spec_sum_bytes(kRowThreads);
   RowAttnArgs aa{};
   aa.rd = R.rd;
   aa.qkv = R.qkv;
@@ -2755,6 +2758,82 @@ extern "C" LLMQ_API int llmq_bench_qmatmul(const QTensor *W, int M, int iters, f
   cudaFree(dA);
   cudaFree(dC);
   free_mat(m);
+  return rc;
+}
+
+namespace {
+// One row per CTA: the row's sequential sum by spec_seq_sum and by the
+// one-thread loop, the segments that missed their window, and the SM cycles of
+// each (clock64 on thread 0, barrier to barrier).
+__global__ void __launch_bounds__(1024) k_spec_sum_check(const float *v, int n, float *sums, int *misses,
+                                                         long long *cycles) {
+  extern __shared__ __align__(16) float row[];
+  __shared__ float s_loop;
+  const int r = blockIdx.x, n4 = (n + 3) & ~3;
+  void *scratch = row + n4;
+  for (int k = threadIdx.x; k < n; k += blockDim.x) row[k] = v[(size_t)r * n + k];
+  __syncthreads();
+  const long long t0 = clock64();
+  int miss = 0;
+  const float s = spec_seq_sum<1024>(row, n, 0.0f, scratch, &miss);
+  const long long t1 = clock64();
+  if (threadIdx.x == 0) s_loop = seq_sum_a16(row, n, 0.0f);
+  __syncthreads();
+  const long long t2 = clock64();
+  if (threadIdx.x == 0) {
+    sums[2 * r] = s;
+    sums[2 * r + 1] = s_loop;
+    misses[r] = miss;
+    cycles[2 * r] = t1 - t0;
+    cycles[2 * r + 1] = t2 - t1;
+  }
+}
+}  // namespace
+
+// The block-wide sequential sum of the RMSNorm prologues, checked on given
+// rows: for each of `rows` rows of n floats (host memory), sums[2r] is the
+// block's result, sums[2r+1] the one-thread loop's, misses[r] the segments that
+// were summed again, cycles[2r] / cycles[2r+1] the two methods' SM cycles.
+// threads: the block size (a multiple of 32, 64..1024).
+extern "C" LLMQ_API int llmq_spec_sum_check(const float *v, int rows, int n, int threads, float *sums, int *misses,
+                                            long long *cycles) {
+  std::lock_guard<std::recursive_mutex> lk(g_mu);
+  DevCtx *c = get_ctx();
+  if (!c) return q_llama_last_error();
+  const size_t smem = (size_t)((n + 3) & ~3) * 4 + spec_sum_bytes(1024);
+  if (!v || !sums || !misses || !cycles || rows <= 0 || n < 0 || threads < 64 || threads > 1024 || threads % 32 ||
+      smem > (size_t)c->max_smem) {
+    llmq_set_error(LLMQ_ERR_ARG, "llmq_spec_sum_check: bad arguments");
+    return LLMQ_ERR_ARG;
+  }
+  float *dv = nullptr, *ds = nullptr;
+  int *dm = nullptr;
+  long long *dc = nullptr;
+  int rc = LLMQ_OK;
+  const size_t vb = (size_t)rows * n * sizeof(float);
+  cudaError_t e = cudaMalloc(&dv, vb ? vb : 4);
+  if (e == cudaSuccess) e = cudaMalloc(&ds, (size_t)rows * 2 * sizeof(float));
+  if (e == cudaSuccess) e = cudaMalloc(&dm, (size_t)rows * sizeof(int));
+  if (e == cudaSuccess) e = cudaMalloc(&dc, (size_t)rows * 2 * sizeof(long long));
+  if (e == cudaSuccess && vb) e = upload_sync(dv, v, vb);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k_spec_sum_check, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 static_cast<int>(smem));
+  if (e == cudaSuccess) {
+    k_spec_sum_check<<<rows, threads, smem, c->stream>>>(dv, n, ds, dm, dc);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(sums, ds, (size_t)rows * 2 * sizeof(float), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(misses, dm, (size_t)rows * sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(cycles, dc, (size_t)rows * 2 * sizeof(long long), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    llmq_set_error(LLMQ_ERR_CUDA, "llmq_spec_sum_check: %s", cudaGetErrorString(e));
+    rc = LLMQ_ERR_CUDA;
+  }
+  cudaFree(dv);
+  cudaFree(ds);
+  cudaFree(dm);
+  cudaFree(dc);
   return rc;
 }
 

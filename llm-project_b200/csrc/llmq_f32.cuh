@@ -207,7 +207,6 @@ __global__ void __launch_bounds__(MAXT, 1) k_gemv_f32(const F32Args a) {
   constexpr bool kProd = f32_producer(EPI);
   extern __shared__ __align__(128) uint8_t sm_f32[];
   __shared__ unsigned long long s_red64[32];
-  __shared__ float s_r;
   __shared__ uint64_t s_xbar;  // the input row's bulk copy
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nwarps = nthr >> 5;
   const int nc = kProd ? nwarps - 1 : nwarps;  // consumer warps; warp nc is the producer
@@ -277,17 +276,14 @@ __global__ void __launch_bounds__(MAXT, 1) k_gemv_f32(const F32Args a) {
   if (PRO != F32_PRO_PLAIN) {
     if (PRO == F32_PRO_EMBED_RMSNORM && blockIdx.x == 0)
       for (int k = tid; k < K; k += nthr) a.x_out[k] = xs[k];
-    // rmsnorm.c:14-19: the sum of squares is one sequential chain
+    // rmsnorm.c:14-19: the sum of squares is one sequential chain, formed by
+    // the block in the loop's order and rounding (spec_seq_sum)
     float *sq = xs + ((K + 3) & ~3);
     for (int k = tid; k < K; k += nthr) sq[k] = __fmul_rn(xs[k], xs[k]);
     __syncthreads();
-    if (tid == 0) {
-      float ms = seq_sum_a16(sq, K, 0.0f);  // sq is 16-byte aligned
-      ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
-      s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
-    }
-    __syncthreads();
-    const float r = s_r;
+    float ms = spec_seq_sum<MAXT>(sq, K, 0.0f, sq + ((K + 3) & ~3));  // sq is 16-byte aligned
+    ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
     for (int k = tid; k < K; k += nthr) xs[k] = __fmul_rn(__fmul_rn(xs[k], r), a.gamma[k]);
   }
   __syncthreads();

@@ -13,6 +13,7 @@
 
 #include "libm_expf.h"
 #include "llmq_device_common.cuh"
+#include "llmq_spec_sum.cuh"
 
 #include <cooperative_groups.h>
 
@@ -349,7 +350,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
   __shared__ float s_red[32];
   __shared__ unsigned long long s_red64[32];
   __shared__ float s_as[MR];
-  __shared__ float s_r;
   __shared__ int s_flag;
   __shared__ int s_abort;
 
@@ -496,18 +496,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     }
     LLMQ_TSTAMP(3);
     // The sum of squares (rmsnorm.c:15): the products are independent, so all
-    // threads form them; the adds stay one sequential chain in thread 0.
+    // threads form them; the adds keep the loop's order and rounding
+    // (spec_seq_sum: every warp runs a segment from candidate starts).
     float *sq = xs + ((K + 3) & ~3);
     for (int k = tid; k < K; k += kThreads) sq[k] = __fmul_rn(xs[k], xs[k]);
     __syncthreads();
-    if (tid == 0) {
-      float ms = seq_sum_a16(sq, K, 0.0f);  // sq is 16-byte aligned
-      ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
-      s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
-      LLMQ_TSTAMP(4);
-    }
-    __syncthreads();
-    const float r = s_r;
+    float ms = spec_seq_sum<kThreads>(sq, K, 0.0f, sq + ((K + 3) & ~3));  // sq is 16-byte aligned
+    ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
+    const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
+    LLMQ_TSTAMP(4);
     float m = 0.0f;
     for (int k = tid; k < K; k += kThreads) {
       const float y = __fmul_rn(__fmul_rn(xs[k], r), a.gamma[k]);

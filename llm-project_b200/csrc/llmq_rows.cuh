@@ -37,12 +37,11 @@ struct RowNormArgs {
 
 // RMSNorm of one row (rmsnorm.c:7-21, the arithmetic of k_gemv's RMSNorm
 // prologue), then its activation codes (quant.c:69-78).  One CTA per row;
-// dynamic shared memory 2 * K floats.
+// dynamic shared memory 2 * K floats and spec_sum_bytes(kRowThreads).
 __global__ void __launch_bounds__(kRowThreads) k_rows_norm_codes(const RowNormArgs a) {
   LLMQ_LAUNCH_SPAN(10);
   extern __shared__ __align__(16) float xs[];
   __shared__ float s_red[32];
-  __shared__ float s_r;
   pdl_launch_dependents();
   pdl_wait();
   const int r = blockIdx.x, tid = threadIdx.x, K = a.K;
@@ -66,13 +65,9 @@ __global__ void __launch_bounds__(kRowThreads) k_rows_norm_codes(const RowNormAr
   __syncthreads();
   for (int k = tid; k < K; k += kRowThreads) sq[k] = __fmul_rn(xs[k], xs[k]);
   __syncthreads();
-  if (tid == 0) {
-    float ms = seq_sum(sq, 1, K, 0.0f);  // rmsnorm.c:15, in index order
-    ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
-    s_r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
-  }
-  __syncthreads();
-  const float rr = s_r;
+  float ms = spec_seq_sum<kRowThreads>(sq, K, 0.0f, sq + ((K + 3) & ~3));  // rmsnorm.c:15, in index order
+  ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
+  const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
   float m = 0.0f;
   for (int k = tid; k < K; k += kRowThreads) {
     const float y = __fmul_rn(__fmul_rn(xs[k], rr), a.gamma[k]);

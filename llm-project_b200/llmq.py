@@ -141,6 +141,8 @@ SIGNATURES = {
     "llmq_bench_qmatmul": (C.c_int, [C.POINTER(QTensor), C.c_int, C.c_int, c_float_p]),
     "llmq_tp_wait_timeout_check": (C.c_int, [C.c_int, C.c_uint, c_int_p, c_float_p]),
     "llmq_rmsnorm_qmatmul": (C.c_int, [c_float_p, c_float_p, C.c_float, C.POINTER(QTensor), c_float_p]),
+    "llmq_spec_sum_check": (C.c_int, [c_float_p, C.c_int, C.c_int, C.c_int, c_float_p, c_int_p,
+                                      C.POINTER(C.c_longlong)]),
     "q_llama_decode_batch": (None, [C.POINTER(QLlamaModel), C.POINTER(C.POINTER(LlamaKV)), c_int_p, C.c_int,
                                     C.POINTER(Tensor)]),
     "q_llama_decode_batch_argmax": (C.c_int, [C.POINTER(QLlamaModel), C.POINTER(C.POINTER(LlamaKV)), c_int_p,
