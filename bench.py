@@ -1,7 +1,7 @@
 """Benchmark: int8 (W8A8) LLaMA-family KV-cache decode on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload 8b|8b2|tiny|serve64|serve64-tp|70b|70b-bs32|sweep]
+                    [--workload 8b|8b2|tiny|serve64|serve16-2l|serve64-tp|70b|70b-bs32|sweep]
 
 Default workload: LLaMA-3-8B-shaped int8 model
 (dm 4096, 32 layers, 32/8 heads, hd 128, dff 14336, vocab 128256, rope 5e5),
@@ -59,6 +59,10 @@ WORKLOADS = {
                              d_ff=14336, rope_base=500000.0, eps=1e-5), prompt=2048, gen=128, batch=64,
                     name="llama3-8b-shaped int8 W8A8 batched serving: 64 sequences, 2048-id prompts prefilled, "
                          "then batched greedy decode"),
+    "serve16-2l": dict(cfg=dict(vocab=128256, d_model=4096, n_layers=2, n_heads=32, n_kv=8, head_dim=128,
+                                d_ff=14336, rope_base=500000.0, eps=1e-5), prompt=1024, gen=8, batch=16,
+                       name="llama3-8b layer shapes, 2 layers (profiling case): 16 sequences, 1024-id prompts "
+                            "prefilled, then batched greedy decode"),
     "70b": dict(cfg=dict(vocab=128256, d_model=8192, n_layers=80, n_heads=64, n_kv=8, head_dim=128, d_ff=28672,
                          rope_base=500000.0, eps=1e-5), prompt=1024, gen=256, tp=True, fast=True,
                 name="llama3-70b-shaped int8 W8A8, batch 1, tensor-parallel over all GPUs: 1024-id prompt then "

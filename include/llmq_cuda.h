@@ -468,11 +468,12 @@ int llmq_step_profile(const QLlamaModel *m, LlamaKV *kv, int token, float *ms, i
 int llmq_rmsnorm_qmatmul(const float *x, const float *gamma, float eps, const QTensor *W, float *out);
 
 /* The RMSNorm's sum of squares (rmsnorm.c:15) as the GEMV prologues form it:
- * one thread block sums a row in the loop's order and rounding, with every warp
- * running a segment from candidate start values.  For each of `rows` rows of
+ * one thread block sums a row in the loop's order and rounding, its 32
+ * segments run in parallel from candidate starts around estimated partial sums
+ * and linked exactly.  For each of `rows` rows of
  * n floats (host array v), sums[2r] is the block's sum and sums[2r+1] the
- * one-thread loop's (equal bit for bit), misses[r] the segments whose start
- * was outside the candidate window (summed again), cycles[2r] and
+ * one-thread loop's (equal bit for bit), misses[r] the segments whose exact
+ * start was not a candidate (summed by one thread), cycles[2r] and
  * cycles[2r+1] the SM cycles of the two.  threads: block size, a multiple of
  * 32 in 64..1024.  Returns 0 or an error code. */
 int llmq_spec_sum_check(const float *v, int rows, int n, int threads, float *sums, int *misses, long long *cycles);

@@ -412,7 +412,7 @@ int plan_gemv(const DevCtx &c, const Mat &m, int pro, int rows, GemvPlan &p) {
   // scratch)
   size_t xs = std::max<size_t>((size_t)kNT * 4, (size_t)kThreads * 4);
   xs = std::max<size_t>(xs, pro == PRO_ABSMAX ? (((size_t)m.K + 3) & ~size_t(3)) * 4
-                                              : 2 * (((size_t)m.K + 3) & ~size_t(3)) * 4 + spec_sum_bytes(kThreads));
+                                              : 2 * (((size_t)m.K + 3) & ~size_t(3)) * 4 + spec_sum_bytes());
   const size_t fixed = codes + align16(xs);
   const size_t budget = (size_t)c.max_smem;
   if (fixed + 2 * (tile + 16) + 32 > budget) {
@@ -1111,7 +1111,7 @@ int build_matf(DevCtx &c, MatF &out, int K, const std::vector<int> &colsrc, cons
   // unrolled full-slot path) when two or more fit; otherwise, and for 64-column
   // tiles, slots of up to 128 rows (16 or 32 KB), as many as fit, at most 8.
   const long long xs_bytes = ((pro == F32_PRO_PLAIN ? 1LL : 2LL) * roundup(K, 4) + 8) * 4 +
-                             (pro == F32_PRO_PLAIN ? 0LL : (long long)spec_sum_bytes(threads));
+                             (pro == F32_PRO_PLAIN ? 0LL : (long long)spec_sum_bytes());
   const long long per_warp = ((long long)c.max_smem - 1024 - xs_bytes) / nc - 2LL * 2 * kF32MaxSlots * 8;
   int rows = 0, slots = 0;
   if (kF32Tile == 32 && per_warp / (kF32RowsFull * 128LL) >= 2) {
@@ -1785,7 +1785,7 @@ int run_rows(DevCtx &c, DevModel *M, const RowDesc *rows_h, int rows, int lm0, f
   na.codes = c.tc_codes;
   na.as = c.tc_as;
   na.err = M->err;
-  const size_t norm_smem = 2 * (size_t)((dm + 3) & ~3) * sizeof(float) + spec_sum_bytes(kRowThreads);
+  const size_t norm_smem = 2 * (size_t)((dm + 3) & ~3) * sizeof(float) + spec_sum_bytes();
   RowAttnArgs aa{};
   aa.rd = R.rd;
   aa.qkv = R.qkv;
@@ -2775,7 +2775,7 @@ __global__ void __launch_bounds__(1024) k_spec_sum_check(const float *v, int n, 
   __syncthreads();
   const long long t0 = clock64();
   int miss = 0;
-  const float s = spec_seq_sum<1024>(row, n, 0.0f, scratch, &miss);
+  const float s = spec_seq_sum(row, n, 0.0f, scratch, &miss);
   const long long t1 = clock64();
   if (threadIdx.x == 0) s_loop = seq_sum_a16(row, n, 0.0f);
   __syncthreads();
@@ -2800,7 +2800,7 @@ extern "C" LLMQ_API int llmq_spec_sum_check(const float *v, int rows, int n, int
   std::lock_guard<std::recursive_mutex> lk(g_mu);
   DevCtx *c = get_ctx();
   if (!c) return q_llama_last_error();
-  const size_t smem = (size_t)((n + 3) & ~3) * 4 + spec_sum_bytes(1024);
+  const size_t smem = (size_t)((n + 3) & ~3) * 4 + spec_sum_bytes();
   if (!v || !sums || !misses || !cycles || rows <= 0 || n < 0 || threads < 64 || threads > 1024 || threads % 32 ||
       smem > (size_t)c->max_smem) {
     llmq_set_error(LLMQ_ERR_ARG, "llmq_spec_sum_check: bad arguments");

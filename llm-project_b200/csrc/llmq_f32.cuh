@@ -281,7 +281,7 @@ __global__ void __launch_bounds__(MAXT, 1) k_gemv_f32(const F32Args a) {
     float *sq = xs + ((K + 3) & ~3);
     for (int k = tid; k < K; k += nthr) sq[k] = __fmul_rn(xs[k], xs[k]);
     __syncthreads();
-    float ms = spec_seq_sum<MAXT>(sq, K, 0.0f, sq + ((K + 3) & ~3));  // sq is 16-byte aligned
+    float ms = spec_seq_sum(sq, K, 0.0f, sq + ((K + 3) & ~3));  // sq is 16-byte aligned
     ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
     for (int k = tid; k < K; k += nthr) xs[k] = __fmul_rn(__fmul_rn(xs[k], r), a.gamma[k]);

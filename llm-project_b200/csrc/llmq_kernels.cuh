@@ -497,11 +497,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
     LLMQ_TSTAMP(3);
     // The sum of squares (rmsnorm.c:15): the products are independent, so all
     // threads form them; the adds keep the loop's order and rounding
-    // (spec_seq_sum: every warp runs a segment from candidate starts).
+    // (spec_seq_sum: segments run in parallel from candidate starts, linked
+    // exactly).
     float *sq = xs + ((K + 3) & ~3);
     for (int k = tid; k < K; k += kThreads) sq[k] = __fmul_rn(xs[k], xs[k]);
     __syncthreads();
-    float ms = spec_seq_sum<kThreads>(sq, K, 0.0f, sq + ((K + 3) & ~3));  // sq is 16-byte aligned
+    float ms = spec_seq_sum(sq, K, 0.0f, sq + ((K + 3) & ~3));  // sq is 16-byte aligned
     ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
     const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
     LLMQ_TSTAMP(4);

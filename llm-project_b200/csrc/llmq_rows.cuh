@@ -37,7 +37,7 @@ struct RowNormArgs {
 
 // RMSNorm of one row (rmsnorm.c:7-21, the arithmetic of k_gemv's RMSNorm
 // prologue), then its activation codes (quant.c:69-78).  One CTA per row;
-// dynamic shared memory 2 * K floats and spec_sum_bytes(kRowThreads).
+// dynamic shared memory 2 * K floats and spec_sum_bytes().
 __global__ void __launch_bounds__(kRowThreads) k_rows_norm_codes(const RowNormArgs a) {
   LLMQ_LAUNCH_SPAN(10);
   extern __shared__ __align__(16) float xs[];
@@ -65,7 +65,7 @@ __global__ void __launch_bounds__(kRowThreads) k_rows_norm_codes(const RowNormAr
   __syncthreads();
   for (int k = tid; k < K; k += kRowThreads) sq[k] = __fmul_rn(xs[k], xs[k]);
   __syncthreads();
-  float ms = spec_seq_sum<kRowThreads>(sq, K, 0.0f, sq + ((K + 3) & ~3));  // rmsnorm.c:15, in index order
+  float ms = spec_seq_sum(sq, K, 0.0f, sq + ((K + 3) & ~3));  // rmsnorm.c:15, in index order
   ms = __fmul_rn(ms, __fdiv_rn(1.0f, static_cast<float>(K)));
   const float rr = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
   float m = 0.0f;

@@ -1,13 +1,13 @@
 """GPU: the block-wide sequential sum of the RMSNorm prologues (rmsnorm.c:15).
 
-Each warp runs one segment of the row from 32 or 64 candidate start values
-around a double-precision estimate; one thread then links the segments in
-order, summing a segment again when its true start is not a candidate.  The
+The row's 32 segments run in parallel from candidate starts around estimated
+partial sums; one thread links them in order using only runs whose start is the
+exact partial sum, summing a segment itself when no candidate matches.  The
 result must equal the one-thread loop (and numpy's sequential float32 sum) bit
-for bit on every row, whether the candidates hit or not.  Rows built so that
-every add rounds the same way drift far from the estimate and force the
-fallback; signed, infinite, NaN, subnormal and overflowing rows check that
-nothing but speed depends on the estimate."""
+for bit on every row, whether the candidates match or not.  Signed and
+overflowing rows defeat the estimates and force that fallback; drifting,
+infinite, NaN and subnormal rows check that nothing but speed depends on the
+estimates."""
 from __future__ import annotations
 
 import ctypes as C
@@ -66,7 +66,7 @@ def test_spec_sum_equals_loop_on_gaussian_squares(lib, n):
     assert np.array_equal(spec.view(np.uint32), want.view(np.uint32))
 
 
-@pytest.mark.parametrize("threads", [64, 96, 512, 1024])
+@pytest.mark.parametrize("threads", [64, 96, 128, 256, 512, 1024])
 def test_spec_sum_block_sizes(lib, threads):
     rng = np.random.default_rng(threads)
     rows = np.stack([_squares(rng.standard_normal(4096)) for _ in range(4)] +
@@ -77,14 +77,20 @@ def test_spec_sum_block_sizes(lib, threads):
     assert np.array_equal(loop.view(np.uint32), want.view(np.uint32))
 
 
-@pytest.mark.parametrize("n,starts", [(4096, (1.0, 1e-30, 7.5)), (8192, (3.0, 1e20))])
-def test_spec_sum_fallback_when_the_estimate_is_far(lib, n, starts):
-    rows = np.stack([_drifting_row(n, s) for s in starts])
+@pytest.mark.parametrize("n", [4096, 8192])
+def test_spec_sum_rows_that_defeat_the_estimates(lib, n):
+    """Rows whose every add rounds the same way (the partial sums drift far from
+    the exact prefix), a signed row and a row that overflows to inf: exact in
+    every case; on the last the estimates fail and segments are summed again."""
+    rng = np.random.default_rng(n + 1)
+    rows = np.stack([_drifting_row(n, 1.0), _drifting_row(n, 1e-30), _drifting_row(n, 7.5),
+                     (rng.standard_normal(n) * 1e4).astype(f32), np.full(n, f32(3e37))])
     spec, loop, misses, _, _ = _run(lib, rows)
-    want = np.array([_seq(r) for r in rows], f32)
+    with np.errstate(all="ignore"):
+        want = np.array([_seq(r) for r in rows], f32)
     assert np.array_equal(spec.view(np.uint32), want.view(np.uint32))
     assert np.array_equal(loop.view(np.uint32), want.view(np.uint32))
-    assert np.all(misses > 0)  # the windows were missed and the segments summed again
+    assert misses[4] > 0  # after the overflow the shifts are inf - inf: segments summed by one thread
 
 
 def test_spec_sum_signed_special_and_extreme_rows(lib):
