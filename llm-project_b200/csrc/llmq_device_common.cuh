@@ -170,6 +170,49 @@ __device__ __forceinline__ float seq_dot(const float *a, const float *b, int sb,
   return acc;
 }
 
+// seq_dot with a contiguous and 16-byte aligned (read as float4), b strided:
+// 16 terms in flight, so a lone warp's chain is not held up by load latency.
+__device__ __forceinline__ float seq_dot_a4(const float *a, const float *b, int sb, int n, float acc) {
+  const float4 *a4 = reinterpret_cast<const float4 *>(a);
+  int i = 0;
+  if (n >= 16) {
+    float4 ca[4];
+    float cb[16];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) ca[u] = a4[u];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) cb[u] = b[(size_t)u * sb];
+    for (i = 16; i + 16 <= n; i += 16) {
+      float4 na[4];
+      float nb[16];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) na[u] = a4[(i >> 2) + u];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) nb[u] = b[(size_t)(i + u) * sb];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc = __fadd_rn(acc, __fmul_rn(ca[u].x, cb[4 * u]));
+        acc = __fadd_rn(acc, __fmul_rn(ca[u].y, cb[4 * u + 1]));
+        acc = __fadd_rn(acc, __fmul_rn(ca[u].z, cb[4 * u + 2]));
+        acc = __fadd_rn(acc, __fmul_rn(ca[u].w, cb[4 * u + 3]));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) ca[u] = na[u];
+#pragma unroll
+      for (int u = 0; u < 16; ++u) cb[u] = nb[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      acc = __fadd_rn(acc, __fmul_rn(ca[u].x, cb[4 * u]));
+      acc = __fadd_rn(acc, __fmul_rn(ca[u].y, cb[4 * u + 1]));
+      acc = __fadd_rn(acc, __fmul_rn(ca[u].z, cb[4 * u + 2]));
+      acc = __fadd_rn(acc, __fmul_rn(ca[u].w, cb[4 * u + 3]));
+    }
+  }
+  for (; i < n; ++i) acc = __fadd_rn(acc, __fmul_rn(a[i], b[(size_t)i * sb]));
+  return acc;
+}
+
 // As seq_dot with 16-byte shared-memory loads: a and b 16-byte aligned, n a
 // multiple of 4.
 __device__ __forceinline__ float seq_dot_v4(const float *a, const float *b, int n, float acc) {

@@ -599,12 +599,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
         const float as = s_as[r];
         for (int c = tid; c < kNT; c += kThreads) {
           const int j = p0 + c;
+          float *o = a.out + (size_t)r * a.N + j;
+          // the scale and the residual are read before the sum, so the three round trips overlap
+          const float wsj = j < a.N ? a.ws[j] : 0.0f;
+          const float res = EPI == EPI_RESID && j < a.N ? *o : 0.0f;
           const int v = atomicExch(a.acc + (size_t)r * a.Npad + j, 0);
           if (j < a.N) {
-            const float y = dequant(as, a.ws[j], v);
-            float *o = a.out + (size_t)r * a.N + j;
+            const float y = dequant(as, wsj, v);
             if (EPI == EPI_RESID)
-              *o = __fadd_rn(*o, y);  // llama.c:578 / llama.c:589
+              *o = __fadd_rn(res, y);  // llama.c:578 / llama.c:589
             else
               *o = y;
           }
@@ -615,9 +618,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       unsigned long long best = 0ull;
       for (int c = tid; c < kNT; c += kThreads) {
         const int j = p0 + c;
+        const float wsj = j < a.N ? a.ws[j] : 0.0f;
         const int v = atomicExch(a.acc + j, 0);
         if (j < a.N) {
-          const float y = dequant(as, a.ws[j], v);
+          const float y = dequant(as, wsj, v);
           a.out[j] = y;
           const unsigned long long key = argmax_key(y, static_cast<uint32_t>(j + a.idx_offset));
           best = key > best ? key : best;
@@ -631,12 +635,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       constexpr int half = kNT / 2;
       for (int c = tid; c < half; c += kThreads) {
         const int j = static_cast<int>(slab) * half + c;  // d_ff index
+        const float wg = j < a.N ? a.ws[p0 + c] : 0.0f, wu = j < a.N ? a.ws[p0 + half + c] : 0.0f;
         const int vg = atomicExch(a.acc + p0 + c, 0);
         const int vu = atomicExch(a.acc + p0 + half + c, 0);
         float h = 0.0f;
         if (j < a.N) {
-          const float z = dequant(as, a.ws[p0 + c], vg);
-          const float u = dequant(as, a.ws[p0 + half + c], vu);
+          const float z = dequant(as, wg, vg);
+          const float u = dequant(as, wu, vu);
           const float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, libm_expf(-z)));  // llama.c:585
           h = __fmul_rn(__fmul_rn(z, s), u);                                // llama.c:586
           a.out[j] = h;
@@ -651,9 +656,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_gemv(const GemvArgs a) {
       if (!pos_ok && tid == 0) atomicOr(a.err, ERR_BAD_POS);
       for (int c = tid; c < kNT; c += kThreads) {
         const int j = p0 + c;
+        const float wsj = j < a.N ? a.ws[j] : 0.0f, bj = j < a.N ? a.bias[j] : 0.0f;
         const int v = atomicExch(a.acc + j, 0);
         if (j >= a.N || !pos_ok) continue;
-        const float y = __fadd_rn(dequant(as, a.ws[j], v), a.bias[j]);  // llama.c:546-548
+        const float y = __fadd_rn(dequant(as, wsj, v), bj);  // llama.c:546-548
         if (j < a.qd + a.kvd) {
           a.out[j] = y;
         } else {
@@ -1087,7 +1093,7 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   cp_async_wait<0>();
   __syncthreads();
   LLMQ_TSTAMP(6);
-  const float o = tid < w ? seq_dot(e, vs + tid, kPVSlice, np, 0.0f) : 0.0f;  // llama.c:574
+  const float o = tid < w ? seq_dot_a4(e, vs + tid, kPVSlice, np, 0.0f) : 0.0f;  // llama.c:574
   if (tid < w) a.out[(size_t)h * hd + d0 + tid] = o;
   if (a.amax_out && tid < 32) warp_amax_publish(o, a.amax_out);  // the Wo product's row absmax
   __syncwarp();
