@@ -134,6 +134,41 @@ __device__ __forceinline__ float seq_sum_a16(const float *v, int n, float acc) {
   return acc;
 }
 
+// seq_sum_a16 with 32 values in flight (eight 16-byte loads ahead), for a
+// lone thread whose loads would otherwise wait on shared-memory latency.
+__device__ __forceinline__ float seq_sum_a32(const float *v, int n, float acc) {
+  const float4 *v4 = reinterpret_cast<const float4 *>(v);
+  int i = 0;
+  if (n >= 32) {
+    float4 c[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) c[u] = v4[u];
+    for (i = 32; i + 32 <= n; i += 32) {
+      float4 nx[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) nx[u] = v4[(i >> 2) + u];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        acc = __fadd_rn(acc, c[u].x);
+        acc = __fadd_rn(acc, c[u].y);
+        acc = __fadd_rn(acc, c[u].z);
+        acc = __fadd_rn(acc, c[u].w);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) c[u] = nx[u];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      acc = __fadd_rn(acc, c[u].x);
+      acc = __fadd_rn(acc, c[u].y);
+      acc = __fadd_rn(acc, c[u].z);
+      acc = __fadd_rn(acc, c[u].w);
+    }
+  }
+  for (; i < n; ++i) acc = __fadd_rn(acc, v[i]);
+  return acc;
+}
+
 // Sequential f32 dot product acc + a[0]*b[0] + a[1]*b[sb] + ..., each product
 // and each sum rounded on its own in C order.  Software-pipelined: the loads of
 // the next group of 8 are issued before the 8 adds of the current group, so

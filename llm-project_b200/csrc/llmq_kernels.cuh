@@ -1031,15 +1031,17 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   const int KC = a.fused_chunk;
   const float *kc = a.kcache + (size_t)kvh * a.max_seq * hd;
   const float *vc = a.vcache + (size_t)kvh * a.max_seq * hd;
-  // the value slice rows [0, pos) (row `pos` is this step's: loaded after the wait)
-  if (w > 0) stage_rows(vs, kPVSlice, vc, hd, 0, pos, d0, w, tid, kFusedThreads);
-  cp_async_commit();
   const int nchunks = (pb - pa + KC - 1) / KC;  // one slot when a part fits in one chunk, else two
   auto stage_keys = [&](int c) {  // cached keys of chunk c (not the row `pos`, rotated below)
     const int r0 = pa + c * KC, r1 = min(pa + (c + 1) * KC, pb);
     stage_rows(kring + (size_t)(c & 1) * KC * stride, stride, kc, hd, r0, min(r1, pos), 0, hd, tid, kFusedThreads);
   };
+  // Copy groups: the first key chunk, then the value slice rows [0, pos) (row
+  // `pos` is this step's: loaded after the wait), so the scores start once
+  // their keys are in; the values keep landing until the weighted sums.
   if (nchunks > 0) stage_keys(0);
+  cp_async_commit();
+  if (w > 0) stage_rows(vs, kPVSlice, vc, hd, 0, pos, d0, w, tid, kFusedThreads);
   cp_async_commit();
   pdl_wait();
   LLMQ_TSTAMP(1);
@@ -1059,7 +1061,10 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   for (int c = 0; c < nchunks; ++c) {
     if (c + 1 < nchunks) stage_keys(c + 1);
     cp_async_commit();
-    cp_async_wait<1>();  // chunk c (and the value slice, committed first) have landed
+    if (c == 0)
+      cp_async_wait<2>();  // chunk 0 has landed (the value slice and chunk 1 may still be in flight)
+    else
+      cp_async_wait<1>();  // chunk c has landed (and everything committed before it)
     __syncthreads();
     const float *ring = kring + (size_t)(c & 1) * KC * stride;
     const int r0 = pa + c * KC, rows = min(KC, pb - r0);
@@ -1085,7 +1090,7 @@ __global__ void __launch_bounds__(kFusedThreads) k_attn_fused(const AttnArgs a) 
   }
   cluster.sync();  // every part's exponentials are in every CTA; no remote accesses after this point
   LLMQ_TSTAMP(4);
-  if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum_a16(e, np, 0.0f));  // llama.c:567
+  if (tid == 0) s_inv = __fdiv_rn(1.0f, seq_sum_a32(e, np, 0.0f));  // llama.c:567
   __syncthreads();
   LLMQ_TSTAMP(5);
   const float inv = s_inv;
