@@ -179,9 +179,31 @@ __device__ __noinline__ bool expf_is_exception(uint32_t key) {
 }
 
 __device__ __forceinline__ float libm_expf(float x) {
+  const double y = exp(static_cast<double>(x));
+  // Fast paths, the same decisions as lx_expf_cr's tests: when y lies in the
+  // normal float range (biased double exponent 897..1150), the 29 low mantissa
+  // bits of y are its position inside one float ulp, with the rounding
+  // midpoint at 2^28.  y is more than LX_WINDOW (2^-9) ulp from the midpoint
+  // exactly when they differ from 2^28 by more than 2^20: (float)y is the
+  // result.  Within the window but more than LX_AMBIG (2^-24) ulp away, y
+  // decides the correct rounding f, and the result is f unless the input is
+  // one of the host library's exceptions, which round to the float on the other
+  // side of y (f's neighbour: exp is positive, so one step of the bit pattern).
+  const unsigned long long yb = static_cast<unsigned long long>(__double_as_longlong(y));
+  const int ye = static_cast<int>((yb >> 52) & 0x7ffu);
+  if (ye >= 897 && ye <= 1150) {
+    const int dist = static_cast<int>(static_cast<uint32_t>(yb & 0x1fffffffull)) - (1 << 28);
+    if (dist > (1 << 20) || dist < -(1 << 20)) return __double2float_rn(y);
+    if (dist > (1 << 5) || dist < -(1 << 5)) {
+      const float f = __double2float_rn(y);
+      const uint32_t fb = __float_as_uint(f);
+      const float other = __uint_as_float(static_cast<double>(f) < y ? fb + 1u : fb - 1u);
+      return expf_is_exception(__float_as_uint(x)) ? other : f;
+    }
+  }
   int near;
   float lo, up;
-  const float cr = lx_expf_cr(x, exp(static_cast<double>(x)), &near, &lo, &up);
+  const float cr = lx_expf_cr(x, y, &near, &lo, &up);
   if (!near) return cr;
   if (expf_is_exception(lx_bits(x))) return (cr == up) ? lo : up;
   return cr;
