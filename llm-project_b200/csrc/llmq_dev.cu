@@ -608,7 +608,8 @@ bool attn_two_kernels_forced() {
 // The batch-1 attention arguments' choice between the two paths.
 void choose_attention(AttnArgs &a) {
   a.pv_whole = pv_whole_bytes(a.max_seq) <= kPVWholeLimit;
-  a.fused_chunk = attn_two_kernels_forced() ? 0 : fused_chunk_rows(a, (size_t)g_smem_optin - 256);
+  // the limit is the kernels' dynamic shared memory attribute (DevCtx::max_smem)
+  a.fused_chunk = attn_two_kernels_forced() ? 0 : fused_chunk_rows(a, (size_t)g_smem_optin - 2048);
 }
 
 // The attention of one layer: k_attn_fused when a.fused_chunk > 0 (part 0;
